@@ -1,0 +1,342 @@
+#!/usr/bin/env python
+"""Benchmark of the quantfun2 DiT attention hot path on B200.
+
+Workload (one "step"): one Sage-style attention call on Flux-shaped heads --
+B=2 sequences x 24 heads x 4608 tokens (4096 image + 512 text) x head_dim 128,
+bf16 inputs resident in HBM; Q, V ~ N(0,1), K ~ N(0,1) + per-channel N(0, 3^2)
+offset.  The call quantizes Q/K to INT8 (per 64-token block, K smoothed by its
+token mean) and V to FP8, then runs the tcgen05 attention kernel (INT8 QK^T,
+FP8 PV, fp32 accumulation).  Metric: attention TFLOPS = 4*B*H*S^2*D / time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched by torchrun, one rank per GPU; each rank runs its own B=2
+problem (independent sequences, no collective on the data path: weak scaling).
+Rank 0 prints one JSON line.  `--impl reference` times the reference's CPU path
+(its torch-eager SDPA branch, fp32) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, H, S, D = 2, 24, 4608, 128
+WORKLOAD = f"sage attention, B={B} H={H} S={S} (4096 img + 512 txt) D={D}, bf16 io, INT8 QK^T / FP8 PV"
+METRIC = "attention TFLOPS (Flux-shaped 4608 tok, Sage INT8 QK / FP8 PV)"
+# dram bytes (read + write) of one sage_attn_kernel launch at this workload, from the ncu
+# capture summarised in profiles/sage_attn_kernel_B2_H24_S4608.md (None until captured)
+NCU_ATTN_TRAFFIC_BYTES = None
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while work runs."""
+
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.rows: list[tuple[float, list[str]]] = []
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            ident = str(device_index)
+        self.cmd = ["nvidia-smi", f"--id={ident}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "100"]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        rows = [r for (t, r) in self.rows if t0 <= t <= t1 + 0.15]
+        window = "timed"
+        if len(rows) < 3:  # very short timed region: include the load just before it
+            rows = [r for (t, r) in self.rows if t0 - 2.0 <= t <= t1 + 0.15]
+            window = "timed+preceding 2 s of the same work"
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "window": window}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+def fp8_gemm_peak_tflops(dev) -> float | None:
+    """cuBLAS e4m3 GEMM throughput (8192^3, best of 10): the dense FP8/INT8 tensor peak
+    this pool's B200 reaches through the vendor library, measured in this run."""
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=dev)
+        for _ in range(3):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1) / 1e3)
+        del a, b
+        return 2.0 * n ** 3 / best / 1e12
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------- reference --
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    from oracle.baseline import sdpa_cpu_sample
+
+    heads = 2
+    for _ in range(max(args.warmup, 0)):
+        sdpa_cpu_sample(heads=heads, S=S, D=D)
+    tot_t, tot_f, threads = 0.0, 0.0, 1
+    for _ in range(args.steps):
+        dt, fl, threads = sdpa_cpu_sample(heads=heads, S=S, D=D)
+        tot_t += dt
+        tot_f += fl
+    tflops = tot_f / tot_t / 1e12
+    sample = f"{heads} heads x {S} tokens x D={D}, fp32 torch SDPA on the host (src/models/flux/attn.py:42-43)"
+    line = {
+        "metric": METRIC, "value": tflops, "unit": "TFLOPS", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": tot_t / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD + " (CPU sample: " + sample + ")"},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": tflops, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- ours --
+def make_inputs(dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, H, S, D, device=dev, generator=g, dtype=torch.float32)
+    k = torch.randn(B, H, S, D, device=dev, generator=g) + 3.0 * torch.randn(1, H, 1, D, device=dev, generator=g)
+    v = torch.randn(B, H, S, D, device=dev, generator=g)
+    return q.bfloat16(), k.bfloat16(), v.bfloat16()
+
+
+def run_ours(args, rank: int, world: int, dev):
+    from quantfun2_b200 import _lib
+    from quantfun2_b200._lib import check, i64, stream_ptr
+    from quantfun2_b200.attention import _workspace, sageattn
+
+    lib = _lib.load()
+    q, k, v = make_inputs(dev, 1234 + rank)
+    out = torch.empty_like(q)
+    nbytes = int(lib.qf2_sage_workspace_bytes(B, H, H, B * S, B * S, S, S, D))
+    ws = _workspace(nbytes, dev)
+    st = lambda t: i64(t.stride(0), t.stride(1), t.stride(2))  # noqa: E731
+    sq, sk, sv, so = st(q), st(k), st(v), st(out)
+    sm = 1.0 / math.sqrt(D)
+    stream = stream_ptr(dev)
+
+    def quant():
+        check(lib.qf2_sage_quantize(q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, None, None, B, S, S, 0, 0,
+                                    0, 0, H, H, D, sm, _lib.QF2_BF16, ws.data_ptr(), ws.numel(), stream), "quant")
+
+    def attn():
+        check(lib.qf2_sage_attn_quantized(out.data_ptr(), so, None, None, B, S, S, 0, 0, 0, 0, H, H, D,
+                                          _lib.QF2_BF16, ws.data_ptr(), ws.numel(), stream), "attn")
+
+    flops_step = 4.0 * B * H * S * S * D
+    peaks = measured_peaks()
+    fp8_peak = fp8_gemm_peak_tflops(dev) if rank == 0 else None
+
+    sampler = ClockSampler(dev.index or 0) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for _ in range(max(args.warmup, 3)):
+        quant()
+        attn()
+    # keep the GPU busy ~1.5 s before timing so the clock record covers steady load
+    t_soak = time.time()
+    while time.time() - t_soak < 1.5:
+        for _ in range(20):
+            quant()
+            attn()
+        torch.cuda.synchronize()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(args.steps):
+        quant()
+        evs[i][0].record()
+        attn()
+        evs[i][1].record()
+    e_end.record()
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        torch.distributed.barrier()
+    total_s = e_start.elapsed_time(e_end) / 1e3
+    attn_s = sum(a.elapsed_time(b) for a, b in evs) / 1e3 / args.steps
+    if world > 1:
+        t = torch.tensor([total_s, attn_s], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_s, attn_s = float(t[0]), float(t[1])
+    clocks = sampler.summary(t_wall0, t_wall1) if sampler else None
+    if sampler:
+        sampler.stop()
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        e2e_steps = max(1, min(args.steps, 50))
+        for _ in range(3):
+            o = sageattn(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True))
+            hout.copy_(o, non_blocking=True)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(e2e_steps):
+            o = sageattn(hq.to(dev, non_blocking=True), hk.to(dev, non_blocking=True), hv.to(dev, non_blocking=True))
+            hout.copy_(o, non_blocking=True)
+        a1.record()
+        torch.cuda.synchronize()
+        e2e_s = a0.elapsed_time(a1) / 1e3 / e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_s = float(t[0])
+        e2e = {"value": world * flops_step / e2e_s / 1e12, "unit": "TFLOPS",
+               "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
+               "d2h_bytes_per_step": out.numel() * out.element_size(), "ms_per_step": e2e_s * 1e3,
+               "steps": e2e_steps}
+
+    if rank != 0:
+        return
+    # ---- CPU baseline: the reference's SDPA branch on a bounded sample (rank 0, N=1 only)
+    cpu = None
+    if world == 1:
+        from oracle.baseline import sdpa_cpu_sample
+
+        sdpa_cpu_sample(heads=1, S=S, D=D)
+        dt, fl, thr = sdpa_cpu_sample(heads=4, S=S, D=D)
+        cpu = {"value": fl / dt / 1e12, "unit": "TFLOPS", "cores": thr, "kind": "port",
+               "sample": f"4 heads x {S} tokens x D={D}, fp32 torch SDPA on the host "
+                         "(the reference's SDPA branch, src/models/flux/attn.py:42-43), one call"}
+
+    per_step = total_s / args.steps
+    value = world * flops_step / per_step / 1e12
+    attn_tflops = flops_step / attn_s / 1e12
+    if fp8_peak:
+        peak, peak_src = fp8_peak, "measured in this run: cuBLAS e4m3 GEMM 8192^3 burst (torch._scaled_mm)"
+    elif peaks.get("bf16_tflops"):
+        peak, peak_src = 2 * peaks["bf16_tflops"], "2 x measured bf16 burst (MEASURED_PEAKS.json)"
+    else:
+        peak, peak_src = 2 * 1590.0, "2 x fallback bf16 1.59 PFLOP/s"
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "i8+e4m3", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S, "heads": H, "head_dim": D,
+                   "parallelism": f"independent sequences per rank x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (q+k+v 170 MB + 85 MB of codes per rank)",
+                   "step": "qf2_sage_quantize + qf2_sage_attn_quantized (4 kernels)"},
+        "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": peak, "unit": "TFLOP/s",
+                     "frac": attn_tflops / peak, "traffic": NCU_ATTN_TRAFFIC_BYTES, "kernel": "sage_attn_kernel",
+                     "kernel_ms": attn_s * 1e3, "peak_source": peak_src,
+                     "frac_of_bf16_measured": (attn_tflops / peaks["bf16_tflops"]) if peaks.get("bf16_tflops")
+                     else None},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        run_ours(args, rank, world, dev)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+/*
+ * qf2b200.h -- C ABI of libqf2b200.so, the B200 (sm_100a) kernels behind the
+ * DiT inference hot path of quantfun2 (Flux / Lumina-Image-2.0).
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers, element strides (not bytes), int64 sizes.
+ *   - Every call is asynchronous and ordered on `stream` (a cudaStream_t;
+ *     NULL = legacy default stream).  Nothing is allocated: outputs and any
+ *     workspace are owned by the caller.
+ *   - Return 0 on success or a negative qf2_status.  Shape/dtype/alignment
+ *     problems are reported before anything is launched.
+ *   - Kernels that wait on mbarriers bound every wait (~2 s); a timed-out
+ *     kernel writes a nonzero code into the status word at the start of the
+ *     caller's workspace and returns.  qf2_workspace_status() reads it back.
+ *
+ * Each entry point names the reference interface it replaces
+ * (paths are relative to the gabe56f/quantfun2 source tree).
+ */
+#ifndef QF2B200_H
+#define QF2B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qf2_stream_t; /* == cudaStream_t */
+
+enum qf2_status {
+  QF2_OK = 0,
+  QF2_ERR_SHAPE = -1,       /* unsupported or inconsistent sizes           */
+  QF2_ERR_DTYPE = -2,       /* unsupported dtype code                      */
+  QF2_ERR_LAUNCH = -3,      /* CUDA launch / runtime error                 */
+  QF2_ERR_TIMEOUT = -4,     /* a bounded device-side wait gave up          */
+  QF2_ERR_ALIGN = -5,       /* pointer or stride alignment not met         */
+  QF2_ERR_WORKSPACE = -6,   /* workspace missing or too small              */
+  QF2_ERR_DEVICE = -7,      /* current device is not an sm_100 part        */
+  QF2_ERR_ARG = -8          /* NULL or otherwise invalid argument          */
+};
+
+enum qf2_dtype {
+  QF2_F32 = 0,
+  QF2_F16 = 1,
+  QF2_BF16 = 2,
+  QF2_I8 = 3,
+  QF2_E4M3 = 4,
+  QF2_I32 = 5
+};
+
+/* ---------------------------------------------------------------- misc -- */
+const char* qf2_version(void);
+const char* qf2_status_string(int status);
+/* 0 when the current CUDA device is compute capability 10.0, else QF2_ERR_DEVICE. */
+int qf2_device_check(void);
+/* Synchronizes `stream`, then returns QF2_ERR_TIMEOUT if the status word at
+ * the start of `workspace` is nonzero (and clears it), else QF2_OK. */
+int qf2_workspace_status(void* workspace, qf2_stream_t stream);
+
+/* ---------------------------------------------------------------- RoPE --
+ * Replaces rope_apply (src/kernels/__init__.py:126-142, eager) and its Triton
+ * body rope_triton (src/kernels/triton/rope.py:83-134).
+ * Rotates interleaved pairs (x[2p], x[2p+1]) of the last dim by the complex
+ * freqs_cis[b, s, p] (complex64, interleaved re/im floats), fp32 math, result
+ * rounded to `dtype`.  x*_strides = {batch, seq, head} in elements; the last
+ * dim is contiguous.  freqs_strides = {batch, seq} in complex elements (batch
+ * stride 0 broadcasts).  xk may be NULL.  Out may alias in (in-place, as the
+ * Triton path does).  flags & QF2_ROPE_FP16_TRIG rounds cos/sin to fp16 first,
+ * which is what the reference's Triton path computes with (rope.py:91-92).
+ */
+#define QF2_ROPE_FP16_TRIG 1
+int qf2_rope_apply(const void* xq, void* xq_out, int64_t Hq, const int64_t* xq_strides,
+                   const int64_t* xq_out_strides, const void* xk, void* xk_out, int64_t Hk,
+                   const int64_t* xk_strides, const int64_t* xk_out_strides, const void* freqs_cis,
+                   const int64_t* freqs_strides, int64_t B, int64_t S, int64_t D, int dtype, int flags,
+                   qf2_stream_t stream);
+
+/* ------------------------------------------------------------- RMSNorm --
+ * Replaces rmsnorm_apply (src/kernels/__init__.py:73-80) and the Triton
+ * apply_rmsnorm (src/kernels/triton/rmsnorm.py:72-95).
+ * out[m, :] = x[m, :] * rsqrt(mean(x[m, :]^2) + eps) * w, with fp32 sum of squares.
+ *   mode QF2_RMS_EAGER : normalized row rounded to x's dtype, then multiplied
+ *                        by w and rounded to out_dtype (the eager body).
+ *   mode QF2_RMS_FUSED : product formed in fp32, rounded once (the Triton body).
+ * Rows are N contiguous elements; row strides in elements.
+ */
+#define QF2_RMS_EAGER 0
+#define QF2_RMS_FUSED 1
+int qf2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, const void* weight, int w_dtype, void* out,
+                int64_t out_row_stride, int out_dtype, int64_t M, int64_t N, float eps, int mode,
+                qf2_stream_t stream);
+
+/* ------------------------------------------------------------- softmax --
+ * Replaces inplace_softmax (src/kernels/__init__.py:83-87) and
+ * inplace_tiled_softmax (src/kernels/triton/softmax.py:82-91): in-place
+ * softmax over each of `rows` rows of `n` elements (row stride in elements).
+ */
+int qf2_softmax_inplace(void* x, int64_t rows, int64_t n, int64_t row_stride, int dtype, qf2_stream_t stream);
+
+/* ------------------------------------------------ Sage-style attention --
+ * Replaces sageattention.sageattn (called at src/models/flux/attn.py:39-41)
+ * and sageattn_varlen (src/models/common/attn.py:109-120).
+ * Algorithm: K smoothed by its per-(sequence, head, channel) token mean; Q
+ * (pre-multiplied by sm_scale*log2(e)) and smoothed K quantized to INT8 per
+ * 64-token block (scale = amax/127, round half to even); V quantized to FP8
+ * e4m3 per channel (scale = amax/448); S = Qi8.Ki8^T on tcgen05 kind::i8 into
+ * TMEM; online softmax in base 2; P quantized to e4m3 (x448) and P.V on
+ * tcgen05 kind::f8f6f4 with fp32 accumulation in TMEM.  D = 128 only.
+ *
+ * Dense: q/k/v/out strides = {batch, head, seq} in elements (HND and NHD both
+ * expressible); dtype QF2_BF16 or QF2_F16; Hq % Hkv == 0 (GQA).
+ * Varlen: q [total_q, Hq, D], k/v [total_k, Hkv, D], strides = {token, head};
+ * cu_seqlens_* are int32 device arrays of batch+1 offsets.
+ * Workspace: caller-owned device memory of qf2_sage_workspace_bytes(); it
+ * holds the quantized codes, scales and the status word.
+ */
+int64_t qf2_sage_workspace_bytes(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
+                                 int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t D);
+int qf2_sageattn(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
+                 const int64_t* v_strides, void* out, const int64_t* out_strides, int64_t B, int64_t Hq,
+                 int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, float sm_scale, int dtype, void* workspace,
+                 int64_t workspace_bytes, qf2_stream_t stream);
+int qf2_sageattn_varlen(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                        const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides,
+                        const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int64_t batch,
+                        int64_t total_q, int64_t total_k, int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t Hq,
+                        int64_t Hkv, int64_t D, float sm_scale, int dtype, void* workspace,
+                        int64_t workspace_bytes, qf2_stream_t stream);
+
+/* Byte offsets inside the Sage workspace (for inspecting the quantized codes):
+ * offsets[0..9] = status, q codes, q scales, k codes, k scales, v codes,
+ * v scales, k mean, k-sum partials, v-amax partials; offsets[10] = total. */
+int qf2_sage_workspace_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
+                              int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t D, int64_t* offsets);
+
+/* Quantization stage alone (same arguments as qf2_sageattn / _varlen; pass
+ * cu_seqlens NULL for the dense form).  Leaves codes and scales in the
+ * workspace, laid out as qf2_sage_workspace_layout() describes. */
+int qf2_sage_quantize(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                      const void* v, const int64_t* v_strides, const int32_t* cu_seqlens_q,
+                      const int32_t* cu_seqlens_k, int64_t batch, int64_t Sq, int64_t Skv, int64_t total_q,
+                      int64_t total_k, int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t Hq, int64_t Hkv,
+                      int64_t D, float sm_scale, int dtype, void* workspace, int64_t workspace_bytes,
+                      qf2_stream_t stream);
+
+/* Attention stage alone, reading the codes qf2_sage_quantize() left in `workspace`
+ * (the second half of qf2_sageattn / qf2_sageattn_varlen; same layout rules). */
+int qf2_sage_attn_quantized(void* out, const int64_t* out_strides, const int32_t* cu_seqlens_q,
+                            const int32_t* cu_seqlens_k, int64_t batch, int64_t Sq, int64_t Skv, int64_t total_q,
+                            int64_t total_k, int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t Hq, int64_t Hkv,
+                            int64_t D, int dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QF2B200_H */

@@ -1,0 +1,43 @@
+// Library-level entry points: version, status strings, device check and the
+// workspace status word read-back used after bounded device waits.
+#include "qf2_common.cuh"
+
+extern "C" const char* qf2_version(void) { return "quantfun2-b200 0.1.0 (sm_100a)"; }
+
+extern "C" const char* qf2_status_string(int status) {
+  switch (status) {
+    case QF2_OK: return "ok";
+    case QF2_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case QF2_ERR_DTYPE: return "unsupported dtype";
+    case QF2_ERR_LAUNCH: return "CUDA launch or runtime error";
+    case QF2_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+    case QF2_ERR_ALIGN: return "pointer or stride alignment not met";
+    case QF2_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case QF2_ERR_DEVICE: return "current device is not compute capability 10.0 (B200)";
+    case QF2_ERR_ARG: return "invalid argument";
+  }
+  return "unknown status";
+}
+
+extern "C" int qf2_device_check(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QF2_ERR_DEVICE;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return QF2_ERR_DEVICE;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return QF2_ERR_DEVICE;
+  return (major == 10 && minor == 0) ? QF2_OK : QF2_ERR_DEVICE;
+}
+
+extern "C" int qf2_workspace_status(void* workspace, qf2_stream_t stream) {
+  if (!workspace) return QF2_ERR_ARG;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return QF2_ERR_LAUNCH;
+  int word = 0;
+  if (cudaMemcpy(&word, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return QF2_ERR_LAUNCH;
+  if (word != 0) {
+    const int zero = 0;
+    cudaMemcpy(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    return QF2_ERR_TIMEOUT;
+  }
+  return QF2_OK;
+}

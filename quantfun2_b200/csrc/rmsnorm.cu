@@ -1,0 +1,198 @@
+// Row RMSNorm (sm_100a).
+//
+// Replaces rmsnorm_apply (src/kernels/__init__.py:73-80) and the Triton
+// rms_norm_kernel / apply_rmsnorm (src/kernels/triton/rmsnorm.py:22-95).
+// A group of LPR lanes owns one row; each lane keeps its slice of the row in
+// registers (16-byte vectors), so x is read from HBM exactly once.  Sum of
+// squares in fp32, warp-shuffle reduction, rsqrt correctly rounded.
+// Rows too long for registers take a two-pass path (second read hits L2).
+#include "qf2_common.cuh"
+
+namespace qf2 {
+namespace rms {
+
+template <typename T>
+QF2_DEV void load_vec(const T* p, float* f, int n) {
+  // n elements (16 bytes) -> fp32
+  if constexpr (sizeof(T) == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+  } else {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = to_f32(e[i]);
+  }
+}
+
+template <typename T>
+QF2_DEV void store_vec(T* p, const float* f) {
+  if constexpr (sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  } else {
+    uint4 v;
+    T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(f[i]);
+    *reinterpret_cast<uint4*>(p) = v;
+  }
+}
+
+template <typename T>
+QF2_DEV float round_to(float v) { return to_f32(from_f32<T>(v)); }
+
+// EAGER: y = round_O( float(round_X(x * r)) * w );  FUSED: y = round_O((x * r) * w)
+template <typename TX, typename TW, typename TO, int LPR, int MAXC, bool EAGER>
+__global__ void __launch_bounds__(256) rmsnorm_reg_kernel(const TX* __restrict__ x, int64_t xs, const TW* __restrict__ w,
+                                                          TO* __restrict__ y, int64_t ys, int64_t M, int64_t N, float eps) {
+  constexpr int V = 16 / sizeof(TX);
+  const int64_t nvec = N / V;
+  const int rows_per_block = blockDim.x / LPR;
+  const int sub = threadIdx.x % LPR;
+  for (int64_t row = (int64_t)blockIdx.x * rows_per_block + threadIdx.x / LPR; row < M;
+       row += (int64_t)gridDim.x * rows_per_block) {
+    const TX* xr = x + row * xs;
+    float v[MAXC][V];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const int64_t vi = sub + (int64_t)c * LPR;
+      if (vi < nvec) {
+        load_vec(xr + vi * V, v[c], V);
+#pragma unroll
+        for (int i = 0; i < V; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+      }
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o, LPR);
+    const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)N), eps));
+    TO* yr = y + row * ys;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const int64_t vi = sub + (int64_t)c * LPR;
+      if (vi < nvec) {
+        float o[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const float wv = to_f32(w[vi * V + i]);
+          const float n = __fmul_rn(v[c][i], r);
+          o[i] = EAGER ? __fmul_rn(round_to<TX>(n), wv) : __fmul_rn(n, wv);
+        }
+        if constexpr (sizeof(TO) == sizeof(TX)) {
+          store_vec(yr + vi * V, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < V; ++i) yr[vi * V + i] = from_f32<TO>(o[i]);
+        }
+      }
+    }
+  }
+}
+
+// Scalar two-pass fallback: any N, any alignment.  One warp per row.
+template <typename TX, typename TW, typename TO, bool EAGER>
+__global__ void __launch_bounds__(256) rmsnorm_generic_kernel(const TX* __restrict__ x, int64_t xs,
+                                                              const TW* __restrict__ w, TO* __restrict__ y, int64_t ys,
+                                                              int64_t M, int64_t N, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x / 32;
+  for (int64_t row = (int64_t)blockIdx.x * wpb + threadIdx.x / 32; row < M; row += (int64_t)gridDim.x * wpb) {
+    const TX* xr = x + row * xs;
+    float ss = 0.f;
+    for (int64_t i = lane; i < N; i += 32) {
+      const float v = to_f32(xr[i]);
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)N), eps));
+    TO* yr = y + row * ys;
+    for (int64_t i = lane; i < N; i += 32) {
+      const float n = __fmul_rn(to_f32(xr[i]), r);
+      const float wv = to_f32(w[i]);
+      yr[i] = from_f32<TO>(EAGER ? __fmul_rn(round_to<TX>(n), wv) : __fmul_rn(n, wv));
+    }
+  }
+}
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <typename TX, typename TW, typename TO, bool EAGER>
+static void dispatch(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t M, int64_t N, float eps,
+                     cudaStream_t st) {
+  constexpr int V = 16 / sizeof(TX);
+  const TX* X = reinterpret_cast<const TX*>(x);
+  const TW* W = reinterpret_cast<const TW*>(w);
+  TO* Y = reinterpret_cast<TO*>(y);
+  const bool vec_ok = (N % V) == 0 && al16(x) && al16(y) && ((xs * (int64_t)sizeof(TX)) % 16) == 0 &&
+                      ((ys * (int64_t)sizeof(TO)) % 16) == 0 && (sizeof(TO) == sizeof(TX) || true);
+  const int64_t nvec = N / V;
+  auto grid_for = [&](int rows_per_block) {
+    int64_t g = (M + rows_per_block - 1) / rows_per_block;
+    if (g > 148 * 16) g = 148 * 16;
+    return (unsigned)(g < 1 ? 1 : g);
+  };
+  if (vec_ok && nvec <= 8) {
+    rmsnorm_reg_kernel<TX, TW, TO, 8, 1, EAGER><<<grid_for(32), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
+  } else if (vec_ok && nvec <= 16) {
+    rmsnorm_reg_kernel<TX, TW, TO, 16, 1, EAGER><<<grid_for(16), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
+  } else if (vec_ok && nvec <= 32 * 16) {
+    rmsnorm_reg_kernel<TX, TW, TO, 32, 16, EAGER><<<grid_for(8), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
+  } else {
+    rmsnorm_generic_kernel<TX, TW, TO, EAGER><<<grid_for(8), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
+  }
+}
+
+template <typename TX, typename TW, bool EAGER>
+static int by_out(int od, const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t M, int64_t N,
+                  float eps, cudaStream_t st) {
+  switch (od) {
+    case QF2_F32: dispatch<TX, TW, float, EAGER>(x, xs, w, y, ys, M, N, eps, st); return QF2_OK;
+    case QF2_F16: dispatch<TX, TW, __half, EAGER>(x, xs, w, y, ys, M, N, eps, st); return QF2_OK;
+    case QF2_BF16: dispatch<TX, TW, __nv_bfloat16, EAGER>(x, xs, w, y, ys, M, N, eps, st); return QF2_OK;
+  }
+  return QF2_ERR_DTYPE;
+}
+
+template <typename TX, bool EAGER>
+static int by_w(int wd, int od, const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t M, int64_t N,
+                float eps, cudaStream_t st) {
+  switch (wd) {
+    case QF2_F32: return by_out<TX, float, EAGER>(od, x, xs, w, y, ys, M, N, eps, st);
+    case QF2_F16: return by_out<TX, __half, EAGER>(od, x, xs, w, y, ys, M, N, eps, st);
+    case QF2_BF16: return by_out<TX, __nv_bfloat16, EAGER>(od, x, xs, w, y, ys, M, N, eps, st);
+  }
+  return QF2_ERR_DTYPE;
+}
+
+template <bool EAGER>
+static int by_x(int xd, int wd, int od, const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t M,
+                int64_t N, float eps, cudaStream_t st) {
+  switch (xd) {
+    case QF2_F32: return by_w<float, EAGER>(wd, od, x, xs, w, y, ys, M, N, eps, st);
+    case QF2_F16: return by_w<__half, EAGER>(wd, od, x, xs, w, y, ys, M, N, eps, st);
+    case QF2_BF16: return by_w<__nv_bfloat16, EAGER>(wd, od, x, xs, w, y, ys, M, N, eps, st);
+  }
+  return QF2_ERR_DTYPE;
+}
+
+}  // namespace rms
+}  // namespace qf2
+
+extern "C" int qf2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, const void* weight, int w_dtype, void* out,
+                           int64_t out_row_stride, int out_dtype, int64_t M, int64_t N, float eps, int mode,
+                           qf2_stream_t stream) {
+  if (!x || !weight || !out) return QF2_ERR_ARG;
+  if (M < 0 || N <= 0) return QF2_ERR_SHAPE;
+  if (mode != QF2_RMS_EAGER && mode != QF2_RMS_FUSED) return QF2_ERR_ARG;
+  if (M == 0) return QF2_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int r = mode == QF2_RMS_EAGER
+                    ? qf2::rms::by_x<true>(x_dtype, w_dtype, out_dtype, x, x_row_stride, weight, out, out_row_stride, M,
+                                           N, eps, st)
+                    : qf2::rms::by_x<false>(x_dtype, w_dtype, out_dtype, x, x_row_stride, weight, out, out_row_stride,
+                                            M, N, eps, st);
+  if (r != QF2_OK) return r;
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}

@@ -1,0 +1,139 @@
+// Rotary position embedding over interleaved pairs (sm_100a).
+//
+// Replaces rope_apply (src/kernels/__init__.py:126-142) and the Triton body
+// rope_kernel_inplace / rope_triton (src/kernels/triton/rope.py:20-134).
+// One launch rotates both q and k: the flat index runs over
+// (batch, seq, head in [0, Hq + Hk), 16-byte chunk of the head row); each thread
+// moves one 16-byte vector (8 bf16/f16 or 4 fp32 elements) with the matching
+// complex factors read once per (batch, seq) from freqs_cis.  HBM-bound: every
+// element is read once and written once.
+#include "qf2_common.cuh"
+
+namespace qf2 {
+namespace rope {
+
+struct Side {
+  const void* x;
+  void* y;
+  int64_t sb, ss, sh;     // input strides (elements)
+  int64_t ob, os, oh;     // output strides
+  int64_t H;
+};
+
+template <typename T, int VEC, bool FP16_TRIG>
+__global__ void __launch_bounds__(256) rope_kernel(Side q, Side k, const float2* __restrict__ freqs, int64_t fsb,
+                                                   int64_t fss, int64_t B, int64_t S, int64_t D) {
+  const int64_t chunks = D / VEC;
+  const int64_t H = q.H + k.H;
+  const int64_t total = B * S * H * chunks;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t t = idx;
+    const int64_t c = t % chunks; t /= chunks;
+    const int64_t h = t % H; t /= H;
+    const int64_t s = t % S;
+    const int64_t b = t / S;
+    const bool is_q = h < q.H;
+    const Side& sd = is_q ? q : k;
+    const int64_t hh = is_q ? h : h - q.H;
+    const T* src = reinterpret_cast<const T*>(sd.x) + b * sd.sb + s * sd.ss + hh * sd.sh + c * VEC;
+    T* dst = reinterpret_cast<T*>(sd.y) + b * sd.ob + s * sd.os + hh * sd.oh + c * VEC;
+    const float2* f = freqs + b * fsb + s * fss + c * (VEC / 2);
+
+    T in[VEC];
+    if constexpr (VEC * sizeof(T) == 16) {
+      *reinterpret_cast<uint4*>(in) = *reinterpret_cast<const uint4*>(src);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) in[i] = src[i];
+    }
+    T out[VEC];
+#pragma unroll
+    for (int p = 0; p < VEC / 2; ++p) {
+      float2 cs = __ldg(f + p);
+      if (FP16_TRIG) {
+        cs.x = __half2float(__float2half_rn(cs.x));
+        cs.y = __half2float(__float2half_rn(cs.y));
+      }
+      const float x0 = to_f32(in[2 * p]), x1 = to_f32(in[2 * p + 1]);
+      // (x0 + i x1) * (c + i s), each product rounded separately
+      const float re = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+      const float im = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+      out[2 * p] = from_f32<T>(re);
+      out[2 * p + 1] = from_f32<T>(im);
+    }
+    if constexpr (VEC * sizeof(T) == 16) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(out);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) dst[i] = out[i];
+    }
+  }
+}
+
+template <typename T, int VEC>
+static void launch(const Side& q, const Side& k, const float2* f, int64_t fsb, int64_t fss, int64_t B, int64_t S,
+                   int64_t D, bool fp16_trig, cudaStream_t st) {
+  const int64_t total = B * S * (q.H + k.H) * (D / VEC);
+  const int threads = 256;
+  int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > 148 * 64) blocks = 148 * 64;  // grid-stride beyond 64 CTAs per SM
+  if (blocks < 1) blocks = 1;
+  if (fp16_trig)
+    rope_kernel<T, VEC, true><<<(unsigned)blocks, threads, 0, st>>>(q, k, f, fsb, fss, B, S, D);
+  else
+    rope_kernel<T, VEC, false><<<(unsigned)blocks, threads, 0, st>>>(q, k, f, fsb, fss, B, S, D);
+}
+
+static bool al(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace rope
+}  // namespace qf2
+
+extern "C" int qf2_rope_apply(const void* xq, void* xq_out, int64_t Hq, const int64_t* xq_strides,
+                              const int64_t* xq_out_strides, const void* xk, void* xk_out, int64_t Hk,
+                              const int64_t* xk_strides, const int64_t* xk_out_strides, const void* freqs_cis,
+                              const int64_t* freqs_strides, int64_t B, int64_t S, int64_t D, int dtype, int flags,
+                              qf2_stream_t stream) {
+  using namespace qf2::rope;
+  if (!xq || !xq_out || !xq_strides || !xq_out_strides || !freqs_cis || !freqs_strides) return QF2_ERR_ARG;
+  if (B < 0 || S < 0 || Hq < 0 || D <= 0 || (D & 1)) return QF2_ERR_SHAPE;
+  const bool has_k = xk != nullptr && Hk > 0;
+  if (has_k && (!xk_out || !xk_strides || !xk_out_strides)) return QF2_ERR_ARG;
+  if (B == 0 || S == 0) return QF2_OK;
+  Side q{xq, xq_out, xq_strides[0], xq_strides[1], xq_strides[2],
+         xq_out_strides[0], xq_out_strides[1], xq_out_strides[2], Hq};
+  Side k{nullptr, nullptr, 0, 0, 0, 0, 0, 0, 0};
+  if (has_k)
+    k = Side{xk, xk_out, xk_strides[0], xk_strides[1], xk_strides[2],
+             xk_out_strides[0], xk_out_strides[1], xk_out_strides[2], Hk};
+  const float2* f = reinterpret_cast<const float2*>(freqs_cis);
+  if (!al(f, 8)) return QF2_ERR_ALIGN;
+  const bool fp16 = (flags & QF2_ROPE_FP16_TRIG) != 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int esz;
+  switch (dtype) {
+    case QF2_F32: esz = 4; break;
+    case QF2_F16: case QF2_BF16: esz = 2; break;
+    default: return QF2_ERR_DTYPE;
+  }
+  // 16-byte vector path when every row start is 16-byte aligned
+  const int vec16 = 16 / esz;
+  bool vec_ok = (D % vec16) == 0 && al(xq, 16) && al(xq_out, 16);
+  const int64_t* all_strides[4] = {xq_strides, xq_out_strides, xk_strides, xk_out_strides};
+  for (int i = 0; i < (has_k ? 4 : 2); ++i)
+    for (int j = 0; j < 3; ++j) vec_ok = vec_ok && ((all_strides[i][j] * esz) % 16 == 0);
+  if (has_k) vec_ok = vec_ok && al(xk, 16) && al(xk_out, 16);
+  if (dtype == QF2_F32) {
+    if (vec_ok) launch<float, 4>(q, k, f, freqs_strides[0], freqs_strides[1], B, S, D, fp16, st);
+    else launch<float, 2>(q, k, f, freqs_strides[0], freqs_strides[1], B, S, D, fp16, st);
+  } else if (dtype == QF2_BF16) {
+    if (vec_ok) launch<__nv_bfloat16, 8>(q, k, f, freqs_strides[0], freqs_strides[1], B, S, D, fp16, st);
+    else launch<__nv_bfloat16, 2>(q, k, f, freqs_strides[0], freqs_strides[1], B, S, D, fp16, st);
+  } else {
+    if (vec_ok) launch<__half, 8>(q, k, f, freqs_strides[0], freqs_strides[1], B, S, D, fp16, st);
+    else launch<__half, 2>(q, k, f, freqs_strides[0], freqs_strides[1], B, S, D, fp16, st);
+  }
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}

@@ -1,0 +1,154 @@
+"""Drop-in kernel ops for the reference's kernel seam (src/kernels/__init__.py).
+
+The reference binds each op once, at import, through
+``implemented_as(cuda_func=..., triton_func=...)`` (src/kernels/module.py:42-54).
+This module exposes the same op names, argument meaning and return convention,
+backed by libqf2b200.so (sm_100a CUDA).  There is no CPU or Triton fallback: the
+ops raise ``QF2Error`` when the library is missing or the tensor is not on a
+B200.
+
+  rope_apply(xq, xk, freqs_cis)        -> (xq_out, xk_out)   __init__.py:126-142
+  rope_apply_(xq, xk, freqs_cis)       -> (xq, xk) in place   triton/rope.py:83-134
+  rmsnorm_apply(x, weight, eps)        -> Tensor              __init__.py:73-80
+  inplace_softmax(x, dim=-1)           -> x                   __init__.py:83-87
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import QF2Error, check, dtype_code, i64, require_device, stream_ptr
+
+__all__ = [
+    "implemented_as",
+    "rope_apply",
+    "rope_apply_",
+    "rmsnorm_apply",
+    "inplace_softmax",
+    "QF2Error",
+]
+
+
+def implemented_as(cuda_func=None, triton_func=None):
+    """Same contract as the reference decorator (src/kernels/module.py:42-54): the
+    decorated eager body is replaced at decoration time.  Here the sm_100a body
+    (`cuda_func`) always wins; `triton_func` is accepted for signature parity and
+    ignored (no Triton on this path)."""
+
+    def decorator(func):
+        impl = cuda_func if cuda_func is not None else func
+
+        def inner(*args, **kwargs):
+            return impl(*args, **kwargs)
+
+        inner.__name__ = getattr(func, "__name__", "op")
+        inner.__doc__ = getattr(impl, "__doc__", None)
+        return inner
+
+    return decorator
+
+
+def _freqs_view(freqs_cis: torch.Tensor, B: int, S: int, half: int):
+    if not freqs_cis.is_complex():
+        freqs_cis = torch.view_as_complex(freqs_cis.contiguous())
+    if freqs_cis.dtype != torch.complex64:
+        freqs_cis = freqs_cis.to(torch.complex64)
+    if freqs_cis.dim() == 2:
+        freqs_cis = freqs_cis.unsqueeze(0)
+    if freqs_cis.dim() != 3 or freqs_cis.shape[-1] != half or freqs_cis.shape[1] != S:
+        raise QF2Error(f"freqs_cis shape {tuple(freqs_cis.shape)} does not match [B, {S}, {half}]")
+    if freqs_cis.stride(-1) != 1:
+        freqs_cis = freqs_cis.contiguous()
+    fb = freqs_cis.shape[0]
+    if fb not in (1, B):
+        raise QF2Error(f"freqs_cis batch {fb} does not broadcast to {B}")
+    sb = 0 if fb == 1 else freqs_cis.stride(0)
+    return freqs_cis, (sb, freqs_cis.stride(1))
+
+
+def _rope(xq, xk, freqs_cis, out_q, out_k, fp16_trig: bool):
+    require_device(xq)
+    if xq.dim() != 4 or (xk is not None and xk.dim() != 4):
+        raise QF2Error("rope_apply expects [B, S, H, D] tensors")
+    B, S, Hq, D = xq.shape
+    if xq.stride(-1) != 1 or out_q.stride(-1) != 1:
+        raise QF2Error("rope_apply needs a contiguous last dim")
+    fc, fs = _freqs_view(freqs_cis.to(xq.device), B, S, D // 2)
+    has_k = xk is not None
+    if has_k:
+        if xk.shape[0] != B or xk.shape[1] != S or xk.shape[3] != D or xk.dtype != xq.dtype:
+            raise QF2Error("xk must match xq in batch, seq, head_dim and dtype")
+        if xk.stride(-1) != 1 or out_k.stride(-1) != 1:
+            raise QF2Error("rope_apply needs a contiguous last dim")
+    Hk = xk.shape[2] if has_k else 0
+    st = check(
+        _lib.load().qf2_rope_apply(
+            xq.data_ptr(), out_q.data_ptr(), Hq, i64(*xq.stride()[:3]), i64(*out_q.stride()[:3]),
+            xk.data_ptr() if has_k else None, out_k.data_ptr() if has_k else None, Hk,
+            i64(*xk.stride()[:3]) if has_k else None, i64(*out_k.stride()[:3]) if has_k else None,
+            fc.data_ptr(), i64(*fs), B, S, D, dtype_code(xq.dtype),
+            _lib.QF2_ROPE_FP16_TRIG if fp16_trig else 0, stream_ptr(xq.device)),
+        "qf2_rope_apply")
+    return st
+
+
+def rope_apply(xq: torch.Tensor, xk: torch.Tensor, freqs_cis: torch.Tensor):
+    """Eager-body semantics (src/kernels/__init__.py:126-142): returns new tensors,
+    inputs untouched; fp32 rotation rounded to the input dtype."""
+    out_q = torch.empty_like(xq)
+    out_k = torch.empty_like(xk) if xk is not None else None
+    _rope(xq, xk, freqs_cis, out_q, out_k, fp16_trig=False)
+    return out_q, out_k
+
+
+def rope_apply_(xq: torch.Tensor, xk: torch.Tensor, freqs_cis: torch.Tensor, fp16_trig: bool = True):
+    """Triton-body semantics (src/kernels/triton/rope.py:83-134): rotates in place and
+    returns the same tensors; cos/sin rounded to fp16 as rope_triton does."""
+    _rope(xq, xk, freqs_cis, xq, xk, fp16_trig=fp16_trig)
+    return xq, xk
+
+
+def rmsnorm_apply(x: torch.Tensor, weight: torch.Tensor, eps: float, fused: bool = False) -> torch.Tensor:
+    """x * rsqrt(mean(x^2, -1) + eps) * weight over the last dim.
+
+    Default: the eager body's rounding (src/kernels/__init__.py:74-80): the
+    normalized row is rounded to x.dtype, multiplied by weight, and the result has
+    the promoted dtype of (x, weight).  fused=True: the Triton body's rounding
+    (src/kernels/triton/rmsnorm.py:179-203): one rounding to x.dtype at the end.
+    """
+    require_device(x)
+    N = weight.shape[0]
+    if x.shape[-1] != N:
+        raise QF2Error(f"last dim {x.shape[-1]} != weight size {N}")
+    x2 = x.reshape(-1, N)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    w = weight.to(x.device)
+    if w.stride(0) != 1:
+        w = w.contiguous()
+    out_dtype = x.dtype if fused else torch.promote_types(x.dtype, w.dtype)
+    out = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    o2 = out.view(-1, N)
+    check(
+        _lib.load().qf2_rmsnorm(
+            x2.data_ptr(), x2.stride(0), dtype_code(x.dtype), w.data_ptr(), dtype_code(w.dtype), o2.data_ptr(),
+            o2.stride(0), dtype_code(out_dtype), x2.shape[0], N, float(eps),
+            _lib.QF2_RMS_FUSED if fused else _lib.QF2_RMS_EAGER, stream_ptr(x.device)),
+        "qf2_rmsnorm")
+    return out
+
+
+def inplace_softmax(x: torch.Tensor, dim: int = -1) -> torch.Tensor:
+    """Row softmax over the last dim, written back into x (src/kernels/__init__.py:83-87).
+    Like the Triton wrapper (src/kernels/triton/softmax.py:82-91), a non-contiguous
+    input is first made contiguous and the contiguous copy is returned."""
+    if dim not in (-1, x.dim() - 1):
+        raise QF2Error("Only dim=-1 is supported")
+    require_device(x)
+    if not x.is_contiguous():
+        x = x.contiguous()
+    n = x.shape[-1]
+    rows = x.numel() // max(n, 1)
+    check(_lib.load().qf2_softmax_inplace(x.data_ptr(), rows, n, n, dtype_code(x.dtype), stream_ptr(x.device)),
+          "qf2_softmax_inplace")
+    return x

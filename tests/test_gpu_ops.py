@@ -1,0 +1,134 @@
+"""GPU parity of RoPE / RMSNorm / softmax (libqf2b200.so) against the reference's golden
+vectors and the oracle restatements."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops
+from oracle.numerics import bf16_bits_to_f32, f32_to_bf16_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def t_bf16(bits, dev):
+    return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def cplx(a):
+    return torch.view_as_complex(torch.from_numpy(np.ascontiguousarray(a)))
+
+
+def test_rope_golden_f32(cuda, golden):
+    from quantfun2_b200.kernels import rope_apply
+
+    xq = torch.from_numpy(golden["rope_f32_xq"]).to(cuda)
+    xk = torch.from_numpy(golden["rope_f32_xk"]).to(cuda)
+    f = cplx(golden["rope_freqs"]).to(cuda)
+    oq, ok = rope_apply(xq, xk, f)
+    np.testing.assert_allclose(oq.cpu().numpy(), golden["rope_f32_oq"], rtol=0, atol=2e-6)
+    np.testing.assert_allclose(ok.cpu().numpy(), golden["rope_f32_ok"], rtol=0, atol=2e-6)
+    # bit-exact against the oracle restatement (same rounding steps)
+    rq, rk = ops.rope_apply(golden["rope_f32_xq"], golden["rope_f32_xk"], cplx(golden["rope_freqs"]).numpy(), "f32")
+    assert np.array_equal(oq.cpu().numpy(), rq) and np.array_equal(ok.cpu().numpy(), rk)
+
+
+def test_rope_golden_bf16_and_inplace(cuda, golden):
+    from quantfun2_b200.kernels import rope_apply, rope_apply_
+
+    xq = t_bf16(golden["rope_bf16_xq"], cuda)
+    xk = t_bf16(golden["rope_bf16_xk"], cuda)
+    f = cplx(golden["rope_freqs"]).to(cuda)
+    oq, ok = rope_apply(xq, xk, f)
+    for got, ref in ((oq, golden["rope_bf16_oq"]), (ok, golden["rope_bf16_ok"])):
+        d = np.abs(bits(got).astype(np.int32) - ref.astype(np.int32))
+        assert d.max() <= 1 and (d == 0).mean() > 0.999
+    # the Triton-path semantics: in place, fp16-rounded cos/sin
+    q2, k2 = xq.clone(), xk.clone()
+    r = rope_apply_(q2, k2, f)
+    assert r[0].data_ptr() == q2.data_ptr()
+    rq, rk = ops.rope_apply(bf16_bits_to_f32(golden["rope_bf16_xq"]), bf16_bits_to_f32(golden["rope_bf16_xk"]),
+                            cplx(golden["rope_freqs"]).numpy(), "bf16", fp16_trig=True)
+    assert np.array_equal(bits(q2), f32_to_bf16_bits(rq)) and np.array_equal(bits(k2), f32_to_bf16_bits(rk))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_rope_strided_hnd_views_and_broadcast(cuda, dtype):
+    """Flux passes q/k as [B, H, L, D] permuted views; freqs broadcast over batch."""
+    from quantfun2_b200.kernels import rope_apply
+
+    g = torch.Generator().manual_seed(3)
+    B, H, L, D = 2, 3, 77, 128
+    qh = torch.randn(B, H, L, D, generator=g).to(dtype)
+    kh = torch.randn(B, H, L, D, generator=g).to(dtype)
+    ang = torch.rand(1, L, D // 2, generator=g) * 6.28
+    f = torch.polar(torch.ones_like(ang), ang)
+    oq, ok = rope_apply(qh.to(cuda).permute(0, 2, 1, 3), kh.to(cuda).permute(0, 2, 1, 3), f.to(cuda))
+    tag = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[dtype]
+    rq, rk = ops.rope_apply(qh.float().permute(0, 2, 1, 3).numpy(), kh.float().permute(0, 2, 1, 3).numpy(),
+                            np.broadcast_to(f.numpy(), (B, L, D // 2)), tag)
+    assert np.array_equal(oq.float().cpu().numpy(), rq)
+    assert np.array_equal(ok.float().cpu().numpy(), rk)
+
+
+@pytest.mark.parametrize("tag", ["head", "row"])
+def test_rmsnorm_golden(cuda, golden, tag):
+    from quantfun2_b200.kernels import rmsnorm_apply
+
+    eps = float(golden[f"rms_{tag}_eps"][0])
+    y = rmsnorm_apply(torch.from_numpy(golden[f"rms_{tag}_x_f32"]).to(cuda),
+                      torch.from_numpy(golden[f"rms_{tag}_w_f32"]).to(cuda), eps)
+    np.testing.assert_allclose(y.cpu().numpy(), golden[f"rms_{tag}_y_f32"], rtol=3e-6, atol=3e-6)
+    yb = rmsnorm_apply(t_bf16(golden[f"rms_{tag}_x_bf16"], cuda), t_bf16(golden[f"rms_{tag}_w_bf16"], cuda), eps)
+    assert yb.dtype == torch.bfloat16
+    d = np.abs(bits(yb).astype(np.int32) - golden[f"rms_{tag}_y_bf16"].astype(np.int32))
+    assert d.max() <= 1 and (d == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("N", [64, 96, 128, 2304, 3072, 5000, 97])
+@pytest.mark.parametrize("fused", [False, True])
+def test_rmsnorm_shapes_vs_oracle(cuda, N, fused):
+    from quantfun2_b200.kernels import rmsnorm_apply
+
+    g = torch.Generator().manual_seed(N)
+    x = (torch.randn(33, N, generator=g) * 2).bfloat16()
+    w = (torch.rand(N, generator=g) + 0.5).bfloat16()
+    y = rmsnorm_apply(x.to(cuda), w.to(cuda), 1e-6, fused=fused)
+    r = ops.rmsnorm_apply(x.float().numpy(), w.float().numpy(), 1e-6, "bf16", fused=fused)
+    d = np.abs(bits(y).astype(np.int32) - f32_to_bf16_bits(r).astype(np.int32))
+    assert d.max() <= 1 and (d == 0).mean() > 0.99
+
+
+def test_rmsnorm_mixed_dtypes(cuda):
+    """bf16 activations with an fp32 weight promote to fp32 output, as the eager body does."""
+    from quantfun2_b200.kernels import rmsnorm_apply
+
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(10, 96, generator=g).bfloat16()
+    w = torch.rand(96, generator=g) + 0.5
+    y = rmsnorm_apply(x.to(cuda), w.to(cuda), 1e-6)
+    assert y.dtype == torch.float32
+    r = ops.rmsnorm_apply(x.float().numpy(), w.numpy(), 1e-6, "bf16", out_dtype="f32")
+    np.testing.assert_allclose(y.cpu().numpy(), r, rtol=1e-6, atol=1e-6)
+
+
+def test_softmax_golden_and_long_rows(cuda, golden):
+    from quantfun2_b200.kernels import inplace_softmax
+
+    x = torch.from_numpy(golden["softmax_x_f32"]).to(cuda)
+    y = inplace_softmax(x, -1)
+    assert y.data_ptr() == x.data_ptr()
+    np.testing.assert_allclose(y.cpu().numpy(), golden["softmax_y_f32"], rtol=1e-5, atol=1e-7)
+    xb = t_bf16(golden["softmax_x_bf16"], cuda)
+    yb = inplace_softmax(xb, -1)
+    d = np.abs(bits(yb).astype(np.int32) - golden["softmax_y_bf16"].astype(np.int32))
+    assert d.max() <= 1
+    g = torch.Generator().manual_seed(9)
+    z = torch.randn(3, 16400, generator=g) * 5
+    z[1, 100:] = -float("inf")
+    r = ops.softmax_lastdim(z.numpy())
+    out = inplace_softmax(z.to(cuda)).cpu().numpy()
+    np.testing.assert_allclose(out, r, rtol=1e-5, atol=1e-9)

@@ -1,0 +1,135 @@
+"""GPU parity of the Sage-style attention path: quantization codes bit-exact against the
+oracle; attention outputs within tolerance of the oracle and of exact SDPA."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sage
+from tests.sage_workspace import decode
+
+pytestmark = pytest.mark.gpu
+
+
+def make_qkv(B, Hq, Hkv, Sq, Skv, seed=0, outlier=3.0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, Sq, 128, generator=g)
+    k = torch.randn(B, Hkv, Skv, 128, generator=g) + outlier * torch.randn(1, Hkv, 1, 128, generator=g)
+    v = torch.randn(B, Hkv, Skv, 128, generator=g)
+    return q.to(dtype), k.to(dtype), v.to(dtype)
+
+
+def cosine(a, b):
+    a = a.astype(np.float64).ravel()
+    b = b.astype(np.float64).ravel()
+    return float(a @ b / math.sqrt((a @ a) * (b @ b)))
+
+
+def check_codes(dec, q, k, v, B, Hq, Hkv, sm_scale):
+    for b in range(B):
+        for h in range(Hq):
+            hk = h // (Hq // Hkv)
+            ref = sage.quantize_head(q[b][h], k[b][hk], v[b][hk], sm_scale)
+            gq = dec[("q", b, h)]
+            assert np.array_equal(gq["codes"], ref["qcodes"]), (b, h)
+            assert np.array_equal(gq["scales"], ref["qscales"]), (b, h)
+        for h in range(Hkv):
+            ref = sage.quantize_head(q[b][0], k[b][h], v[b][h], sm_scale)
+            gk = dec[("k", b, h)]
+            assert np.array_equal(gk["kmean"], ref["kmean"]), (b, h)
+            assert np.array_equal(gk["codes"], ref["kcodes"]), (b, h)
+            assert np.array_equal(gk["scales"], ref["kscales"]), (b, h)
+            assert np.array_equal(gk["vscale"], ref["vscale"]), (b, h)
+            assert np.array_equal(gk["v8"], ref["v8"]), (b, h)
+
+
+@pytest.mark.parametrize("layout", ["HND", "NHD"])
+@pytest.mark.parametrize("shape", [(2, 4, 2, 200, 200), (1, 2, 2, 64, 1), (1, 3, 1, 129, 300)])
+def test_sage_quant_codes_bit_exact(cuda, layout, shape):
+    from quantfun2_b200.attention import sage_quantize
+
+    B, Hq, Hkv, Sq, Skv = shape
+    q, k, v = make_qkv(B, Hq, Hkv, Sq, Skv, seed=Sq)
+    sm = 1.0 / math.sqrt(128)
+    tr = (lambda t: t) if layout == "HND" else (lambda t: t.transpose(1, 2).contiguous())
+    ws, offs = sage_quantize(tr(q).to(cuda), tr(k).to(cuda), tr(v).to(cuda), sm, tensor_layout=layout)
+    torch.cuda.synchronize()
+    dec = decode(ws.cpu().numpy(), offs, B, Hq, Hkv, [Sq] * B, [Skv] * B,
+                 [b * ((Sq + 127) // 128) for b in range(B)], [b * ((Skv + 127) // 128) for b in range(B)])
+    check_codes(dec, q.float().numpy(), k.float().numpy(), v.float().numpy(), B, Hq, Hkv, sm)
+
+
+def test_sage_quant_codes_varlen_bit_exact(cuda):
+    from quantfun2_b200.attention import sage_quantize
+
+    lens = [130, 64, 257, 1]
+    Hq, Hkv = 4, 2
+    g = torch.Generator().manual_seed(11)
+    T = sum(lens)
+    q = torch.randn(T, Hq, 128, generator=g).bfloat16()
+    k = (torch.randn(T, Hkv, 128, generator=g) + 2 * torch.randn(1, Hkv, 128, generator=g)).bfloat16()
+    v = torch.randn(T, Hkv, 128, generator=g).bfloat16()
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    sm = 0.1
+    ws, offs = sage_quantize(q.to(cuda), k.to(cuda), v.to(cuda), sm, cu_seqlens_q=cu.to(cuda),
+                             cu_seqlens_k=cu.to(cuda), max_seqlen_q=max(lens), max_seqlen_k=max(lens))
+    torch.cuda.synchronize()
+    tile0 = [int(cu[b]) // 128 + b for b in range(len(lens))]
+    dec = decode(ws.cpu().numpy(), offs, len(lens), Hq, Hkv, lens, lens, tile0, tile0)
+    qs = [q[cu[b]:cu[b + 1]].float().permute(1, 0, 2).numpy() for b in range(len(lens))]
+    ks = [k[cu[b]:cu[b + 1]].float().permute(1, 0, 2).numpy() for b in range(len(lens))]
+    vs = [v[cu[b]:cu[b + 1]].float().permute(1, 0, 2).numpy() for b in range(len(lens))]
+    check_codes(dec, qs, ks, vs, len(lens), Hq, Hkv, sm)
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 2, 256, 256), (2, 4, 2, 200, 333), (1, 2, 1, 1000, 77)])
+def test_sage_attention_matches_oracle(cuda, shape):
+    from quantfun2_b200.attention import sageattn
+
+    B, Hq, Hkv, Sq, Skv = shape
+    q, k, v = make_qkv(B, Hq, Hkv, Sq, Skv, seed=7)
+    o = sageattn(q.to(cuda), k.to(cuda), v.to(cuda)).float().cpu().numpy()
+    qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
+    ro = sage.sageattn(qf, kf, vf)
+    rs = sage.sdpa_reference(qf, kf, vf)
+    c_or, c_sd = cosine(o, ro), cosine(o, rs)
+    print(f"cos(oracle)={c_or:.6f} cos(sdpa)={c_sd:.6f} maxabs(oracle)={np.abs(o - ro).max():.4g}")
+    assert c_or >= 0.9995
+    assert c_sd >= 0.998
+    assert np.abs(o - ro).max() < 0.05
+
+
+def test_sage_attention_nhd_and_varlen_consistent(cuda):
+    from quantfun2_b200.attention import sageattn, sageattn_varlen
+
+    lens = [300, 128, 45]
+    H = 2
+    outs = []
+    g = torch.Generator().manual_seed(5)
+    seqs = [torch.randn(3, L, H, 128, generator=g).bfloat16() for L in lens]
+    for s in seqs:
+        o = sageattn(s[0:1].to(cuda), s[1:2].to(cuda), s[2:3].to(cuda), tensor_layout="NHD")
+        outs.append(o[0])
+    cat = torch.cat(seqs, 1)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=cuda)
+    ov = sageattn_varlen(cat[0].to(cuda), cat[1].to(cuda), cat[2].to(cuda), cu, cu, max(lens), max(lens))
+    # same per-sequence math -> identical results
+    assert torch.equal(ov, torch.cat(outs, 0))
+
+
+def test_sage_attention_flux_shape_vs_sdpa(cuda):
+    """The benchmarked shape (B=1, 24 heads, 4608 tokens, D=128) against fp32 SDPA on the device."""
+    from quantfun2_b200.attention import sageattn
+
+    q, k, v = make_qkv(1, 24, 24, 4608, 4608, seed=1)
+    q, k, v = q.to(cuda), k.to(cuda), v.to(cuda)
+    o = sageattn(q, k, v).float()
+    r = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float())
+    c = torch.nn.functional.cosine_similarity(o.flatten(), r.flatten(), dim=0).item()
+    err = (o - r).abs().max().item()
+    print(f"cos={c:.6f} maxabs={err:.4g}")
+    assert c >= 0.998
+    from quantfun2_b200 import _lib
+
+    assert _lib.load().qf2_device_check() == 0

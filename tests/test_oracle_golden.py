@@ -1,0 +1,99 @@
+"""CPU: pin the oracle restatements to golden vectors produced by the reference code
+(tests/golden/make_golden.py imports the reference's eager bodies)."""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import ops, sage
+from oracle.numerics import bf16_bits_to_f32, f32_to_bf16_bits, round_bf16
+
+
+def cplx(a):
+    return a[..., 0] + 1j * a[..., 1]
+
+
+def test_rope_f32_matches_reference(golden):
+    f = cplx(golden["rope_freqs"]).astype(np.complex64)
+    oq, ok = ops.rope_apply(golden["rope_f32_xq"], golden["rope_f32_xk"], f, "f32")
+    np.testing.assert_allclose(oq, golden["rope_f32_oq"], rtol=0, atol=2e-6)
+    np.testing.assert_allclose(ok, golden["rope_f32_ok"], rtol=0, atol=2e-6)
+
+
+def test_rope_bf16_matches_reference_bits(golden):
+    f = cplx(golden["rope_freqs"]).astype(np.complex64)
+    xq = bf16_bits_to_f32(golden["rope_bf16_xq"])
+    xk = bf16_bits_to_f32(golden["rope_bf16_xk"])
+    oq, ok = ops.rope_apply(xq, xk, f, "bf16")
+    for got, ref in ((oq, golden["rope_bf16_oq"]), (ok, golden["rope_bf16_ok"])):
+        gb = f32_to_bf16_bits(got).astype(np.int32)
+        diff = np.abs(gb - ref.astype(np.int32))
+        assert diff.max() <= 1, diff.max()          # at most one bf16 ulp
+        assert (diff == 0).mean() > 0.999
+
+
+@pytest.mark.parametrize("tag", ["head", "row"])
+def test_rmsnorm_matches_reference(golden, tag):
+    eps = float(golden[f"rms_{tag}_eps"][0])
+    y = ops.rmsnorm_apply(golden[f"rms_{tag}_x_f32"], golden[f"rms_{tag}_w_f32"], eps, "f32")
+    np.testing.assert_allclose(y, golden[f"rms_{tag}_y_f32"], rtol=2e-6, atol=2e-6)
+    xb = bf16_bits_to_f32(golden[f"rms_{tag}_x_bf16"])
+    wb = bf16_bits_to_f32(golden[f"rms_{tag}_w_bf16"])
+    yb = ops.rmsnorm_apply(xb, wb, eps, "bf16")
+    diff = np.abs(f32_to_bf16_bits(yb).astype(np.int32) - golden[f"rms_{tag}_y_bf16"].astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.99
+
+
+def test_softmax_matches_reference(golden):
+    y = ops.softmax_lastdim(golden["softmax_x_f32"], "f32")
+    np.testing.assert_allclose(y, golden["softmax_y_f32"], rtol=1e-5, atol=1e-7)
+    yb = ops.softmax_lastdim(bf16_bits_to_f32(golden["softmax_x_bf16"]), "bf16")
+    diff = np.abs(f32_to_bf16_bits(yb).astype(np.int32) - golden["softmax_y_bf16"].astype(np.int32))
+    assert diff.max() <= 1
+
+
+def _joint_attention_oracle(g):
+    dim, heads, kvh, seq = [int(v) for v in g["jattn_meta"]]
+    D = dim // heads
+    x = g["jattn_x"].astype(np.float64)[0]
+    q = (x @ g["jattn_wq"].T.astype(np.float64)).astype(np.float32).reshape(1, seq, heads, D)
+    k = (x @ g["jattn_wk"].T.astype(np.float64)).astype(np.float32).reshape(1, seq, kvh, D)
+    v = (x @ g["jattn_wv"].T.astype(np.float64)).astype(np.float32).reshape(1, seq, kvh, D)
+    q = ops.rmsnorm_apply(q, g["jattn_qnorm"], 1e-6, "f32")
+    k = ops.rmsnorm_apply(k, g["jattn_knorm"], 1e-6, "f32")
+    f = cplx(g["jattn_freqs"]).astype(np.complex64)
+    q, k = ops.rope_apply(q, k, f, "f32")
+    o = sage.sdpa_reference(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3),
+                            1.0 / math.sqrt(D))
+    o = o.transpose(0, 2, 1, 3).reshape(1, seq, dim)
+    return (o.astype(np.float64) @ g["jattn_wo"].T.astype(np.float64)).astype(np.float32)
+
+
+def test_joint_attention_block_composition(golden):
+    """The oracle's QKV -> per-head RMSNorm -> RoPE -> SDPA -> O composition reproduces
+    the reference JointAttention.forward (src/models/common/attn.py:190-236)."""
+    y = _joint_attention_oracle(golden)
+    np.testing.assert_allclose(y, golden["jattn_y"], rtol=1e-4, atol=1e-5)
+
+
+def test_sage_oracle_close_to_sdpa():
+    rng = np.random.default_rng(0)
+    B, H, S, D = 1, 2, 200, 128
+    q = round_bf16(rng.standard_normal((B, H, S, D)).astype(np.float32))
+    k = round_bf16((rng.standard_normal((B, H, S, D)) + 3 * rng.standard_normal((1, H, 1, D))).astype(np.float32))
+    v = round_bf16(rng.standard_normal((B, H, S, D)).astype(np.float32))
+    o = sage.sageattn(q, k, v)
+    r = sage.sdpa_reference(q, k, v)
+    cos = float((o * r).sum() / np.sqrt((o * o).sum() * (r * r).sum()))
+    assert cos > 0.995, cos
+
+
+def test_sage_quant_rules():
+    """Hand-checkable cases of the stated quantization rules."""
+    x = np.zeros((64, 128), np.float32)
+    x[0, 0], x[1, 1], x[2, 2] = 127.0, 63.5, -0.5   # scale 1.0: ties go to even
+    codes, scales = sage._block_quant(x)
+    assert scales[0] == np.float32(1.0)
+    assert codes[0, 0] == 127 and codes[1, 1] == 64 and codes[2, 2] == 0
+    z, zs = sage._block_quant(np.zeros((70, 128), np.float32))
+    assert (z == 0).all() and (zs == 1.0).all() and zs.shape == (2,)
