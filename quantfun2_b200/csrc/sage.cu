@@ -270,19 +270,30 @@ __global__ void __launch_bounds__(256) sage_quant_kernel(const T* __restrict__ q
 }
 
 // ------------------------------------------------------------- attention --
-constexpr int kAttnThreads = 192;  // warp0 producer, warp1 MMA, warps2-5 softmax
+// One CTA = two 128-row Q tiles of one (sequence, head) sharing every K/V tile.
+//   warp 0      producer: bulk copies of Q tiles, K scales, K/V tiles (3-stage ring)
+//   warp 1      MMA issuer: per KV tile QK0, QK1 (kind::i8 -> S_t in TMEM), then
+//               PV0, PV1 of the previous tile (kind::f8f6f4 -> O_t in TMEM)
+//   warps 4-7   softmax for Q tile 0, warps 8-11 softmax for Q tile 1: one row per
+//               thread, TMEM -> registers, base-2 online softmax with lazy rescaling
+//               (the running max only moves when a row's max grows by more than
+//               kTau), P -> e4m3 into a double-buffered swizzled smem tile, epilogue
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// Registers: 384 threads x 168; a softmax thread holds its full 128-column S row.
+constexpr int kAttnThreads = 384;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;       // S double buffer: cols [0,128) and [128,256)
-constexpr uint32_t kColO = 256;     // O accumulator: cols [256,384)
+constexpr float kTau = 4.0f;                    // lazy-rescale threshold (log2 units)
+constexpr float kPScaleLog2 = kLog2_448 - kTau;  // P_fp8 = 2^(x - m_run + kPScaleLog2) <= 448
+constexpr float kMagic = 12582912.0f;           // 1.5 * 2^23
+constexpr int kMagicBits = 0x4B400000;
 
 struct AttnSmem {
-  // offsets (bytes) from the 1024-aligned dynamic smem base
-  static constexpr int q = 0;
-  static constexpr int kv = q + kTileBytes;                       // stages x (K, V)
-  static constexpr int p = kv + kStages * 2 * kTileBytes;          // 2 P buffers
-  static constexpr int kscale = p + 2 * kTileBytes;                // up to kMaxKvTiles x 16 B
+  static constexpr int q = 0;                                   // 2 Q tiles
+  static constexpr int kv = q + 2 * kTileBytes;                 // stages x (K, V)
+  static constexpr int p = kv + kStages * 2 * kTileBytes;       // 2 tiles x 2 buffers
+  static constexpr int kscale = p + 4 * kTileBytes;             // up to kMaxKvTiles x 16 B
   static constexpr int bars = kscale + kMaxKvTiles * 16;
-  static constexpr int nbars = 1 + 2 * kStages + 2 + 2 + 2 + 2 + 1 + 1;
+  static constexpr int nbars = 1 + 2 * kStages + 2 * (1 + 1 + 2 + 2) + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int total = misc + 64;
   static constexpr int alloc = total + 1024;  // slack for manual 1024-B alignment
@@ -329,13 +340,43 @@ QF2_DEV void store_row_out(void* out, const Strides3& os, int b, int h, int64_t 
   }
 }
 
-// grid (max q tiles, Hq, batch)
+// fma / add on two packed fp32 lanes (sm_100 f32x2 instructions)
+QF2_DEV float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
+QF2_DEV float2 fadd2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+QF2_DEV float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+
+// grid (ceil(max q tiles / 2), Hq, batch)
 __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P) {
   extern __shared__ uint8_t smem_raw[];
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int pair = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const SeqInfo sq = seq_q(P.g, b);
   const int64_t nqt = (sq.len + kTile - 1) / kTile;
-  if (qt >= nqt) return;
+  const int qt0 = 2 * pair;
+  if (qt0 >= nqt) return;
+  const int ntile = (qt0 + 1 < nqt) ? 2 : 1;  // Q tiles in this CTA
   const SeqInfo sk = seq_k(P.g, b);
   const int nkt = (int)((sk.len + kTile - 1) / kTile);
   const int hk = h / (P.Hq / P.Hkv);
@@ -346,15 +387,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   uint8_t* sP = base + AttnSmem::p;
   float4* sKS = reinterpret_cast<float4*>(base + AttnSmem::kscale);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + AttnSmem::bars);
-  uint64_t* bar_q = bars + 0;
+  uint64_t* bar_q = bars;
   uint64_t* bar_kv_full = bars + 1;
-  uint64_t* bar_kv_empty = bars + 1 + kStages;
-  uint64_t* bar_s_full = bars + 1 + 2 * kStages;
-  uint64_t* bar_s_empty = bar_s_full + 2;
-  uint64_t* bar_p_full = bar_s_empty + 2;
-  uint64_t* bar_p_empty = bar_p_full + 2;
-  uint64_t* bar_o = bar_p_empty + 2;
-  uint64_t* bar_drain = bar_o + 1;
+  uint64_t* bar_kv_empty = bar_kv_full + kStages;
+  uint64_t* bar_s_full = bar_kv_empty + kStages;  // [2] per Q tile
+  uint64_t* bar_s_empty = bar_s_full + 2;          // [2]
+  uint64_t* bar_p_full = bar_s_empty + 2;          // [2 tiles][2 buffers]
+  uint64_t* bar_o_done = bar_p_full + 4;           // [2 tiles][PV index parity]
+  uint64_t* bar_drain = bar_o_done + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + AttnSmem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + AttnSmem::misc + 8);
 
@@ -363,13 +403,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
     for (int s = 0; s < kStages; ++s) { mbar_init(bar_kv_full + s, 1); mbar_init(bar_kv_empty + s, 1); }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar_s_full + s, 1);
-      mbar_init(bar_s_empty + s, 4);
-      mbar_init(bar_p_full + s, 4);
-      mbar_init(bar_p_empty + s, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar_s_full + t, 1);
+      mbar_init(bar_s_empty + t, 4);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(bar_p_full + 2 * t + i, 4);
+        mbar_init(bar_o_done + 2 * t + i, 1);
+      }
     }
-    mbar_init(bar_o, 1);
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -389,13 +430,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
     *abort_flag = 1;
   };
 
-  if (warp == 0) {
-    // ------------------------------------------------------- producer --
-    if (lane == 0 && nkt > 0) {
-      const int64_t qslot = (int64_t)h * ws.tq + sq.tile0 + qt;
+  if (warp < 4) {
+    if (warp == 0 && lane == 0 && nkt > 0) {
+      // ------------------------------------------------------- producer --
+      const int64_t qslot = (int64_t)h * ws.tq + sq.tile0 + qt0;
       const int64_t kslot0 = (int64_t)hk * ws.tk + sk.tile0;
-      mbar_arrive_expect_tx(bar_q, kTileBytes + nkt * 16);
-      bulk_g2s(sQ, ws.qc + qslot * kTileBytes, kTileBytes, bar_q);
+      mbar_arrive_expect_tx(bar_q, ntile * kTileBytes + nkt * 16);
+      bulk_g2s(sQ, ws.qc + qslot * kTileBytes, ntile * kTileBytes, bar_q);
       bulk_g2s(sKS, ws.ks + kslot0 * 4, nkt * 16, bar_q);
       int issued = 0;
       for (int j = 0; j < nkt; ++j) {
@@ -413,41 +454,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
           mbar_wait(bar_kv_full + (j % kStages), (j / kStages) & 1);
       }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA --
-    if (lane == 0 && nkt > 0) {
-      constexpr uint32_t idesc_qk = make_idesc(2, 1, 1, 0, 0, kTile, kTile);        // s8 x s8 -> s32
-      constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 0, 0, kTile, kHeadDim);     // e4m3 x e4m3 -> f32
-      const uint32_t aQ = smem_u32(sQ);
+    } else if (warp == 1 && lane == 0 && nkt > 0) {
+      // ------------------------------------------------------------ MMA --
+      constexpr uint32_t idesc_qk = make_idesc(2, 1, 1, 0, 0, kTile, kTile);     // s8 x s8 -> s32
+      constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 0, 0, kTile, kHeadDim);  // e4m3 x e4m3 -> f32
       bool ok = mbar_wait(bar_q, 0);
       auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1;
-        if (!mbar_wait(bar_p_full + pb, (i >> 1) & 1) || *abort_flag) return false;
-        tc_fence_after();
-        const uint32_t aP = smem_u32(sP + pb * kTileBytes);
         const uint32_t aV = smem_u32(sKV + (i % kStages) * 2 * kTileBytes + kTileBytes);
+        for (int t = 0; t < ntile; ++t) {
+          if (!mbar_wait(bar_p_full + 2 * t + (i & 1), (i >> 1) & 1) || *abort_flag) return false;
+          tc_fence_after();
+          const uint32_t aP = smem_u32(sP + (2 * t + (i & 1)) * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f8f6f4(tmem + kColO, sdesc_sw128_kmajor(aP + kk * 32), sdesc_sw128_kmajor(aV + kk * 32), idesc_pv,
-                     (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f8f6f4(tmem + 256 + t * 128, sdesc_sw128_kmajor(aP + kk * 32), sdesc_sw128_kmajor(aV + kk * 32),
+                       idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(bar_o_done + 2 * t + (i & 1));
+        }
         tc_commit(bar_kv_empty + (i % kStages));
-        tc_commit(bar_p_empty + pb);
-        tc_commit(bar_o);
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j) {
-        const int s = j % kStages, sb = j & 1;
+        const int s = j % kStages;
         if (!mbar_wait(bar_kv_full + s, (j / kStages) & 1) || *abort_flag) { ok = false; break; }
-        if (!mbar_wait(bar_s_empty + sb, ((j >> 1) & 1) ^ 1) || *abort_flag) { ok = false; break; }
-        tc_fence_after();
         const uint32_t aK = smem_u32(sKV + s * 2 * kTileBytes);
+        for (int t = 0; t < ntile && ok; ++t) {
+          if (j > 0 && (!mbar_wait(bar_s_empty + t, (j - 1) & 1) || *abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aQ = smem_u32(sQ + t * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_i8(tmem + kColS + sb * kTile, sdesc_sw128_kmajor(aQ + kk * 32), sdesc_sw128_kmajor(aK + kk * 32),
-                 idesc_qk, kk > 0 ? 1u : 0u);
-        tc_commit(bar_s_full + sb);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+          for (int kk = 0; kk < 4; ++kk)
+            mma_i8(tmem + t * 128, sdesc_sw128_kmajor(aQ + kk * 32), sdesc_sw128_kmajor(aK + kk * 32), idesc_qk,
+                   kk > 0 ? 1u : 0u);
+          tc_commit(bar_s_full + t);
+        }
+        if (ok && j > 0 && !issue_pv(j - 1)) ok = false;
       }
       if (ok) ok = issue_pv(nkt - 1);
       if (!ok) fail(kDevTimeoutMma);
@@ -457,124 +498,142 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
     }
   } else {
     // -------------------------------------------------------- softmax --
+    const int t = (warp >> 2) - 1;  // Q tile of this warpgroup
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int64_t qslot = (int64_t)h * ws.tq + sq.tile0 + qt;
-    const float sqs = ws.qs[qslot * 4 + (row >> 6)];
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + 256 + t * 128;
+    const bool active = t < ntile;
+    const int qt = qt0 + t;
     const float* vsc = ws.vs + ((int64_t)b * P.Hkv + hk) * kHeadDim;
-    float m_run = -INFINITY, l_run = 0.f;
     // warp-uniform bounded wait: every lane agrees on the outcome, so the
     // .sync.aligned tcgen05 ops that follow always see a converged warp
     auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
       const bool w = mbar_wait(bar, parity) && (*abort_flag == 0);
       return __all_sync(0xffffffffu, w);
     };
-    bool ok = nkt > 0;
-    if (ok) ok = wwait(bar_q, 0);  // k scales are in smem once Q has landed
+    bool ok = active && nkt > 0;
+    float sqs = 0.f;
+    if (ok) {
+      const int64_t qslot = (int64_t)h * ws.tq + sq.tile0 + qt;
+      sqs = ws.qs[qslot * 4 + (row >> 6)];
+      ok = wwait(bar_q, 0);  // k scales are in smem once the Q tiles have landed
+    }
+    float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; ok && j < nkt; ++j) {
-      const int sb = j & 1;
-      if (!wwait(bar_s_full + sb, (j >> 1) & 1)) { ok = false; break; }
+      if (!wwait(bar_s_full + t, j & 1)) { ok = false; break; }
       tc_fence_after();
-      uint32_t s[4][32];
+      uint32_t s[128];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_off + kColS + sb * kTile + c * 32, s[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_s_empty + sb);
+      if (lane == 0) mbar_arrive(bar_s_empty + t);
 
+      // int32 -> fp32 exactly via the 1.5*2^23 magic constant (|s| < 2^22)
+      float mf[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) mf[i] = __int_as_float((int)s[i] + kMagicBits);
+      const int64_t rem = sk.len - (int64_t)j * kTile;
+      if (rem < kTile) {
+        // ragged last tile: 0.0 is below every magic-encoded value, so it acts as -inf
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= rem) mf[i] = 0.0f;
+      }
+      float mx0 = mf[0], mx1 = mf[64];
+#pragma unroll
+      for (int i = 1; i < 63; i += 2) mx0 = fmax3(mx0, mf[i], mf[i + 1]);
+      mx0 = fmaxf(mx0, mf[63]);
+#pragma unroll
+      for (int i = 65; i < 127; i += 2) mx1 = fmax3(mx1, mf[i], mf[i + 1]);
+      mx1 = fmaxf(mx1, mf[127]);
       const float4 ksc = sKS[j];
       const float sc0 = sqs * ksc.x, sc1 = sqs * ksc.y;
-      const int64_t rem = sk.len - (int64_t)j * kTile;
-      const int valid = rem < kTile ? (int)rem : kTile;
-      // dequantize to base-2 logits, row max
-      float f[4][32];
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float sc = c < 2 ? sc0 : sc1;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          // exact int32 -> fp32 for |x| < 2^22 via the 1.5*2^23 magic constant
-          const float xi = __int_as_float((int)s[c][i] + 0x4B400000) - 12582912.0f;
-          float v = xi * sc;
-          if (c * 32 + i >= valid) v = -INFINITY;
-          f[c][i] = v;
-          mx = fmaxf(mx, v);
-        }
+      const float m_tile = fmaxf((mx0 - kMagic) * sc0, (mx1 - kMagic) * sc1);
+      const float m_new = fmaxf(m_run, m_tile);
+      const bool rescale = __any_sync(0xffffffffu, m_new > m_run + kTau);
+      float alpha = 1.0f;
+      if (rescale) {
+        alpha = fast_exp2(m_run - m_new);  // 0 on the first tile
+        m_run = m_new;
+        l_run *= alpha;
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = fast_exp2(m_run - m_new);  // 0 on the first tile
-      const float bias = m_new - kLog2_448;          // p * 448 = 2^(x - bias)
-      if (!wwait(bar_p_empty + sb, ((j >> 1) & 1) ^ 1)) { ok = false; break; }
-      uint8_t* pdst = sP + sb * kTileBytes;
-      float rs = 0.f;
+      // P_fp8 = 2^(x - m_run + kPScaleLog2), x = (mf - magic) * sc: exact subtraction, one fma
+      const float bias = m_run - kPScaleLog2;
+      const float2 nb = make_float2(-bias, -bias), nmag = make_float2(-kMagic, -kMagic);
+      const float2 sc0v = make_float2(sc0, sc0), sc1v = make_float2(sc1, sc1);
+      // the P buffer (j & 1) was last read by PV(j-2)
+      if (j >= 2 && !wwait(bar_o_done + 2 * t + (j & 1), ((j - 2) >> 1) & 1)) { ok = false; break; }
+      uint8_t* pdst = sP + (2 * t + (j & 1)) * kTileBytes;
+      float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int chunk = 0; chunk < 8; ++chunk) {
+        const float2 scv = chunk < 4 ? sc0v : sc1v;
+        uint32_t w[4];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t w[4];
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const int i0 = half * 16 + q4 * 4;
-            const float p0 = fast_exp2(f[c][i0 + 0] - bias);
-            const float p1 = fast_exp2(f[c][i0 + 1] - bias);
-            const float p2 = fast_exp2(f[c][i0 + 2] - bias);
-            const float p3 = fast_exp2(f[c][i0 + 3] - bias);
-            rs += (p0 + p1) + (p2 + p3);
-            w[q4] = (uint32_t)f32x2_to_e4m3x2(p0, p1) | ((uint32_t)f32x2_to_e4m3x2(p2, p3) << 16);
-          }
-          const int chunk = c * 2 + half;  // 16-byte chunk index along kv
-          *reinterpret_cast<uint4*>(pdst + swz(row, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int i0 = chunk * 16 + q4 * 4;
+          const float2 x01 = ffma2(fadd2(make_float2(mf[i0], mf[i0 + 1]), nmag), scv, nb);
+          const float2 x23 = ffma2(fadd2(make_float2(mf[i0 + 2], mf[i0 + 3]), nmag), scv, nb);
+          const float2 p01 = make_float2(fast_exp2(x01.x), fast_exp2(x01.y));
+          const float2 p23 = make_float2(fast_exp2(x23.x), fast_exp2(x23.y));
+          acc = fadd2(acc, fadd2(p01, p23));
+          w[q4] = (uint32_t)f32x2_to_e4m3x2(p01.x, p01.y) | ((uint32_t)f32x2_to_e4m3x2(p23.x, p23.y) << 16);
         }
+        *reinterpret_cast<uint4*>(pdst + swz(row, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l_run = l_run * alpha + rs;
-      m_run = m_new;
-      fence_async_smem();
-      if (j > 0) {
-        // PV(j-1) must have finished accumulating before O is rescaled
-        if (!wwait(bar_o, (j - 1) & 1)) { ok = false; break; }
+      l_run += acc.x + acc.y;
+      if (rescale && j > 0) {
+        // O holds sum_{i<j} P_i V_i against the old max: PV(j-1) must have finished
+        // before the rescale, and PV(j) is only issued after p_full(j) below
+        if (!wwait(bar_o_done + 2 * t + ((j - 1) & 1), ((j - 1) >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_off + kColO + c * 32, o);
-            tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem + lane_off + kColO + c * 32, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
         }
+        tmem_wait_st();
       }
+      fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p_full + sb);
+      if (lane == 0) mbar_arrive(bar_p_full + 2 * t + (j & 1));
     }
-    if (!ok && nkt > 0) fail(kDevTimeoutSoftmax);
+    if (active && nkt > 0 && !ok) fail(kDevTimeoutSoftmax);
     // ------------------------------------------------------- epilogue --
-    const int64_t r_tok = (int64_t)qt * kTile + row;
-    if (ok && nkt > 0) {
-      if (!wwait(bar_o, (nkt - 1) & 1)) { fail(kDevTimeoutEpilogue); ok = false; }
-      tc_fence_after();
-    }
-    const float inv_l = (ok && l_run > 0.f) ? 1.0f / l_run : 0.f;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      uint32_t o[32];
+    if (active) {
+      const int64_t r_tok = (int64_t)qt * kTile + row;
       if (ok && nkt > 0) {
-        tmem_ld32(tmem + lane_off + kColO + c * 32, o);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0u;
+        if (!wwait(bar_o_done + 2 * t + ((nkt - 1) & 1), ((nkt - 1) >> 1) & 1)) {
+          fail(kDevTimeoutEpilogue);
+          ok = false;
+        }
+        tc_fence_after();
       }
-      float of[32];
+      const float inv_l = (ok && l_run > 0.f) ? 1.0f / l_run : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        if (ok && nkt > 0) {
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+        } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) of[i] = __uint_as_float(o[i]) * vsc[c * 32 + i] * inv_l;
-      if (r_tok < sq.len) store_row_out(P.out, P.os, P.g.cu_q ? 0 : b, h, sq.tok0 + r_tok, of, P.out_bf16, c * 32);
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        float of[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) of[i] = __uint_as_float(o[i]) * vsc[c * 32 + i] * inv_l;
+        if (r_tok < sq.len) store_row_out(P.out, P.os, P.g.cu_q ? 0 : b, h, sq.tok0 + r_tok, of, P.out_bf16, c * 32);
+      }
     }
   }
 
@@ -719,8 +778,8 @@ static int launch_attn(const Args& a) {
   if (cudaFuncSetAttribute(sage_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::alloc) !=
       cudaSuccess)
     return QF2_ERR_LAUNCH;
-  sage_attn_kernel<<<dim3((unsigned)mqt, (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads, AttnSmem::alloc,
-                     a.stream>>>(P);
+  sage_attn_kernel<<<dim3((unsigned)((mqt + 1) / 2), (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads,
+                     AttnSmem::alloc, a.stream>>>(P);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }
