@@ -102,8 +102,9 @@ int qf2_softmax_inplace(void* x, int64_t rows, int64_t n, int64_t row_stride, in
  * and sageattn_varlen (src/models/common/attn.py:109-120).
  * Algorithm: K smoothed by its per-(sequence, head, channel) token mean; Q
  * (pre-multiplied by sm_scale*log2(e)) and smoothed K quantized to INT8 per
- * 64-token block (scale = amax/127, round half to even); V quantized to FP8
- * e4m3 per channel (scale = amax/448); S = Qi8.Ki8^T on tcgen05 kind::i8 into
+ * 64-token block (code = rint(x * (127/amax)), scale = amax/127); V quantized
+ * to FP8 e4m3 per channel (code = e4m3(v * (448/amax)), scale = amax/448);
+ * S = Qi8.Ki8^T on tcgen05 kind::i8 into
  * TMEM; online softmax in base 2; P quantized to e4m3 (x448) and P.V on
  * tcgen05 kind::f8f6f4 with fp32 accumulation in TMEM.  D = 128 only.
  *
@@ -128,8 +129,9 @@ int qf2_sageattn_varlen(const void* q, const int64_t* q_strides, const void* k, 
                         int64_t workspace_bytes, qf2_stream_t stream);
 
 /* Byte offsets inside the Sage workspace (for inspecting the quantized codes):
- * offsets[0..9] = status, q codes, q scales, k codes, k scales, v codes,
- * v scales, k mean, k-sum partials, v-amax partials; offsets[10] = total. */
+ * offsets[0..10] = status, q codes, q scales, k codes, k scales, v codes,
+ * v scales, k mean, v inverse scales, k-sum partials, v-amax partials;
+ * offsets[11] = total. */
 int qf2_sage_workspace_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
                               int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t D, int64_t* offsets);
 

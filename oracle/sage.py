@@ -14,11 +14,13 @@ so that the CUDA path can be checked bit-exactly against it:
      k' = float32(k) - km  (one fp32 rounding).
   2. Q pre-scale: q' = float32(q) * c with c = float32(float64(float32(sm_scale)) * log2(e)),
      which folds the softmax scale and the base-2 exponent into Q.
-  3. INT8 per 64-token block (per sequence, head): scale = float32(amax) / 127 in fp32
-     (1.0 for an all-zero block); code = rint(x / scale) (fp32 division, round half to
-     even), clamped to [-127, 127].
-  4. V per channel over the whole sequence: vs = amax / 448 (fp32; 1.0 if zero);
-     v8 = e4m3(v / vs) with round-to-nearest-even.
+  3. INT8 per 64-token block (per sequence, head): inv = 127 / amax and the dequant
+     scale = amax / 127, both one fp32 IEEE division (1.0 for an all-zero block);
+     code = rint(float32(x * inv)) (round half to even), clamped to [-127, 127].
+     (The published kernels divide by the scale; multiplying by the block reciprocal
+     is this build's definition -- one rounding per element either way.)
+  4. V per channel over the whole sequence: vinv = 448 / amax, vs = amax / 448 (fp32;
+     1.0 if zero); v8 = e4m3(float32(v * vinv)) with round-to-nearest-even.
   5. Logits (base 2): S = (int32)(qcode . kcode) * (sq * sk)  (fp32 product of scales).
   6. Softmax in base 2; P = e4m3(448 * 2^(S - rowmax)); O = (P . v8) * vs / sum(448 * 2^(S - rowmax)).
      The GPU kernel does step 6 online (running max per 128-key tile), so its P
@@ -49,9 +51,10 @@ def _block_quant(x: np.ndarray):
     for i in range(nb):
         blk = x[i * QBLOCK:(i + 1) * QBLOCK]
         am = np.float32(np.max(np.abs(blk))) if blk.size else np.float32(0)
-        sc = (am / np.float32(127.0)).astype(np.float32) if am > 0 else np.float32(1.0)
+        sc = np.float32(am / np.float32(127.0)) if am > 0 else np.float32(1.0)
+        inv = np.float32(np.float32(127.0) / am) if am > 0 else np.float32(1.0)
         scales[i] = sc
-        c = np.rint((blk / sc).astype(np.float32))
+        c = np.rint((blk * inv).astype(np.float32))
         codes[i * QBLOCK:(i + 1) * QBLOCK] = np.clip(c, -127, 127).astype(np.int8)
     return codes, scales
 
@@ -69,18 +72,11 @@ def quantize_head(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float):
     kcodes, kscales = _block_quant(kx)
     v = np.asarray(v, dtype=np.float32)
     am = np.max(np.abs(v), axis=0).astype(np.float32) if v.shape[0] else np.zeros(v.shape[1], np.float32)
-    vscale = np.where(am > 0, (am / np.float32(448.0)).astype(np.float32), np.float32(1.0)).astype(np.float32)
-    v8 = to_e4m3_bits((v / vscale[None, :]).astype(np.float32))
+    safe = np.where(am > 0, am, np.float32(1.0)).astype(np.float32)
+    vscale = np.where(am > 0, (safe / np.float32(448.0)).astype(np.float32), np.float32(1.0)).astype(np.float32)
+    vinv = np.where(am > 0, (np.float32(448.0) / safe).astype(np.float32), np.float32(1.0)).astype(np.float32)
+    v8 = to_e4m3_bits((v * vinv[None, :]).astype(np.float32))
     return dict(qcodes=qcodes, qscales=qscales, kcodes=kcodes, kscales=kscales, kmean=kmean, v8=v8, vscale=vscale)
-
-
-def kmean_vscale(k: np.ndarray, v: np.ndarray):
-    k = np.asarray(k, dtype=np.float32)
-    v = np.asarray(v, dtype=np.float32)
-    kmean = (np.sum(k.astype(np.float64), axis=0) / max(k.shape[0], 1)).astype(np.float32)
-    am = np.max(np.abs(v), axis=0).astype(np.float32)
-    vscale = np.where(am > 0, (am / np.float32(448.0)).astype(np.float32), np.float32(1.0)).astype(np.float32)
-    return kmean, vscale
 
 
 def attention_from_codes(qz: dict) -> np.ndarray:

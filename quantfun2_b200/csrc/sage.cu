@@ -76,7 +76,7 @@ struct Workspace {
   int8_t* qc; float* qs;
   int8_t* kc; float* ks;
   uint8_t* vc; float* vs;
-  float* kmean;
+  float* kmean; float* vinv;
   double* ksum_part; float* vamax_part;
   int64_t tq, tk;   // tile slots per head
   int64_t nch;      // stats chunks per sequence
@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(128) sage_finalize_kernel(SeqGeom g, int Hkv, 
   const int64_t o = ((int64_t)b * Hkv + h) * kHeadDim + c;
   ws.kmean[o] = si.len > 0 ? (float)(acc / (double)si.len) : 0.f;
   ws.vs[o] = am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f;
+  ws.vinv[o] = am > 0.f ? __fdiv_rn(448.0f, am) : 1.0f;
 }
 
 // ----------------------------------------------------------------- quant --
@@ -152,7 +153,18 @@ __global__ void __launch_bounds__(128) sage_finalize_kernel(SeqGeom g, int Hkv, 
 // 128B-swizzle K-major layout: row r at r*128, chunk c at slot c ^ (r & 7).
 QF2_DEV int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
+template <typename T>
+QF2_DEV void unpack8(const uint4& raw, float* f) {
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = to_f32(e[j]);
+}
+
 // grid (max tiles, Hq + 2*Hkv, batch), 256 threads.
+// Q/K tile: thread = (row slot 0..15, 8-channel chunk 0..15), rows slot + 16*i.
+//   code = rint(x * (127 / amax_block)) with x = q * qmul or k - kmean (fp32).
+// V tile: thread = (channel pair 0..63, 32-token group 0..3); writes rows of V^T.
+//   code = e4m3(v * (448 / amax_channel)).
 template <typename T>
 __global__ void __launch_bounds__(256) sage_quant_kernel(const T* __restrict__ q, Strides3 qs_, const T* __restrict__ k,
                                                          Strides3 ks_, const T* __restrict__ v, Strides3 vs_, SeqGeom g,
@@ -162,7 +174,6 @@ __global__ void __launch_bounds__(256) sage_quant_kernel(const T* __restrict__ q
   __shared__ float s_red[2][8];
 
   if (job < Hq + Hkv) {
-    // ---- Q or K: 128 rows x 128 channels, INT8 per 64-row block ----
     const bool is_q = job < Hq;
     const int h = is_q ? job : job - Hq;
     const SeqInfo si = is_q ? seq_q(g, b) : seq_k(g, b);
@@ -172,32 +183,31 @@ __global__ void __launch_bounds__(256) sage_quant_kernel(const T* __restrict__ q
     const Strides3 st = is_q ? qs_ : ks_;
     const int rg = tid >> 4, c8 = tid & 15;
     float sub[8];
+    if (is_q) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sub[j] = 0.f;
-    if (!is_q) {
-      const float* km = ws.kmean + ((int64_t)b * Hkv + h) * kHeadDim + c8 * 8;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sub[j] = km[j];
+      for (int j = 0; j < 8; ++j) sub[j] = 0.f;
+    } else {
+      const float4* km = reinterpret_cast<const float4*>(ws.kmean + ((int64_t)b * Hkv + h) * kHeadDim + c8 * 8);
+      const float4 a = km[0], c = km[1];
+      sub[0] = a.x; sub[1] = a.y; sub[2] = a.z; sub[3] = a.w; sub[4] = c.x; sub[5] = c.y; sub[6] = c.z; sub[7] = c.w;
     }
-    float x[8][8];
-    float am[2] = {0.f, 0.f};
+    const T* base = src + (int64_t)b * st.b + (int64_t)h * st.h + (si.tok0 + (int64_t)tile * kTile) * st.s + c8 * 8;
+    const int valid = (int)min((int64_t)kTile, si.len - (int64_t)tile * kTile);
+    uint4 raw[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = rg + 16 * i;
-      const int64_t t = (int64_t)tile * kTile + r;
-      if (t < si.len) {
-        const T* row = src + (int64_t)b * st.b + (int64_t)h * st.h + (si.tok0 + t) * st.s + c8 * 8;
-        const uint4 raw = *reinterpret_cast<const uint4*>(row);
-        const T* e = reinterpret_cast<const T*>(&raw);
+      raw[i] = r < valid ? *reinterpret_cast<const uint4*>(base + (int64_t)r * st.s) : make_uint4(0, 0, 0, 0);
+    }
+    auto xform = [&](float f, int j) { return is_q ? __fmul_rn(f, qmul) : __fsub_rn(f, sub[j]); };
+    float am[2] = {0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float f = to_f32(e[j]);
-          x[i][j] = is_q ? __fmul_rn(f, qmul) : __fsub_rn(f, sub[j]);
-          am[i >> 2] = fmaxf(am[i >> 2], fabsf(x[i][j]));
-        }
-      } else {
+    for (int i = 0; i < 8; ++i) {
+      if (rg + 16 * i < valid) {
+        float f[8];
+        unpack8<T>(raw[i], f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
+        for (int j = 0; j < 8; ++j) am[i >> 2] = fmaxf(am[i >> 2], fabsf(xform(f[j], j)));
       }
     }
 #pragma unroll
@@ -210,26 +220,30 @@ __global__ void __launch_bounds__(256) sage_quant_kernel(const T* __restrict__ q
     float bm[2] = {0.f, 0.f};
 #pragma unroll
     for (int w = 0; w < 8; ++w) { bm[0] = fmaxf(bm[0], s_red[0][w]); bm[1] = fmaxf(bm[1], s_red[1][w]); }
-    const float scale[2] = {bm[0] > 0.f ? __fdiv_rn(bm[0], 127.0f) : 1.0f,
-                            bm[1] > 0.f ? __fdiv_rn(bm[1], 127.0f) : 1.0f};
+    const float inv[2] = {bm[0] > 0.f ? __fdiv_rn(127.0f, bm[0]) : 1.0f, bm[1] > 0.f ? __fdiv_rn(127.0f, bm[1]) : 1.0f};
     const int64_t slot = (int64_t)h * (is_q ? ws.tq : ws.tk) + si.tile0 + tile;
     int8_t* dst = (is_q ? ws.qc : ws.kc) + slot * kTileBytes;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = rg + 16 * i;
-      const float s = scale[i >> 2];
       uint32_t w[2] = {0u, 0u};
+      if (r < valid) {
+        float f[8];
+        unpack8<T>(raw[i], f);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        int c = __float2int_rn(__fdiv_rn(x[i][j], s));
-        c = max(-127, min(127, c));
-        w[j >> 2] |= (uint32_t)(c & 0xff) << ((j & 3) * 8);
+        for (int j = 0; j < 8; ++j) {
+          int c = __float2int_rn(__fmul_rn(xform(f[j], j), inv[i >> 2]));
+          c = max(-127, min(127, c));
+          w[j >> 2] |= (uint32_t)(c & 0xff) << ((j & 3) * 8);
+        }
       }
       *reinterpret_cast<uint2*>(dst + swz(r, c8 >> 1) + (c8 & 1) * 8) = make_uint2(w[0], w[1]);
     }
     if (tid == 0) {
       float* sc = (is_q ? ws.qs : ws.ks) + slot * 4;
-      *reinterpret_cast<float4*>(sc) = make_float4(scale[0], scale[1], 0.f, 0.f);
+      const float s0 = bm[0] > 0.f ? __fdiv_rn(bm[0], 127.0f) : 1.0f;
+      const float s1 = bm[1] > 0.f ? __fdiv_rn(bm[1], 127.0f) : 1.0f;
+      *reinterpret_cast<float4*>(sc) = make_float4(s0, s1, 0.f, 0.f);
     }
   } else {
     // ---- V: transpose to [d][token] and quantize to e4m3 per channel ----
@@ -238,26 +252,28 @@ __global__ void __launch_bounds__(256) sage_quant_kernel(const T* __restrict__ q
     const int64_t ntiles = (si.len + kTile - 1) / kTile;
     if (tile >= ntiles) return;
     const int dp = tid & 63, tg = tid >> 6;  // channel pair, 32-token group
-    const float* vsc = ws.vs + ((int64_t)b * Hkv + h) * kHeadDim;
-    const float s0 = vsc[2 * dp], s1 = vsc[2 * dp + 1];
-    uint32_t out0[8], out1[8];  // 32 bytes per channel
+    const float2 inv = *reinterpret_cast<const float2*>(ws.vinv + ((int64_t)b * Hkv + h) * kHeadDim + 2 * dp);
+    const int valid = (int)min((int64_t)kTile, si.len - (int64_t)tile * kTile);
+    const T* base = v + (int64_t)b * vs_.b + (int64_t)h * vs_.h + (si.tok0 + (int64_t)tile * kTile + tg * 32) * vs_.s +
+                    2 * dp;
+    uint32_t raw[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) { out0[i] = 0u; out1[i] = 0u; }
+    for (int i = 0; i < 32; ++i)
+      raw[i] = (tg * 32 + i < valid) ? *reinterpret_cast<const uint32_t*>(base + (int64_t)i * vs_.s) : 0u;
+    uint32_t out0[8], out1[8];  // 32 bytes of V^T row per channel
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int64_t t = (int64_t)tile * kTile + tg * 32 + i;
-      float a = 0.f, c = 0.f;
-      if (t < si.len) {
-        const T* row = v + (int64_t)b * vs_.b + (int64_t)h * vs_.h + (si.tok0 + t) * vs_.s + 2 * dp;
-        const uint32_t raw = *reinterpret_cast<const uint32_t*>(row);
-        const T* e = reinterpret_cast<const T*>(&raw);
-        a = __fdiv_rn(to_f32(e[0]), s0);
-        c = __fdiv_rn(to_f32(e[1]), s1);
+    for (int i = 0; i < 32; i += 2) {
+      const T* e0 = reinterpret_cast<const T*>(&raw[i]);
+      const T* e1 = reinterpret_cast<const T*>(&raw[i + 1]);
+      const uint16_t p0 = f32x2_to_e4m3x2(__fmul_rn(to_f32(e0[0]), inv.x), __fmul_rn(to_f32(e1[0]), inv.x));
+      const uint16_t p1 = f32x2_to_e4m3x2(__fmul_rn(to_f32(e0[1]), inv.y), __fmul_rn(to_f32(e1[1]), inv.y));
+      if ((i & 2) == 0) {
+        out0[i >> 2] = p0;
+        out1[i >> 2] = p1;
+      } else {
+        out0[i >> 2] |= (uint32_t)p0 << 16;
+        out1[i >> 2] |= (uint32_t)p1 << 16;
       }
-      const uint16_t pa = f32x2_to_e4m3x2(a, 0.f);
-      const uint16_t pc = f32x2_to_e4m3x2(c, 0.f);
-      out0[i >> 2] |= (uint32_t)(pa & 0xff) << ((i & 3) * 8);
-      out1[i >> 2] |= (uint32_t)(pc & 0xff) << ((i & 3) * 8);
     }
     const int64_t slot = (int64_t)h * ws.tk + si.tile0 + tile;
     uint8_t* dst = ws.vc + slot * kTileBytes;
@@ -648,7 +664,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
 
 // ------------------------------------------------------------------ host --
 struct Layout {
-  int64_t off[11];
+  int64_t off[12];
   int64_t tq, tk, nch;
 };
 
@@ -675,9 +691,10 @@ static Layout make_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_
   put(5, Hkv * L.tk * kTileBytes);                   // v codes (V^T tiles)
   put(6, batch * Hkv * kHeadDim * 4);                // v scales
   put(7, batch * Hkv * kHeadDim * 4);                // k mean
-  put(8, batch * Hkv * L.nch * kHeadDim * 8);        // k sum partials (fp64)
-  put(9, batch * Hkv * L.nch * kHeadDim * 4);        // v amax partials
-  L.off[10] = o;
+  put(8, batch * Hkv * kHeadDim * 4);                // v inverse scales (448 / amax)
+  put(9, batch * Hkv * L.nch * kHeadDim * 8);        // k sum partials (fp64)
+  put(10, batch * Hkv * L.nch * kHeadDim * 4);       // v amax partials
+  L.off[11] = o;
   return L;
 }
 
@@ -692,8 +709,9 @@ static Workspace bind_ws(void* w, const Layout& L) {
   ws.vc = reinterpret_cast<uint8_t*>(p + L.off[5]);
   ws.vs = reinterpret_cast<float*>(p + L.off[6]);
   ws.kmean = reinterpret_cast<float*>(p + L.off[7]);
-  ws.ksum_part = reinterpret_cast<double*>(p + L.off[8]);
-  ws.vamax_part = reinterpret_cast<float*>(p + L.off[9]);
+  ws.vinv = reinterpret_cast<float*>(p + L.off[8]);
+  ws.ksum_part = reinterpret_cast<double*>(p + L.off[9]);
+  ws.vamax_part = reinterpret_cast<float*>(p + L.off[10]);
   ws.tq = L.tq; ws.tk = L.tk; ws.nch = L.nch;
   return ws;
 }
@@ -727,7 +745,7 @@ static int validate(const Args& a, bool need_out) {
   }
   const bool varlen = a.cu_q != nullptr;
   const Layout L = make_layout(a.batch, a.Hq, a.Hkv, a.total_q, a.total_k, a.max_q, a.max_k, varlen);
-  if (a.ws_bytes < L.off[10] || !aligned16(a.workspace) || (reinterpret_cast<uintptr_t>(a.workspace) & 1023))
+  if (a.ws_bytes < L.off[11] || !aligned16(a.workspace) || (reinterpret_cast<uintptr_t>(a.workspace) & 1023))
     return QF2_ERR_WORKSPACE;
   return QF2_OK;
 }
@@ -814,7 +832,7 @@ extern "C" int64_t qf2_sage_workspace_bytes(int64_t batch, int64_t Hq, int64_t H
   // dense callers pass total = batch * S; the varlen capacity bound covers both forms
   const Layout L = make_layout(batch, Hq, Hkv, total_q, total_k, max_seqlen_q, max_seqlen_k, true);
   const Layout Ld = make_layout(batch, Hq, Hkv, total_q, total_k, max_seqlen_q, max_seqlen_k, false);
-  return std::max(L.off[10], Ld.off[10]);
+  return std::max(L.off[11], Ld.off[11]);
 }
 
 extern "C" int qf2_sage_workspace_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
@@ -824,7 +842,7 @@ extern "C" int qf2_sage_workspace_layout(int64_t batch, int64_t Hq, int64_t Hkv,
   // total_q < 0 selects the dense layout (batch * ceil(S / 128) tiles per head)
   const bool varlen = total_q >= 0;
   const Layout L = make_layout(batch, Hq, Hkv, total_q, total_k, max_seqlen_q, max_seqlen_k, varlen);
-  for (int i = 0; i < 11; ++i) offsets[i] = L.off[i];
+  for (int i = 0; i < 12; ++i) offsets[i] = L.off[i];
   return QF2_OK;
 }
 

@@ -42,14 +42,14 @@ def test_argument_validation_without_device():
 
 def test_sage_workspace_layout_is_consistent():
     lib = _lib.load()
-    offs = _lib.i64(*([0] * 11))
+    offs = _lib.i64(*([0] * 12))
     B, H, S = 2, 24, 4608
     assert lib.qf2_sage_workspace_layout(B, H, H, -1, -1, S, S, 128, offs) == 0
     o = list(offs)
     assert o == sorted(o) and all(x % 1024 == 0 for x in o)
     tiles = B * ((S + 127) // 128)
     assert o[2] - o[1] == H * tiles * 16384          # q codes
-    assert lib.qf2_sage_workspace_bytes(B, H, H, B * S, B * S, S, S, 128) >= o[10]
+    assert lib.qf2_sage_workspace_bytes(B, H, H, B * S, B * S, S, S, 128) >= o[11]
 
 
 def test_device_check_reports_missing_device():

@@ -91,7 +91,7 @@ def test_sage_oracle_close_to_sdpa():
 def test_sage_quant_rules():
     """Hand-checkable cases of the stated quantization rules."""
     x = np.zeros((64, 128), np.float32)
-    x[0, 0], x[1, 1], x[2, 2] = 127.0, 63.5, -0.5   # scale 1.0: ties go to even
+    x[0, 0], x[1, 1], x[2, 2] = 127.0, 63.5, -0.5   # scale 1.0, inverse 1.0: ties go to even
     codes, scales = sage._block_quant(x)
     assert scales[0] == np.float32(1.0)
     assert codes[0, 0] == 127 and codes[1, 1] == 64 and codes[2, 2] == 0
