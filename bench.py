@@ -36,8 +36,8 @@ sys.path.insert(0, str(ROOT))
 B, H, S, D = 2, 24, 4608, 128
 WORKLOAD = f"sage attention, B={B} H={H} S={S} (4096 img + 512 txt) D={D}, bf16 io, INT8 QK^T / FP8 PV"
 METRIC = "attention TFLOPS (Flux-shaped 4608 tok, Sage INT8 QK / FP8 PV)"
-# dram bytes (read + write) of one sage_attn_kernel launch at this workload, from the ncu
-# capture summarised in profiles/sage_attn_kernel_B2_H24_S4608.md (None until captured)
+# dram bytes (read + write) of one sage_attn_kernel launch at this workload, from the
+# ncu capture summarised under profiles/ (None until captured)
 NCU_ATTN_TRAFFIC_BYTES = None
 
 

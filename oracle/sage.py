@@ -4,7 +4,7 @@ The reference reaches this path through the third-party `sageattention` package:
     sageattn(q, k, v)                       src/models/flux/attn.py:39-41 (HND layout)
     sageattn_varlen(q, k, v, cu_seqlens...) src/models/common/attn.py:109-120
 That package is not vendored, its version is not pinned anywhere in the reference
-(SURVEY: absent), and no test or golden vector of the reference touches it, so
+tree (and it is not installed here), and no test or golden vector of the reference touches it, so
 parity of the quantization codes is UNPINNED against the package itself.  This module
 restates the published SageAttention / SageAttention2 algorithm (Zhang et al.,
 "SageAttention", ICLR 2025; "SageAttention2", 2025) with every rounding step stated
