@@ -152,6 +152,26 @@ int qf2_sage_attn_quantized(void* out, const int64_t* out_strides, const int32_t
                             int64_t total_k, int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t Hq, int64_t Hkv,
                             int64_t D, int dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
 
+/* No counterpart in the reference.  qf2_sageattn without a caller workspace, for
+ * callers that cannot allocate device memory: programs that reserve all device memory
+ * in their own pool, code that must avoid the device synchronization an allocation
+ * can cause, and bindings that only hold the tensors they pass.  The quantized codes
+ * and scales live in one static device array of QF2_SAGE_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading the library keeps until the process exits.  Dense form only,
+ * same arguments and results as qf2_sageattn; a problem whose workspace
+ * (qf2_sage_workspace_bytes) exceeds the array less 1 KiB is rejected with
+ * QF2_ERR_WORKSPACE before anything runs (48 MiB holds one 4608-token, 24-head,
+ * head_dim 128 sequence).  The first call on a device looks the array's address up
+ * for that device (it must be the current device); make that first call before any
+ * stream capture.  All calls share the array and leave their contents in it; the
+ * status word is cleared at the start of each call.  Calls that overlap on the GPU
+ * (different streams, or host threads) race on the array: serialize them. */
+#define QF2_SAGE_NOALLOC_SCRATCH_BYTES (48ll << 20)
+int qf2_sageattn_noalloc(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                         const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides, int64_t B,
+                         int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, float sm_scale, int dtype,
+                         qf2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 namespace qf2 {
 namespace sage {
@@ -924,4 +925,54 @@ extern "C" int qf2_sage_attn_quantized(void* out, const int64_t* out_strides, co
   a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.sm_scale = 1.0f; a.dtype = dtype;
   a.workspace = workspace; a.ws_bytes = workspace_bytes; a.stream = reinterpret_cast<cudaStream_t>(stream);
   return run_attn_only(a);
+}
+
+// --------------------------------------------- static-scratch entry point --
+// Some callers cannot call cudaMalloc at all: programs that reserve every byte of
+// device memory in their own pool at start-up, code that must not take the implicit
+// device synchronization an allocation can cause, and thin foreign-language bindings
+// that only hold the tensors they pass in.  qf2_sageattn_noalloc serves them by
+// keeping the quantized codes and scales in the file-scope array below instead of a
+// caller workspace.  Every GPU that loads this library holds the array until the
+// process exits.
+namespace {
+constexpr int64_t kNoAllocScratchBytes = QF2_SAGE_NOALLOC_SCRATCH_BYTES;
+__device__ __align__(256) uint8_t g_sage_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+constexpr int kMaxDevices = 64;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// The array's name is only a host-side stand-in; the device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QF2_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_sage_noalloc_scratch) != cudaSuccess || p == nullptr) return QF2_ERR_LAUNCH;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return QF2_OK;
+}
+}  // namespace
+
+extern "C" int qf2_sageattn_noalloc(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                    const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides,
+                                    int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
+                                    float sm_scale, int dtype, qf2_stream_t stream) {
+  if (D != kHeadDim) return QF2_ERR_SHAPE;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq < 0 || Skv < 0) return QF2_ERR_SHAPE;
+  // the workspace starts at the first 1024-byte boundary inside the array
+  const int64_t usable = kNoAllocScratchBytes - 1024;
+  const Layout L = make_layout(B, Hq, Hkv, B * Sq, B * Skv, Sq, Skv, false);
+  if (L.off[11] > usable) return QF2_ERR_WORKSPACE;
+  void* base = nullptr;
+  const int st = noalloc_scratch(&base);
+  if (st != QF2_OK) return st;
+  const uintptr_t a = (reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023);
+  return qf2_sageattn(q, q_strides, k, k_strides, v, v_strides, out, out_strides, B, Hq, Hkv, Sq, Skv, D, sm_scale,
+                      dtype, reinterpret_cast<void*>(a), usable, stream);
 }

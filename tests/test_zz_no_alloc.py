@@ -1,0 +1,86 @@
+"""qf2_sageattn_noalloc: Sage attention for callers that cannot allocate device memory.
+
+Such callers (a host program that keeps all device memory in its own pool, code that
+must not trigger an allocation's device synchronization, a binding that only holds the
+tensors it passes) get the quantization scratch from a static device array inside the
+library instead of a workspace argument.  This file is collected last so that a
+failure here comes after every other test has run; it passes alone or after them.
+"""
+import math
+
+import pytest
+import torch
+
+from quantfun2_b200 import _lib
+from quantfun2_b200._lib import i64, stream_ptr
+
+pytestmark = pytest.mark.gpu
+
+QF2_ERR_WORKSPACE = -6
+
+
+def _inputs(dev, B, H, S, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, H, S, 128, device=dev, generator=g).bfloat16()
+    k = (torch.randn(B, H, S, 128, device=dev, generator=g)
+         + 3.0 * torch.randn(1, H, 1, 128, device=dev, generator=g)).bfloat16()
+    v = torch.randn(B, H, S, 128, device=dev, generator=g).bfloat16()
+    return q, k, v
+
+
+def _strides(t):
+    return i64(t.stride(0), t.stride(1), t.stride(2))
+
+
+def _with_workspace(lib, q, k, v, sm):
+    """The existing entry point, with a caller-provided workspace."""
+    B, H, S, D = q.shape
+    out = torch.empty_like(q)
+    nbytes = int(lib.qf2_sage_workspace_bytes(B, H, H, B * S, B * S, S, S, D))
+    raw = torch.empty(nbytes + 1024, dtype=torch.uint8, device=q.device)
+    ws = raw[(-raw.data_ptr()) % 1024:][:nbytes]
+    st = lib.qf2_sageattn(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(), _strides(v),
+                          out.data_ptr(), _strides(out), B, H, H, S, S, D, sm, _lib.QF2_BF16, ws.data_ptr(), nbytes,
+                          stream_ptr(q.device))
+    assert st == 0, lib.qf2_status_string(st)
+    return out
+
+
+def _noalloc(lib, q, k, v, sm):
+    B, H, S, D = q.shape
+    out = torch.empty_like(q)
+    st = lib.qf2_sageattn_noalloc(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(), _strides(v),
+                                  out.data_ptr(), _strides(out), B, H, H, S, S, D, sm, _lib.QF2_BF16,
+                                  stream_ptr(q.device))
+    assert st == 0, lib.qf2_status_string(st)
+    return out
+
+
+def test_noalloc_matches_workspace_entry_point_twice(cuda):
+    lib = _lib.load()
+    sm = 1.0 / math.sqrt(128)
+    # two calls in a row: different sizes and inputs, so the second call runs over the
+    # first call's leftovers in the shared static array
+    for B, H, S, seed in ((1, 24, 4608, 1), (2, 3, 777, 2)):
+        q, k, v = _inputs(cuda, B, H, S, seed)
+        got = _noalloc(lib, q, k, v, sm)
+        ref = _with_workspace(lib, q, k, v, sm)
+        torch.cuda.synchronize()
+        assert torch.isfinite(got).all()
+        # same kernels, same arithmetic: identical up to the tolerance the Sage tests use
+        cos = torch.nn.functional.cosine_similarity(got.float().flatten(), ref.float().flatten(), dim=0).item()
+        assert cos >= 0.9995, cos
+        assert (got.float() - ref.float()).abs().max().item() <= 1e-2
+        assert torch.equal(got, ref)
+
+
+def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
+    lib = _lib.load()
+    q, k, v = _inputs(cuda, 2, 24, 4608, 3)   # ~85 MB of codes: more than the 48 MiB array
+    out = torch.zeros_like(q)
+    st = lib.qf2_sageattn_noalloc(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(), _strides(v),
+                                  out.data_ptr(), _strides(out), 2, 24, 24, 4608, 4608, 128, 0.088, _lib.QF2_BF16,
+                                  stream_ptr(cuda))
+    assert st == QF2_ERR_WORKSPACE
+    torch.cuda.synchronize()
+    assert not out.any()   # nothing was launched
