@@ -51,6 +51,9 @@ enum qf2_dtype {
 /* ---------------------------------------------------------------- misc -- */
 const char* qf2_version(void);
 const char* qf2_status_string(int status);
+/* Text of the CUDA error behind the last QF2_ERR_LAUNCH returned on this host thread
+ * (empty if none). */
+const char* qf2_last_error(void);
 /* 0 when the current CUDA device is compute capability 10.0, else QF2_ERR_DEVICE. */
 int qf2_device_check(void);
 /* Synchronizes `stream`, then returns QF2_ERR_TIMEOUT if the status word at

@@ -25,6 +25,7 @@ _P32 = POINTER(ctypes.c_int32)
 SIGNATURES = {
     "qf2_version": (ctypes.c_char_p, []),
     "qf2_status_string": (ctypes.c_char_p, [c_int]),
+    "qf2_last_error": (ctypes.c_char_p, []),
     "qf2_device_check": (c_int, []),
     "qf2_workspace_status": (c_int, [c_void_p, c_void_p]),
     "qf2_rope_apply": (
@@ -96,7 +97,10 @@ def load() -> ctypes.CDLL:
 
 def check(status: int, what: str) -> None:
     if status != QF2_OK:
-        msg = load().qf2_status_string(status).decode()
+        lib = load()
+        msg = lib.qf2_status_string(status).decode()
+        if status == -3:
+            msg += ": " + lib.qf2_last_error().decode()
         raise QF2Error(f"{what} failed: {msg} ({status})")
 
 

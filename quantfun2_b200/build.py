@@ -37,9 +37,9 @@ def _headers_mtime() -> float:
     return max((h.stat().st_mtime for h in hs), default=0.0)
 
 
-def _compile(src: Path, verbose: bool, extra: list[str]) -> Path:
+def _compile(src: Path, verbose: bool, extra: list[str], force: bool) -> Path:
     obj = BUILD / (src.stem + ".o")
-    if obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, _headers_mtime()) and not extra:
+    if not force and obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, _headers_mtime()):
         return obj
     cmd = [NVCC, *CFLAGS, *extra, "-c", str(src), "-o", str(obj)]
     if verbose:
@@ -53,13 +53,20 @@ def _compile(src: Path, verbose: bool, extra: list[str]) -> Path:
 
 
 def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
+    """Compile and link.  Extra nvcc flags (e.g. -D tuning macros) may be passed in the
+    QF2_NVCC_FLAGS environment variable; they force a full rebuild."""
     BUILD.mkdir(exist_ok=True)
     srcs = sorted(CSRC.glob("*.cu"))
-    extra = ["-Xptxas", "-v"] if ptxas_info else []
+    flags = os.environ.get("QF2_NVCC_FLAGS", "").split()
+    extra = (["-Xptxas", "-v"] if ptxas_info else []) + flags
+    stamp = BUILD / "flags.txt"
+    changed = not stamp.exists() or stamp.read_text() != " ".join(flags)
+    force = changed or ptxas_info
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose or ptxas_info, extra), srcs))
+        objs = list(ex.map(lambda s: _compile(s, verbose or ptxas_info, extra, force), srcs))
+    stamp.write_text(" ".join(flags))
     newest = max(o.stat().st_mtime for o in objs)
-    if not LIB.exists() or LIB.stat().st_mtime < newest or extra:
+    if not LIB.exists() or LIB.stat().st_mtime < newest or force:
         cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
         if verbose:
             print(" ".join(cmd), flush=True)

@@ -2,6 +2,16 @@
 // workspace status word read-back used after bounded device waits.
 #include "qf2_common.cuh"
 
+#include <cstdio>
+
+static thread_local char g_last_error[256] = "";
+
+void qf2_record_cuda_error(cudaError_t e, const char* where) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s (%s) at %s", cudaGetErrorName(e), cudaGetErrorString(e), where);
+}
+
+extern "C" const char* qf2_last_error(void) { return g_last_error; }
+
 extern "C" const char* qf2_version(void) { return "quantfun2-b200 0.1.0 (sm_100a)"; }
 
 extern "C" const char* qf2_status_string(int status) {

@@ -294,9 +294,26 @@ QF2_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
 }  // namespace qf2
 
+// Records the CUDA error behind a QF2_ERR_LAUNCH for qf2_last_error().
+void qf2_record_cuda_error(cudaError_t e, const char* where);
+
 // Host-side launch check shared by every entry point.
-#define QF2_LAUNCH_CHECK()                            \
-  do {                                                \
-    cudaError_t _e = cudaGetLastError();              \
-    if (_e != cudaSuccess) return QF2_ERR_LAUNCH;     \
+#define QF2_LAUNCH_CHECK()                                          \
+  do {                                                              \
+    cudaError_t _e = cudaGetLastError();                            \
+    if (_e != cudaSuccess) {                                        \
+      qf2_record_cuda_error(_e, __FILE__ ":" QF2_STR(__LINE__));    \
+      return QF2_ERR_LAUNCH;                                        \
+    }                                                               \
+  } while (0)
+#define QF2_STR2(x) #x
+#define QF2_STR(x) QF2_STR2(x)
+// Same, for a runtime call that returns cudaError_t.
+#define QF2_CUDA_CHECK(call)                                        \
+  do {                                                              \
+    cudaError_t _e = (call);                                        \
+    if (_e != cudaSuccess) {                                        \
+      qf2_record_cuda_error(_e, __FILE__ ":" QF2_STR(__LINE__));    \
+      return QF2_ERR_LAUNCH;                                        \
+    }                                                               \
   } while (0)

@@ -794,9 +794,8 @@ static int launch_attn(const Args& a) {
   P.out_bf16 = a.dtype == QF2_BF16;
   const int64_t mqt = (a.max_q + kTile - 1) / kTile;
   if (mqt == 0) return QF2_OK;
-  if (cudaFuncSetAttribute(sage_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::alloc) !=
-      cudaSuccess)
-    return QF2_ERR_LAUNCH;
+  QF2_CUDA_CHECK(
+      cudaFuncSetAttribute(sage_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::alloc));
   sage_attn_kernel<<<dim3((unsigned)((mqt + 1) / 2), (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads,
                      AttnSmem::alloc, a.stream>>>(P);
   QF2_LAUNCH_CHECK();
@@ -813,7 +812,7 @@ static int run(const Args& a, bool quant_only) {
   int st = validate(a, !quant_only);
   if (st != QF2_OK) return st;
   // the status word starts every call at zero (stream-ordered, no allocation)
-  if (cudaMemsetAsync(a.workspace, 0, sizeof(int), a.stream) != cudaSuccess) return QF2_ERR_LAUNCH;
+  QF2_CUDA_CHECK(cudaMemsetAsync(a.workspace, 0, sizeof(int), a.stream));
   st = (a.dtype == QF2_BF16) ? launch_quant<__nv_bfloat16>(a) : launch_quant<__half>(a);
   if (st != QF2_OK || quant_only) return st;
   return launch_attn(a);
