@@ -31,7 +31,7 @@ constexpr int kHeadDim = 128;       // D
 constexpr int kTileBytes = 16384;   // 128 rows x 128 bytes of 8-bit codes
 constexpr int kQuantBlock = 64;     // tokens per INT8 scale block
 constexpr int kStatChunk = 512;     // tokens per stats partial
-constexpr int kStages = 3;          // K/V smem ring depth
+constexpr int kStages = 4;          // K/V smem ring depth
 constexpr int kMaxKvTiles = 512;    // k-scale smem capacity (65536 tokens)
 constexpr float kLog2_448 = 8.807354922057604f;
 
@@ -307,10 +307,10 @@ constexpr int kMagicBits = 0x4B400000;
 struct AttnSmem {
   static constexpr int q = 0;                                   // 2 Q tiles
   static constexpr int kv = q + 2 * kTileBytes;                 // stages x (K, V)
-  static constexpr int p = kv + kStages * 2 * kTileBytes;       // 2 tiles x 2 buffers
-  static constexpr int kscale = p + 4 * kTileBytes;             // up to kMaxKvTiles x 16 B
+  static constexpr int p = kv + kStages * 2 * kTileBytes;       // one P tile per Q tile
+  static constexpr int kscale = p + 2 * kTileBytes;             // up to kMaxKvTiles x 16 B
   static constexpr int bars = kscale + kMaxKvTiles * 16;
-  static constexpr int nbars = 1 + 2 * kStages + 2 * (1 + 1 + 2 + 2) + 1;
+  static constexpr int nbars = 1 + 2 * kStages + 2 * 4 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int total = misc + 64;
   static constexpr int alloc = total + 1024;  // slack for manual 1024-B alignment
@@ -409,9 +409,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   uint64_t* bar_kv_empty = bar_kv_full + kStages;
   uint64_t* bar_s_full = bar_kv_empty + kStages;  // [2] per Q tile
   uint64_t* bar_s_empty = bar_s_full + 2;          // [2]
-  uint64_t* bar_p_full = bar_s_empty + 2;          // [2 tiles][2 buffers]
-  uint64_t* bar_o_done = bar_p_full + 4;           // [2 tiles][PV index parity]
-  uint64_t* bar_drain = bar_o_done + 4;
+  uint64_t* bar_p_full = bar_s_empty + 2;          // [2 tiles]
+  uint64_t* bar_o_done = bar_p_full + 2;           // [2 tiles]: PV_t(i) completed
+  uint64_t* bar_drain = bar_o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + AttnSmem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + AttnSmem::misc + 8);
 
@@ -423,10 +423,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar_s_full + t, 1);
       mbar_init(bar_s_empty + t, 4);
-      for (int i = 0; i < 2; ++i) {
-        mbar_init(bar_p_full + 2 * t + i, 4);
-        mbar_init(bar_o_done + 2 * t + i, 1);
-      }
+      mbar_init(bar_p_full + t, 4);
+      mbar_init(bar_o_done + t, 1);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -447,71 +445,98 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
     *abort_flag = 1;
   };
 
+  // warp-uniform bounded wait: every lane agrees on the outcome, so .sync.aligned
+  // instructions and elected issue that follow always see a converged warp
+  auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    const bool w = mbar_wait(bar, parity) && (*abort_flag == 0);
+    return __all_sync(0xffffffffu, w);
+  };
+
   if (warp < 4) {
-    if (warp == 0 && lane == 0 && nkt > 0) {
+    if (warp == 0 && nkt > 0) {
       // ------------------------------------------------------- producer --
+      // the whole warp runs the loop (uniform addresses), lane 0 issues the copies
       const int64_t qslot = (int64_t)h * ws.tq + sq.tile0 + qt0;
       const int64_t kslot0 = (int64_t)hk * ws.tk + sk.tile0;
-      mbar_arrive_expect_tx(bar_q, ntile * kTileBytes + nkt * 16);
-      bulk_g2s(sQ, ws.qc + qslot * kTileBytes, ntile * kTileBytes, bar_q);
-      bulk_g2s(sKS, ws.ks + kslot0 * 4, nkt * 16, bar_q);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_q, ntile * kTileBytes + nkt * 16);
+        bulk_g2s(sQ, ws.qc + qslot * kTileBytes, ntile * kTileBytes, bar_q);
+        bulk_g2s(sKS, ws.ks + kslot0 * 4, nkt * 16, bar_q);
+      }
       int issued = 0;
       for (int j = 0; j < nkt; ++j) {
         const int s = j % kStages, r = j / kStages;
-        if (!mbar_wait(bar_kv_empty + s, (r & 1) ^ 1) || *abort_flag) { fail(kDevTimeoutProducer); break; }
-        mbar_arrive_expect_tx(bar_kv_full + s, 2 * kTileBytes);
-        uint8_t* dK = sKV + s * 2 * kTileBytes;
-        bulk_g2s(dK, ws.kc + (kslot0 + j) * kTileBytes, kTileBytes, bar_kv_full + s);
-        bulk_g2s(dK + kTileBytes, ws.vc + (kslot0 + j) * kTileBytes, kTileBytes, bar_kv_full + s);
+        if (!wwait(bar_kv_empty + s, (r & 1) ^ 1)) { if (lane == 0) fail(kDevTimeoutProducer); break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar_kv_full + s, 2 * kTileBytes);
+          uint8_t* dK = sKV + s * 2 * kTileBytes;
+          bulk_g2s(dK, ws.kc + (kslot0 + j) * kTileBytes, kTileBytes, bar_kv_full + s);
+          bulk_g2s(dK + kTileBytes, ws.vc + (kslot0 + j) * kTileBytes, kTileBytes, bar_kv_full + s);
+        }
+        __syncwarp();
         issued = j + 1;
       }
-      if (*abort_flag) {
+      if (*abort_flag && lane == 0) {
         // let the copies already issued land before the CTA's shared memory goes away
         mbar_wait(bar_q, 0);
         for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
           mbar_wait(bar_kv_full + (j % kStages), (j / kStages) & 1);
       }
-    } else if (warp == 1 && lane == 0 && nkt > 0) {
+    } else if (warp == 1 && nkt > 0) {
       // ------------------------------------------------------------ MMA --
+      // converged warp: descriptors are warp-uniform, lane 0 issues and commits
       constexpr uint32_t idesc_qk = make_idesc(2, 1, 1, 0, 0, kTile, kTile);     // s8 x s8 -> s32
       constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 0, 0, kTile, kHeadDim);  // e4m3 x e4m3 -> f32
-      bool ok = mbar_wait(bar_q, 0);
+      bool ok = wwait(bar_q, 0);
+      // Descriptors are built once; per stage / k-step only the 14-bit start-address
+      // field moves (16-byte units: a stage is 2048, a 32-byte k-step is 2).
+      const uint64_t dQ0 = sdesc_sw128_kmajor(smem_u32(sQ));
+      const uint64_t dP0 = sdesc_sw128_kmajor(smem_u32(sP));
+      const uint64_t dK0 = sdesc_sw128_kmajor(smem_u32(sKV));
+      constexpr uint64_t kTileStep = kTileBytes >> 4, kStageStep = 2 * kTileBytes >> 4;
       auto issue_pv = [&](int i) -> bool {
-        const uint32_t aV = smem_u32(sKV + (i % kStages) * 2 * kTileBytes + kTileBytes);
+        const uint64_t dV = dK0 + (uint64_t)(i % kStages) * kStageStep + kTileStep;
         for (int t = 0; t < ntile; ++t) {
-          if (!mbar_wait(bar_p_full + 2 * t + (i & 1), (i >> 1) & 1) || *abort_flag) return false;
+          if (!wwait(bar_p_full + t, i & 1)) return false;
           tc_fence_after();
-          const uint32_t aP = smem_u32(sP + (2 * t + (i & 1)) * kTileBytes);
+          const uint64_t dP = dP0 + (uint64_t)t * kTileStep;
+          if (lane == 0) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f8f6f4(tmem + 256 + t * 128, sdesc_sw128_kmajor(aP + kk * 32), sdesc_sw128_kmajor(aV + kk * 32),
-                       idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(bar_o_done + 2 * t + (i & 1));
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f8f6f4(tmem + 256 + t * 128, dP + 2 * kk, dV + 2 * kk, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(bar_o_done + t);
+          }
+          __syncwarp();
         }
-        tc_commit(bar_kv_empty + (i % kStages));
+        if (lane == 0) tc_commit(bar_kv_empty + (i % kStages));
+        __syncwarp();
         return true;
       };
       for (int j = 0; ok && j < nkt; ++j) {
         const int s = j % kStages;
-        if (!mbar_wait(bar_kv_full + s, (j / kStages) & 1) || *abort_flag) { ok = false; break; }
-        const uint32_t aK = smem_u32(sKV + s * 2 * kTileBytes);
+        if (!wwait(bar_kv_full + s, (j / kStages) & 1)) { ok = false; break; }
+        const uint64_t dK = dK0 + (uint64_t)s * kStageStep;
         for (int t = 0; t < ntile && ok; ++t) {
-          if (j > 0 && (!mbar_wait(bar_s_empty + t, (j - 1) & 1) || *abort_flag)) { ok = false; break; }
+          if (j > 0 && !wwait(bar_s_empty + t, (j - 1) & 1)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t aQ = smem_u32(sQ + t * kTileBytes);
+          const uint64_t dQ = dQ0 + (uint64_t)t * kTileStep;
+          if (lane == 0) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_i8(tmem + t * 128, sdesc_sw128_kmajor(aQ + kk * 32), sdesc_sw128_kmajor(aK + kk * 32), idesc_qk,
-                   kk > 0 ? 1u : 0u);
-          tc_commit(bar_s_full + t);
+            for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + t * 128, dQ + 2 * kk, dK + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+            tc_commit(bar_s_full + t);
+          }
+          __syncwarp();
         }
         if (ok && j > 0 && !issue_pv(j - 1)) ok = false;
       }
       if (ok) ok = issue_pv(nkt - 1);
-      if (!ok) fail(kDevTimeoutMma);
-      // drain: wait until every MMA issued above has completed
-      tc_commit(bar_drain);
-      mbar_wait(bar_drain, 0);
+      if (lane == 0) {
+        if (!ok) fail(kDevTimeoutMma);
+        // drain: wait until every MMA issued above has completed
+        tc_commit(bar_drain);
+        mbar_wait(bar_drain, 0);
+      }
+      __syncwarp();
     }
   } else {
     // -------------------------------------------------------- softmax --
@@ -524,12 +549,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
     const bool active = t < ntile;
     const int qt = qt0 + t;
     const float* vsc = ws.vs + ((int64_t)b * P.Hkv + hk) * kHeadDim;
-    // warp-uniform bounded wait: every lane agrees on the outcome, so the
-    // .sync.aligned tcgen05 ops that follow always see a converged warp
-    auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
-      const bool w = mbar_wait(bar, parity) && (*abort_flag == 0);
-      return __all_sync(0xffffffffu, w);
-    };
     bool ok = active && nkt > 0;
     float sqs = 0.f;
     if (ok) {
@@ -560,13 +579,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         for (int i = 0; i < 128; ++i)
           if (i >= rem) mf[i] = 0.0f;
       }
-      float mx0 = mf[0], mx1 = mf[64];
+      // row max per 64-column half (one K scale each): 4 independent fmax3 chains
+      float mq[8];
 #pragma unroll
-      for (int i = 1; i < 63; i += 2) mx0 = fmax3(mx0, mf[i], mf[i + 1]);
-      mx0 = fmaxf(mx0, mf[63]);
+      for (int c = 0; c < 8; ++c) {
+        float m = fmax3(mf[c * 16], mf[c * 16 + 1], mf[c * 16 + 2]);
 #pragma unroll
-      for (int i = 65; i < 127; i += 2) mx1 = fmax3(mx1, mf[i], mf[i + 1]);
-      mx1 = fmaxf(mx1, mf[127]);
+        for (int i = 3; i < 15; i += 2) m = fmax3(m, mf[c * 16 + i], mf[c * 16 + i + 1]);
+        mq[c] = fmaxf(m, mf[c * 16 + 15]);
+      }
+      const float mx0 = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      const float mx1 = fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]));
       const float4 ksc = sKS[j];
       const float sc0 = sqs * ksc.x, sc1 = sqs * ksc.y;
       const float m_tile = fmaxf((mx0 - kMagic) * sc0, (mx1 - kMagic) * sc1);
@@ -582,9 +605,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       const float bias = m_run - kPScaleLog2;
       const float2 nb = make_float2(-bias, -bias), nmag = make_float2(-kMagic, -kMagic);
       const float2 sc0v = make_float2(sc0, sc0), sc1v = make_float2(sc1, sc1);
-      // the P buffer (j & 1) was last read by PV(j-2)
-      if (j >= 2 && !wwait(bar_o_done + 2 * t + (j & 1), ((j - 2) >> 1) & 1)) { ok = false; break; }
-      uint8_t* pdst = sP + (2 * t + (j & 1)) * kTileBytes;
+      // P_t was last read by PV_t(j-1); its completion also orders the O rescale below
+      if (j >= 1 && !wwait(bar_o_done + t, (j - 1) & 1)) { ok = false; break; }
+      uint8_t* pdst = sP + t * kTileBytes;
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int chunk = 0; chunk < 8; ++chunk) {
@@ -604,9 +627,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       }
       l_run += acc.x + acc.y;
       if (rescale && j > 0) {
-        // O holds sum_{i<j} P_i V_i against the old max: PV(j-1) must have finished
-        // before the rescale, and PV(j) is only issued after p_full(j) below
-        if (!wwait(bar_o_done + 2 * t + ((j - 1) & 1), ((j - 1) >> 1) & 1)) { ok = false; break; }
+        // O holds sum_{i<j} P_i V_i against the old max (PV(j-1) completed above);
+        // PV(j) is only issued after p_full(j) below
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -622,14 +644,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p_full + 2 * t + (j & 1));
+      if (lane == 0) mbar_arrive(bar_p_full + t);
     }
     if (active && nkt > 0 && !ok) fail(kDevTimeoutSoftmax);
     // ------------------------------------------------------- epilogue --
     if (active) {
       const int64_t r_tok = (int64_t)qt * kTile + row;
       if (ok && nkt > 0) {
-        if (!wwait(bar_o_done + 2 * t + ((nkt - 1) & 1), ((nkt - 1) >> 1) & 1)) {
+        if (!wwait(bar_o_done + t, (nkt - 1) & 1)) {
           fail(kDevTimeoutEpilogue);
           ok = false;
         }
