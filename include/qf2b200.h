@@ -155,6 +155,28 @@ int qf2_sage_attn_quantized(void* out, const int64_t* out_strides, const int32_t
                             int64_t total_k, int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t Hq, int64_t Hkv,
                             int64_t D, int dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
 
+/* ------------------------------------------ top-k block-sparse attention --
+ * Replaces topk_attn (src/kernels/__init__.py:146-195) and its mask cache POS_DICT
+ * (src/models/common/attn.py:20, :24-56), in block form with 128-token blocks:
+ *   qf2_blocktopk_select: mean-pool Q and K per block (fp64 sums, fp32 means), block
+ *     scores pooled_q . pooled_k^T (fp64, d ascending, rounded to fp32), keep the top
+ *     `keep` key blocks per query block (lower index wins ties) and write them in
+ *     ascending order to idx_out [B, Hq, ceil(S/128), keep] (int32).  The caller may
+ *     cache idx across layers as the reference caches POS_DICT.
+ *   qf2_blocksparse_attn: exact softmax attention of every query block over its kept
+ *     key blocks (keys beyond S masked); bf16/fp16, D = 128, tcgen05 kind::f16.
+ * q/k/v/out strides = {batch, head, seq} in elements, multiples of 8.  The select
+ * workspace holds the pooled blocks (qf2_blocktopk_workspace_bytes); the attention
+ * workspace holds only the status word (256 bytes). */
+int64_t qf2_blocktopk_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t D);
+int qf2_blocktopk_select(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, int64_t B,
+                         int64_t Hq, int64_t Hkv, int64_t S, int64_t D, int64_t keep, int dtype, int32_t* idx_out,
+                         void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
+int qf2_blocksparse_attn(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                         const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides, int64_t B,
+                         int64_t Hq, int64_t Hkv, int64_t S, int64_t D, const int32_t* idx, int64_t keep,
+                         float sm_scale, int dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
+
 /* No counterpart in the reference.  qf2_sageattn without a caller workspace, for
  * callers that cannot allocate device memory: programs that reserve all device memory
  * in their own pool, code that must avoid the device synchronization an allocation

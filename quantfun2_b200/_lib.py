@@ -63,6 +63,17 @@ SIGNATURES = {
         [c_void_p, _P64, _P32, _P32, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
          c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p],
     ),
+    "qf2_blocktopk_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int64, c_int64]),
+    "qf2_blocktopk_select": (
+        c_int,
+        [c_void_p, _P64, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p,
+         c_void_p, c_int64, c_void_p],
+    ),
+    "qf2_blocksparse_attn": (
+        c_int,
+        [c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64,
+         c_int64, c_void_p, c_int64, c_float, c_int, c_void_p, c_int64, c_void_p],
+    ),
     "qf2_sageattn_noalloc": (
         c_int,
         [c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64,

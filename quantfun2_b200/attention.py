@@ -22,7 +22,8 @@ import torch
 from . import _lib
 from ._lib import QF2Error, check, i64, ptr32, require_device, stream_ptr
 
-__all__ = ["sageattn", "sageattn_varlen", "sage_quantize", "sage_workspace_layout"]
+__all__ = ["sageattn", "sageattn_varlen", "sage_quantize", "sage_workspace_layout", "block_topk_select",
+           "blocksparse_attn"]
 
 
 def _dt(t: torch.Tensor) -> int:
@@ -167,3 +168,67 @@ def sage_quantize(q, k, v, sm_scale=None, tensor_layout="HND", cu_seqlens_q=None
                                 Hq, Hkv, D, float(sm_scale), _dt(q), ws.data_ptr(), ws.numel(),
                                 stream_ptr(q.device)), "qf2_sage_quantize")
     return ws, sage_workspace_layout(batch, Hq, Hkv, int(max_seqlen_q), int(max_seqlen_k), D, (Tq, Tk))
+
+
+# ------------------------------------------------------ top-k block sparse --
+BLOCK = 128
+
+
+def _hnd(t: torch.Tensor, layout: str):
+    """(B, H, S, D) view and {batch, head, seq} strides of a q/k/v tensor."""
+    if layout == "HND":
+        return t.shape[0], t.shape[1], t.shape[2], t.shape[3], (t.stride(0), t.stride(1), t.stride(2))
+    if layout == "NHD":
+        return t.shape[0], t.shape[2], t.shape[1], t.shape[3], (t.stride(0), t.stride(2), t.stride(1))
+    raise QF2Error(f"unknown tensor_layout {layout}")
+
+
+def block_topk_select(q: torch.Tensor, k: torch.Tensor, keep: int, tensor_layout: str = "HND") -> torch.Tensor:
+    """Kept key blocks per 128-token query block: int32 [B, Hq, ceil(S/128), keep], ascending.
+    Block scores are mean-pooled Q . mean-pooled K^T (fp64, rounded to fp32); the lower block
+    index wins ties."""
+    require_device(q)
+    q, k = _fix(q), _fix(k)
+    B, Hq, S, D, qs = _hnd(q, tensor_layout)
+    _, Hkv, Sk, _, ks = _hnd(k, tensor_layout)
+    if Sk != S:
+        raise QF2Error("block top-k needs equal query and key lengths")
+    nb = (S + BLOCK - 1) // BLOCK
+    keep = min(int(keep), nb)
+    idx = torch.empty(B, Hq, nb, keep, dtype=torch.int32, device=q.device)
+    lib = _lib.load()
+    nbytes = int(lib.qf2_blocktopk_workspace_bytes(B, Hq, Hkv, S, D))
+    if nbytes < 0:
+        check(nbytes, "qf2_blocktopk_workspace_bytes")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    check(lib.qf2_blocktopk_select(q.data_ptr(), i64(*qs), k.data_ptr(), i64(*ks), B, Hq, Hkv, S, D, keep, _dt(q),
+                                   idx.data_ptr(), ws.data_ptr(), nbytes, stream_ptr(q.device)),
+          "qf2_blocktopk_select")
+    return idx
+
+
+def blocksparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, idx: torch.Tensor,
+                     sm_scale: float | None = None, tensor_layout: str = "HND") -> torch.Tensor:
+    """Exact softmax attention of each 128-row query block over its kept key blocks `idx`."""
+    require_device(q)
+    q, k, v = _fix(q), _fix(k), _fix(v)
+    B, Hq, S, D, qs = _hnd(q, tensor_layout)
+    _, Hkv, _, _, ks = _hnd(k, tensor_layout)
+    _, _, _, _, vs = _hnd(v, tensor_layout)
+    if v.shape != k.shape or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise QF2Error("k and v must have the same shape, and q/k/v the same dtype")
+    nb = (S + BLOCK - 1) // BLOCK
+    if idx.dim() != 4 or tuple(idx.shape[:3]) != (B, Hq, nb) or idx.dtype != torch.int32:
+        raise QF2Error(f"idx must be int32 [B, Hq, {nb}, keep]")
+    idx = idx.to(q.device).contiguous()
+    out = torch.empty_like(q)
+    _, _, _, _, os_ = _hnd(out, tensor_layout)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    ws = torch.empty(256, dtype=torch.uint8, device=q.device)
+    check(_lib.load().qf2_blocksparse_attn(q.data_ptr(), i64(*qs), k.data_ptr(), i64(*ks), v.data_ptr(), i64(*vs),
+                                           out.data_ptr(), i64(*os_), B, Hq, Hkv, S, D, idx.data_ptr(),
+                                           idx.shape[3], float(sm_scale), _dt(q), ws.data_ptr(), 256,
+                                           stream_ptr(q.device)),
+          "qf2_blocksparse_attn")
+    return out

@@ -1,0 +1,482 @@
+// Top-k block-sparse attention for B200 (sm_100a).
+//
+// Replaces the reference's sparse attention path, topk_attn
+// (src/kernels/__init__.py:146-195) with its mask cache POS_DICT
+// (src/models/common/attn.py:20, :24-56), in block form:
+//   1. blocktopk_pool_kernel    mean of Q and K over 128-token blocks (fp64 sums, fp32 means)
+//   2. blocktopk_select_kernel  block scores pooled_q . pooled_k^T (fp64, fixed order,
+//                               rounded to fp32) and the top `keep` key blocks per query
+//                               block (lower index wins ties), written ascending (int32)
+//   3. blocksparse_attn_kernel  exact softmax attention of each 128-row query block over
+//                               its kept key blocks: TMA tiles (bf16/fp16, 128-byte
+//                               swizzle) fetched by block index, tcgen05.mma kind::f16
+//                               QK^T into TMEM (double-buffered S), P through shared
+//                               memory, PV with V read as an MN-major operand, fp32 O in TMEM.
+#include "qf2_common.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace qf2 {
+namespace bsa {
+
+constexpr int kBlk = 128;       // tokens per block (MMA M and N)
+constexpr int kD = 128;         // head dim
+constexpr int kMaxBlocks = 1024;
+
+struct S3 { int64_t b, h, s; };
+
+// ------------------------------------------------------------------ pool --
+// grid (nb, Hq + Hkv, B), 128 threads (one per channel)
+template <typename T>
+__global__ void __launch_bounds__(128) blocktopk_pool_kernel(const T* __restrict__ q, S3 qs, const T* __restrict__ k,
+                                                             S3 ks, int64_t S, int Hq, int Hkv, float* __restrict__ pq,
+                                                             float* __restrict__ pk) {
+  const int blk = blockIdx.x, job = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+  const bool is_q = job < Hq;
+  const int h = is_q ? job : job - Hq;
+  const T* src = (is_q ? q : k) + (int64_t)b * (is_q ? qs.b : ks.b) + (int64_t)h * (is_q ? qs.h : ks.h) + d;
+  const int64_t ss = is_q ? qs.s : ks.s;
+  const int64_t r0 = (int64_t)blk * kBlk;
+  const int n = (int)min((int64_t)kBlk, S - r0);
+  double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int r = 0; r < n; ++r) acc[r & 7] += (double)to_f32(src[(r0 + r) * ss]);
+  // every partial sum is exact for 16-bit inputs, so the combination order is immaterial
+  const double sum = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+  const int nb = (int)((S + kBlk - 1) / kBlk);
+  float* dst = is_q ? pq + (((int64_t)b * Hq + h) * nb + blk) * kD : pk + (((int64_t)b * Hkv + h) * nb + blk) * kD;
+  dst[d] = (float)(sum / (double)n);
+}
+
+// ---------------------------------------------------------------- select --
+// grid (nqb, Hq, B), 128 threads
+__global__ void __launch_bounds__(128) blocktopk_select_kernel(const float* __restrict__ pq, const float* __restrict__ pk,
+                                                               int nb, int Hq, int Hkv, int keep, int32_t* __restrict__ idx) {
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int hk = h / (Hq / Hkv);
+  __shared__ double sq[kD];
+  __shared__ float sc[kMaxBlocks];
+  __shared__ unsigned char sel[kMaxBlocks];
+  sq[tid] = (double)pq[(((int64_t)b * Hq + h) * nb + qb) * kD + tid];
+  __syncthreads();
+  const float* kb = pk + ((int64_t)b * Hkv + hk) * nb * kD;
+  for (int j = tid; j < nb; j += blockDim.x) {
+    const float* row = kb + (int64_t)j * kD;
+    double acc = 0.0;
+    for (int d = 0; d < kD; ++d) acc = __dadd_rn(acc, __dmul_rn(sq[d], (double)row[d]));
+    sc[j] = (float)acc;
+  }
+  __syncthreads();
+  for (int j = tid; j < nb; j += blockDim.x) {
+    const float v = sc[j];
+    int rank = 0;
+    for (int i = 0; i < nb; ++i) {
+      const float u = sc[i];
+      rank += (u > v) || (u == v && i < j);
+    }
+    sel[j] = rank < keep;
+  }
+  __syncthreads();
+  int32_t* out = idx + (((int64_t)b * Hq + h) * nb + qb) * keep;
+  for (int j = tid; j < nb; j += blockDim.x) {
+    if (sel[j]) {
+      int pos = 0;
+      for (int i = 0; i < j; ++i) pos += sel[i];
+      out[pos] = j;
+    }
+  }
+}
+
+// ------------------------------------------------------------- attention --
+constexpr int kThreads = 192;   // warp 0 producer, warp 1 MMA, warps 2-5 softmax
+constexpr int kTile = 16384;    // 128 rows x 128 bytes (one 128-byte swizzle atom column)
+constexpr int kOpBytes = 2 * kTile;  // 128 x 128 16-bit elements
+constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
+
+struct Smem {
+  static constexpr int q = 0;
+  static constexpr int kv = q + kOpBytes;          // 2 stages x (K, V)
+  static constexpr int p = kv + 2 * 2 * kOpBytes;  // P tile (single buffer)
+  static constexpr int bars = p + kOpBytes;
+  static constexpr int nbars = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+  static constexpr int misc = bars + nbars * 8;
+  static constexpr int total = misc + 64;
+  static constexpr int alloc = total + 1024;
+};
+
+struct AttnArgs {
+  const int32_t* idx;
+  void* out;
+  S3 os;
+  int64_t S;
+  int Hq, Hkv, keep, nb;
+  float scale_log2;  // sm_scale * log2(e)
+  int f16;           // 1: fp16 operands, 0: bf16
+  int* status;
+};
+
+QF2_DEV uint32_t pack2(float a, float b, bool f16) {
+  if (f16) {
+    __half2 t = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&t);
+  }
+  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    blocksparse_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                            const __grid_constant__ CUtensorMap tmv, AttnArgs A) {
+  extern __shared__ uint8_t smem_raw[];
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (A.Hq / A.Hkv);
+  const int keep = A.keep;
+  const int32_t* idx = A.idx + (((int64_t)b * A.Hq + h) * A.nb + qb) * keep;
+
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = base + Smem::q;
+  uint8_t* sKV = base + Smem::kv;
+  uint8_t* sP = base + Smem::p;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Smem::bars);
+  uint64_t* bar_q = bars;
+  uint64_t* bar_kv_full = bars + 1;   // [2]
+  uint64_t* bar_kv_empty = bars + 3;  // [2]
+  uint64_t* bar_s_full = bars + 5;    // [2]
+  uint64_t* bar_s_empty = bars + 7;   // [2]
+  uint64_t* bar_p_full = bars + 9;
+  uint64_t* bar_o_done = bars + 10;
+  uint64_t* bar_drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + Smem::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + Smem::misc + 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_kv_full + s, 1);
+      mbar_init(bar_kv_empty + s, 1);
+      mbar_init(bar_s_full + s, 1);
+      mbar_init(bar_s_empty + s, 4);
+    }
+    mbar_init(bar_p_full, 4);
+    mbar_init(bar_o_done, 1);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) {
+    atomicExch(A.status, code);
+    *abort_flag = 1;
+  };
+  auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    const bool w = mbar_wait(bar, parity) && (*abort_flag == 0);
+    return __all_sync(0xffffffffu, w);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------- producer --
+    if (keep > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&tmq);
+        prefetch_tmap(&tmk);
+        prefetch_tmap(&tmv);
+        mbar_arrive_expect_tx(bar_q, kOpBytes);
+        tma_load_4d(sQ, &tmq, 0, qb * kBlk, h, b, bar_q);
+        tma_load_4d(sQ + kTile, &tmq, 64, qb * kBlk, h, b, bar_q);
+      }
+      int issued = 0;
+      for (int j = 0; j < keep; ++j) {
+        const int s = j & 1;
+        if (!wwait(bar_kv_empty + s, ((j >> 1) & 1) ^ 1)) { if (lane == 0) fail(kDevTimeoutProducer); break; }
+        if (lane == 0) {
+          const int kb = idx[j];
+          uint8_t* dK = sKV + s * 2 * kOpBytes;
+          uint8_t* dV = dK + kOpBytes;
+          mbar_arrive_expect_tx(bar_kv_full + s, 2 * kOpBytes);
+          tma_load_4d(dK, &tmk, 0, kb * kBlk, hk, b, bar_kv_full + s);
+          tma_load_4d(dK + kTile, &tmk, 64, kb * kBlk, hk, b, bar_kv_full + s);
+          tma_load_4d(dV, &tmv, 0, kb * kBlk, hk, b, bar_kv_full + s);
+          tma_load_4d(dV + kTile, &tmv, 64, kb * kBlk, hk, b, bar_kv_full + s);
+        }
+        __syncwarp();
+        issued = j + 1;
+      }
+      if (*abort_flag && lane == 0) {
+        mbar_wait(bar_q, 0);
+        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) mbar_wait(bar_kv_full + (j & 1), (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA --
+    if (keep > 0) {
+      const uint32_t ab = A.f16 ? 0u : 1u;
+      const uint32_t idesc_qk = make_idesc(1, ab, ab, 0, 0, kBlk, kBlk);   // K-major x K-major -> f32
+      const uint32_t idesc_pv = make_idesc(1, ab, ab, 0, 1, kBlk, kD);     // P K-major x V MN-major -> f32
+      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      bool ok = wwait(bar_q, 0);
+      auto issue_pv = [&](int i) -> bool {
+        if (!wwait(bar_p_full, i & 1)) return false;
+        tc_fence_after();
+        const uint32_t aV = smem_u32(sKV + (i & 1) * 2 * kOpBytes + kOpBytes);
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            // A: P rows, 16 keys per step (two 64-key swizzle atoms); B: V rows kk*16.. as
+            // MN-major (head-dim halves 16 KB apart, 8-row groups 1 KB apart)
+            const uint64_t da = sdesc_sw128_kmajor(aP + (kk >> 2) * kTile + (kk & 3) * 32);
+            const uint64_t db = sdesc_sw128_mnmajor(aV + kk * 16 * 128, kTile, 1024);
+            mma_f16(tmem + 256, da, db, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(bar_o_done);
+          tc_commit(bar_kv_empty + (i & 1));
+        }
+        __syncwarp();
+        return true;
+      };
+      for (int j = 0; ok && j < keep; ++j) {
+        const int s = j & 1;
+        if (!wwait(bar_kv_full + s, (j >> 1) & 1)) { ok = false; break; }
+        if (!wwait(bar_s_empty + s, ((j >> 1) & 1) ^ 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t aK = smem_u32(sKV + s * 2 * kOpBytes);
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * kTile + (kk & 3) * 32;
+            mma_f16(tmem + s * kBlk, sdesc_sw128_kmajor(aQ + off), sdesc_sw128_kmajor(aK + off), idesc_qk,
+                    kk > 0 ? 1u : 0u);
+          }
+          tc_commit(bar_s_full + s);
+        }
+        __syncwarp();
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) ok = issue_pv(keep - 1);
+      if (lane == 0) {
+        if (!ok) fail(kDevTimeoutMma);
+        tc_commit(bar_drain);
+        mbar_wait(bar_drain, 0);
+      }
+      __syncwarp();
+    }
+  } else {
+    // -------------------------------------------------------- softmax --
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const bool f16 = A.f16 != 0;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = keep > 0;
+    for (int j = 0; ok && j < keep; ++j) {
+      const int s = j & 1;
+      if (!wwait(bar_s_full + s, (j >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(tmem + lane_off + s * kBlk + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_s_empty + s);
+
+      const int64_t valid = A.S - (int64_t)idx[j] * kBlk;  // keys of this block inside the sequence
+      float x[128];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        float v = __uint_as_float(sr[i]) * A.scale_log2;
+        if (i >= valid) v = -INFINITY;
+        x[i] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a fully masked block contributes nothing
+      const float alpha = fast_exp2(m_run - m_use);
+      float rs = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = fast_exp2(x[2 * i] - m_use), p1 = fast_exp2(x[2 * i + 1] - m_use);
+        rs += p0 + p1;
+        pk[i] = pack2(p0, p1, f16);
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      if (j > 0) {
+        // PV(j-1) has read P and finished accumulating O before both are touched
+        if (!wwait(bar_o_done, (j - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_off + 256 + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tmem + lane_off + 256 + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row: 128 keys = two 64-key swizzle atoms of 8 x 16-byte chunks
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint8_t* dst = sP + (c >> 3) * kTile + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p_full);
+    }
+    if (keep > 0 && !ok) fail(kDevTimeoutSoftmax);
+    // ------------------------------------------------------- epilogue --
+    if (ok && keep > 0) {
+      if (!wwait(bar_o_done, (keep - 1) & 1)) { fail(kDevTimeoutEpilogue); ok = false; }
+      tc_fence_after();
+    }
+    const int64_t tok = (int64_t)qb * kBlk + row;
+    const float inv_l = (ok && l_run > 0.f) ? 1.0f / l_run : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      if (ok && keep > 0) {
+        tmem_ld32(tmem + lane_off + 256 + c * 32, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      if (tok < A.S) {
+        uint8_t* dst = reinterpret_cast<uint8_t*>(A.out) +
+                       2 * ((int64_t)b * A.os.b + (int64_t)h * A.os.h + tok * A.os.s + c * 32);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l, f16);
+          w.y = pack2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l, f16);
+          w.z = pack2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l, f16);
+          w.w = pack2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l, f16);
+          *reinterpret_cast<uint4*>(dst + v * 16) = w;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host --
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int check_common(const void* q, const int64_t* qs, const void* k, const int64_t* ks, int64_t B, int64_t Hq,
+                        int64_t Hkv, int64_t S, int64_t D, int dtype) {
+  if (!q || !k || !qs || !ks) return QF2_ERR_ARG;
+  if (dtype != QF2_BF16 && dtype != QF2_F16) return QF2_ERR_DTYPE;
+  if (D != kD || B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || S <= 0) return QF2_ERR_SHAPE;
+  if ((S + kBlk - 1) / kBlk > kMaxBlocks || B > 65535 || Hq + Hkv > 65535) return QF2_ERR_SHAPE;
+  if (!al16(q) || !al16(k)) return QF2_ERR_ALIGN;
+  for (int i = 0; i < 3; ++i)
+    if ((qs[i] % 8) || (ks[i] % 8)) return QF2_ERR_ALIGN;
+  return QF2_OK;
+}
+
+static bool make_map(CUtensorMap* m, const void* base, const int64_t* st, int64_t B, int64_t H, int64_t S, int dtype) {
+  const uint64_t dims[4] = {(uint64_t)kD, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  const uint32_t box[4] = {64, (uint32_t)kBlk, 1, 1};
+  return qf2_make_tmap_4d(m, dtype == QF2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          base, dims, strides, box);
+}
+
+}  // namespace bsa
+}  // namespace qf2
+
+using namespace qf2::bsa;
+
+extern "C" int64_t qf2_blocktopk_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t D) {
+  if (D != kD || B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0) return (int64_t)QF2_ERR_SHAPE;
+  const int64_t nb = (S + kBlk - 1) / kBlk;
+  return 256 + (B * Hq + B * Hkv) * nb * kD * 4;
+}
+
+extern "C" int qf2_blocktopk_select(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                    int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t D, int64_t keep, int dtype,
+                                    int32_t* idx_out, void* workspace, int64_t workspace_bytes, qf2_stream_t stream) {
+  int st = check_common(q, q_strides, k, k_strides, B, Hq, Hkv, S, D, dtype);
+  if (st != QF2_OK) return st;
+  const int64_t nb = (S + kBlk - 1) / kBlk;
+  if (!idx_out || keep <= 0 || keep > nb) return keep <= 0 || keep > nb ? QF2_ERR_SHAPE : QF2_ERR_ARG;
+  if (!workspace || workspace_bytes < qf2_blocktopk_workspace_bytes(B, Hq, Hkv, S, D) || !al16(workspace))
+    return QF2_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float* pq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + 256);
+  float* pk = pq + B * Hq * nb * kD;
+  const S3 qs{q_strides[0], q_strides[1], q_strides[2]}, ks{k_strides[0], k_strides[1], k_strides[2]};
+  const dim3 gp((unsigned)nb, (unsigned)(Hq + Hkv), (unsigned)B);
+  if (dtype == QF2_BF16)
+    blocktopk_pool_kernel<__nv_bfloat16><<<gp, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(q), qs,
+                                                             reinterpret_cast<const __nv_bfloat16*>(k), ks, S,
+                                                             (int)Hq, (int)Hkv, pq, pk);
+  else
+    blocktopk_pool_kernel<__half><<<gp, 128, 0, s>>>(reinterpret_cast<const __half*>(q), qs,
+                                                      reinterpret_cast<const __half*>(k), ks, S, (int)Hq, (int)Hkv,
+                                                      pq, pk);
+  QF2_LAUNCH_CHECK();
+  blocktopk_select_kernel<<<dim3((unsigned)nb, (unsigned)Hq, (unsigned)B), 128, 0, s>>>(pq, pk, (int)nb, (int)Hq,
+                                                                                     (int)Hkv, (int)keep, idx_out);
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}
+
+extern "C" int qf2_blocksparse_attn(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                    const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides,
+                                    int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t D, const int32_t* idx,
+                                    int64_t keep, float sm_scale, int dtype, void* workspace,
+                                    int64_t workspace_bytes, qf2_stream_t stream) {
+  int st = check_common(q, q_strides, k, k_strides, B, Hq, Hkv, S, D, dtype);
+  if (st != QF2_OK) return st;
+  if (!v || !v_strides || !out || !out_strides || !idx) return QF2_ERR_ARG;
+  if (!al16(v) || !al16(out)) return QF2_ERR_ALIGN;
+  for (int i = 0; i < 3; ++i)
+    if ((v_strides[i] % 8) || (out_strides[i] % 8)) return QF2_ERR_ALIGN;
+  const int64_t nb = (S + kBlk - 1) / kBlk;
+  if (keep <= 0 || keep > nb) return QF2_ERR_SHAPE;
+  if (!workspace || workspace_bytes < 256 || !al16(workspace)) return QF2_ERR_WORKSPACE;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, q, q_strides, B, Hq, S, dtype) || !make_map(&mk, k, k_strides, B, Hkv, S, dtype) ||
+      !make_map(&mv, v, v_strides, B, Hkv, S, dtype))
+    return QF2_ERR_ALIGN;
+  AttnArgs a;
+  a.idx = idx;
+  a.out = out;
+  a.os = S3{out_strides[0], out_strides[1], out_strides[2]};
+  a.S = S;
+  a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.keep = (int)keep; a.nb = (int)nb;
+  a.scale_log2 = (float)((double)sm_scale * 1.4426950408889634);
+  a.f16 = dtype == QF2_F16;
+  a.status = reinterpret_cast<int*>(workspace);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  QF2_CUDA_CHECK(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  QF2_CUDA_CHECK(
+      cudaFuncSetAttribute(blocksparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::alloc));
+  blocksparse_attn_kernel<<<dim3((unsigned)nb, (unsigned)Hq, (unsigned)B), kThreads, Smem::alloc, s>>>(mq, mk, mv, a);
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}

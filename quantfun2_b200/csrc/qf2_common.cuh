@@ -131,6 +131,15 @@ QF2_DEV void tma_load_3d(void* smem_dst, const void* tmap, int32_t x, int32_t y,
       : "memory");
 }
 
+// 4-D tiled TMA load (no multicast).
+QF2_DEV void tma_load_4d(void* smem_dst, const void* tmap, int32_t x, int32_t y, int32_t z, int32_t w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
 QF2_DEV void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -293,6 +302,15 @@ template <>
 QF2_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
 }  // namespace qf2
+
+// ------------------------------------------------------------- host: TMA --
+#include <cudaTypedefs.h>
+
+// Encodes a 4-D tiled tensor map (dims innermost first, byte strides of dims 1..3)
+// with 128-byte swizzle; out-of-bounds elements read as zero.  Returns false when
+// the driver entry point is unavailable or the encoder rejects the layout.
+bool qf2_make_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[4],
+                      const uint64_t strides_bytes[3], const uint32_t box[4]);
 
 // Records the CUDA error behind a QF2_ERR_LAUNCH for qf2_last_error().
 void qf2_record_cuda_error(cudaError_t e, const char* where);

@@ -11,8 +11,11 @@ B200.
   rope_apply_(xq, xk, freqs_cis)       -> (xq, xk) in place   triton/rope.py:83-134
   rmsnorm_apply(x, weight, eps)        -> Tensor              __init__.py:73-80
   inplace_softmax(x, dim=-1)           -> x                   __init__.py:83-87
+  topk_attn(xq, xk, xv, mask, ...)     -> (out, POS_DICT)     __init__.py:146-195 (block form)
 """
 from __future__ import annotations
+
+import math
 
 import torch
 
@@ -25,6 +28,7 @@ __all__ = [
     "rope_apply_",
     "rmsnorm_apply",
     "inplace_softmax",
+    "topk_attn",
     "QF2Error",
 ]
 
@@ -152,3 +156,27 @@ def inplace_softmax(x: torch.Tensor, dim: int = -1) -> torch.Tensor:
     check(_lib.load().qf2_softmax_inplace(x.data_ptr(), rows, n, n, dtype_code(x.dtype), stream_ptr(x.device)),
           "qf2_softmax_inplace")
     return x
+
+
+def topk_attn(xq, xk, xv, mask, fn, HEAD_DIM, scale=None, TOP_K=256, POS_DICT=None, N_HEADS=32, N_KV_HEADS=8):
+    """Block-sparse replacement of the reference's topk_attn (src/kernels/__init__.py:146-195).
+
+    Same call and return convention: xq [B, S, Hq, D], xk/xv [B, S, Hkv, D] ->
+    (out [B, S, Hq, D], POS_DICT).  Selection is per 128-token block: every query block
+    keeps ceil(TOP_K / 128) key blocks ranked by mean-pooled Q . K^T; POS_DICT is the
+    int32 block-index tensor [B, Hq, ceil(S/128), keep], computed when None and reused
+    otherwise (the reference's layer-to-layer cache).  The inputs are not modified (the
+    reference transposes them in place).  Key padding masks are not supported: `mask`
+    must be None or all True.
+    """
+    from .attention import block_topk_select, blocksparse_attn
+
+    if mask is not None and not bool(mask.all()):
+        raise QF2Error("block-sparse topk_attn supports unpadded sequences only")
+    if scale is None:
+        scale = 1.0 / math.sqrt(HEAD_DIM)
+    if POS_DICT is None:
+        keep = max(1, -(-int(TOP_K) // 128))
+        POS_DICT = block_topk_select(xq, xk, keep, tensor_layout="NHD")
+    out = blocksparse_attn(xq, xk, xv, POS_DICT, sm_scale=scale, tensor_layout="NHD")
+    return out, POS_DICT
