@@ -177,6 +177,32 @@ int qf2_blocksparse_attn(const void* q, const int64_t* q_strides, const void* k,
                          int64_t Hq, int64_t Hkv, int64_t S, int64_t D, const int32_t* idx, int64_t keep,
                          float sm_scale, int dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
 
+/* ------------------------------------------------------ quantized linears --
+ * Replace the torchao weight subclasses the reference swaps into nn.Linear.weight
+ * (src/quant.py:131-148; int8 weight-only :209-224, float8 weight-only :227-241).
+ *
+ * qf2_quantize_rows: per-row symmetric quantization of x [M, K] (row stride ldx):
+ *   QF2_I8:   scale = max(amax / 127.5, FLT_EPSILON), code = rint(x / scale) in [-128, 127]
+ *   QF2_E4M3: scale = amax / 448 (1 for a zero row), code = e4m3(x * (448 / amax))
+ * One fp32 scale per row in `scales` (weights: per output channel; activations: per token).
+ *
+ * qf2_codes_to_bf16: int8 / e4m3 codes -> bf16 (exact).
+ *
+ * qf2_gemm: D[M, N] = (A . B^T) * row_scale[m] * col_scale[n] + bias[n] on tcgen05 tensor
+ * cores, A [M, K] and B [N, K] both QF2_BF16 or both QF2_E4M3 with K contiguous (row
+ * strides lda/ldb in elements), fp32 accumulation, D QF2_BF16 or QF2_F32 (row stride
+ * ldd).  row_scale, col_scale and bias may be NULL; bias is QF2_BF16 or QF2_F32.
+ * N % 8 == 0.  Workspace: >= 256 bytes (status word).
+ * Weight-only INT8/FP8 linear: D = qf2_gemm(x_bf16, bf16(codes), col_scale = w_scale).
+ * W8A8 FP8 linear: D = qf2_gemm(e4m3(x), e4m3 codes, row_scale = x_scale, col_scale = w_scale). */
+int qf2_quantize_rows(const void* x, int64_t ldx, int x_dtype, int64_t M, int64_t K, void* q, int64_t ldq,
+                      int q_dtype, float* scales, qf2_stream_t stream);
+int qf2_codes_to_bf16(const void* q, int64_t ldq, int q_dtype, int64_t M, int64_t K, void* out, int64_t ldo,
+                      qf2_stream_t stream);
+int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M, int64_t N,
+             int64_t K, int ab_dtype, int d_dtype, const float* row_scale, const float* col_scale, const void* bias,
+             int bias_dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
+
 /* No counterpart in the reference.  qf2_sageattn without a caller workspace, for
  * callers that cannot allocate device memory: programs that reserve all device memory
  * in their own pool, code that must avoid the device synchronization an allocation

@@ -74,6 +74,14 @@ SIGNATURES = {
         [c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64,
          c_int64, c_void_p, c_int64, c_float, c_int, c_void_p, c_int64, c_void_p],
     ),
+    "qf2_quantize_rows": (
+        c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "qf2_codes_to_bf16": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
+    "qf2_gemm": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+         c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p],
+    ),
     "qf2_sageattn_noalloc": (
         c_int,
         [c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64,

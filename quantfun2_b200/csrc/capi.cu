@@ -12,25 +12,44 @@ void qf2_record_cuda_error(cudaError_t e, const char* where) {
 
 extern "C" const char* qf2_last_error(void) { return g_last_error; }
 
-bool qf2_make_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[4],
-                      const uint64_t strides_bytes[3], const uint32_t box[4]) {
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
         q != cudaDriverEntryPointSuccess || fn == nullptr)
-      return false;
+      return nullptr;
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
-  const cuuint64_t gdim[4] = {dims[0], dims[1], dims[2], dims[3]};
-  const cuuint64_t gstr[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
-  const cuuint32_t bdim[4] = {box[0], box[1], box[2], box[3]};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUresult r = encode(map, dtype, 4, const_cast<void*>(base), gdim, gstr, bdim, estr,
+  return encode;
+}
+
+static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                      const cuuint64_t* gdim, const cuuint64_t* gstr, const cuuint32_t* bdim) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tmap_encoder();
+  if (encode == nullptr) return false;
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = encode(map, dtype, rank, const_cast<void*>(base), gdim, gstr, bdim, estr,
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+bool qf2_make_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[4],
+                      const uint64_t strides_bytes[3], const uint32_t box[4]) {
+  const cuuint64_t gdim[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t gstr[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  const cuuint32_t bdim[4] = {box[0], box[1], box[2], box[3]};
+  return make_tmap(map, dtype, 4, base, gdim, gstr, bdim);
+}
+
+bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
+                      uint64_t stride_bytes, const uint32_t box[2]) {
+  const cuuint64_t gdim[2] = {dims[0], dims[1]};
+  const cuuint64_t gstr[1] = {stride_bytes};
+  const cuuint32_t bdim[2] = {box[0], box[1]};
+  return make_tmap(map, dtype, 2, base, gdim, gstr, bdim);
 }
 
 extern "C" const char* qf2_version(void) { return "quantfun2-b200 0.1.0 (sm_100a)"; }

@@ -311,6 +311,9 @@ QF2_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
 // the driver entry point is unavailable or the encoder rejects the layout.
 bool qf2_make_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[4],
                       const uint64_t strides_bytes[3], const uint32_t box[4]);
+// Same, 2-D (dims innermost first, byte stride of dim 1).
+bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
+                      uint64_t stride_bytes, const uint32_t box[2]);
 
 // Records the CUDA error behind a QF2_ERR_LAUNCH for qf2_last_error().
 void qf2_record_cuda_error(cudaError_t e, const char* where);
