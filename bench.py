@@ -10,6 +10,10 @@ FP8 PV, fp32 accumulation).  Metric: attention TFLOPS = 4*B*H*S^2*D / time.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
+The JSON line also carries "flux_step": the ms per Flux-dev-shaped denoise step
+(19 double + 38 single blocks, 4608 tokens, FP8 linears + Sage attention), split
+over the N ranks with Ulysses head-parallel attention when N > 1.
+
 N > 1 is launched by torchrun, one rank per GPU; each rank runs its own B=2
 problem (independent sequences, no collective on the data path: weak scaling).
 Rank 0 prints one JSON line.  `--impl reference` times the reference's CPU path
@@ -48,6 +52,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-flux", action="store_true")
     return p.parse_args()
 
 
@@ -177,6 +182,83 @@ def make_inputs(dev, seed):
     return q.bfloat16(), k.bfloat16(), v.bfloat16()
 
 
+def run_flux_step(rank: int, world: int, dev, warmup: int = 2, steps: int = 5) -> dict:
+    """One Flux-dev-shaped forward (19 double + 38 single blocks, hidden 3072, 24 x 128 heads,
+    4096 img + 512 txt tokens, FP8 W8A8 linears, Sage attention) per step; with N ranks the
+    joint sequence is split N ways and attention runs head-parallel (Ulysses all-to-all)."""
+    from quantfun2_b200.dit import FluxDiT, SeqParallel, flux_position_ids, flux_step_flops, rope_freqs
+
+    T, side = 512, 64
+    I = side * side
+    if T % world or I % world or 24 % world:
+        return {"skipped": f"{world} ranks do not divide 512 txt / 4096 img tokens and 24 heads"}
+    model = FluxDiT(device=dev, seed=0)
+    sp = SeqParallel(torch.distributed.group.WORLD if world > 1 else None)
+    g = torch.Generator(device=dev).manual_seed(0)  # identical inputs on every rank
+    img = torch.randn(1, I, 64, device=dev, generator=g).bfloat16()
+    txt = torch.randn(1, T, 4096, device=dev, generator=g).bfloat16()
+    t = torch.rand(1, device=dev, generator=g)
+    y = torch.randn(1, 768, device=dev, generator=g).bfloat16()
+    freqs = rope_freqs(flux_position_ids(1, T, side, side, dev), (16, 56, 56))
+    tl, il = T // world, I // world
+    img_l, txt_l = img[:, rank * il:(rank + 1) * il].contiguous(), txt[:, rank * tl:(rank + 1) * tl].contiguous()
+    f_l = torch.cat([freqs[:, rank * tl:(rank + 1) * tl], freqs[:, T + rank * il:T + (rank + 1) * il]], 1).contiguous()
+    def timed(fn):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        sec = e0.elapsed_time(e1) / 1e3 / steps
+        if world > 1:
+            tt = torch.tensor([sec], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+            sec = float(tt[0])
+        return sec
+
+    fwd = lambda: model(img_l, txt_l, t, y, f_l, sp)  # noqa: E731
+    with torch.inference_mode():
+        for _ in range(warmup):
+            fwd()
+        eager = timed(fwd)
+        # the whole step as one CUDA graph: the ~2000 launches of a step replay without
+        # host-side launch cost (the step is otherwise bound by Python/launch overhead)
+        graph, sec, out = None, eager, None
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                fwd()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = fwd()
+            for _ in range(warmup):
+                graph.replay()
+            sec = timed(graph.replay)
+        except Exception as e:  # noqa: BLE001
+            graph = None
+            out = fwd()
+            graph_error = f"{type(e).__name__}: {e}"[:200]
+        finite = bool(torch.isfinite(out.float()).all())
+    res_graph = graph is not None
+    del graph, model
+    torch.cuda.empty_cache()
+    fl = flux_step_flops(T + I)
+    res = {"ms_per_step": sec * 1e3, "tflops": fl / sec / 1e12, "flops_per_step": fl, "tokens": T + I,
+           "steps": steps, "warmup": warmup, "cuda_graph": res_graph, "eager_ms_per_step": eager * 1e3,
+           "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU",
+           "linears": "FP8 e4m3 W8A8 (per-token activation, per-channel weight scales)",
+           "attention": "Sage INT8 QK / FP8 PV", "output_finite": finite}
+    if not res_graph:
+        res["graph_error"] = graph_error
+    return res
+
+
 def run_ours(args, rank: int, world: int, dev):
     from quantfun2_b200 import _lib
     from quantfun2_b200._lib import check, i64, stream_ptr
@@ -274,6 +356,13 @@ def run_ours(args, rank: int, world: int, dev):
                "d2h_bytes_per_step": out.numel() * out.element_size(), "ms_per_step": e2e_s * 1e3,
                "steps": e2e_steps}
 
+    # ---- the Flux-shaped denoise step (Ulysses over the ranks when N > 1)
+    flux = None
+    if not args.no_flux:
+        del q, k, v, out, ws
+        torch.cuda.empty_cache()
+        flux = run_flux_step(rank, world, dev)
+
     if rank != 0:
         return
     # ---- CPU baseline: the reference's SDPA branch on a bounded sample (rank 0, N=1 only)
@@ -313,6 +402,7 @@ def run_ours(args, rank: int, world: int, dev):
         "e2e": e2e,
         "gpu_launches": 4 * args.steps,
         "clocks": clocks,
+        "flux_step": flux,
     }
     print(json.dumps(line), flush=True)
 

@@ -78,6 +78,17 @@ int qf2_rope_apply(const void* xq, void* xq_out, int64_t Hq, const int64_t* xq_s
                    const int64_t* freqs_strides, int64_t B, int64_t S, int64_t D, int dtype, int flags,
                    qf2_stream_t stream);
 
+/* Fused per-head q/k RMSNorm + RoPE on a fused QKV projection output, replacing the
+ * q_norm / k_norm + rope_apply sequence of the attention blocks (src/models/flux/mmdit.py
+ * :133-149, src/models/common/attn.py:209-212): qkv [B*L, 3*H*D] bf16 (row stride
+ * qkv_row_stride); q and k rows -> x * rsqrt(mean(x^2) + eps) * w, rotated by
+ * freqs_cis[b, s] (complex64, strides {batch, seq} in complex elements), rounded once;
+ * v copied.  Outputs through {batch, seq, head} element strides.  D = 128, bf16. */
+int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_t L, int64_t H, int64_t D,
+                      void* q_out, const int64_t* q_strides, void* k_out, const int64_t* k_strides, void* v_out,
+                      const int64_t* v_strides, const void* q_weight, const void* k_weight, float eps,
+                      const void* freqs_cis, const int64_t* freqs_strides, qf2_stream_t stream);
+
 /* ------------------------------------------------------------- RMSNorm --
  * Replaces rmsnorm_apply (src/kernels/__init__.py:73-80) and the Triton
  * apply_rmsnorm (src/kernels/triton/rmsnorm.py:72-95).
@@ -202,6 +213,23 @@ int qf2_codes_to_bf16(const void* q, int64_t ldq, int q_dtype, int64_t M, int64_
 int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M, int64_t N,
              int64_t K, int ab_dtype, int d_dtype, const float* row_scale, const float* col_scale, const void* bias,
              int bias_dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
+/* qf2_gemm with the DiT block epilogues fused (src/models/flux/mmdit.py:152-160, :226-231):
+ * y = (A . B^T) * row_scale * col_scale + bias;  y = gelu_tanh(y) on columns >= gelu_col0
+ * (gelu_col0 < 0: none);  D = residual + gate[m / rows_per_gate][n] * y when residual is
+ * non-NULL (bf16, row stride ldr; gate bf16 with row stride gate_stride, NULL = 1).
+ * D may alias residual. */
+int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M, int64_t N,
+                int64_t K, int ab_dtype, int d_dtype, const float* row_scale, const float* col_scale,
+                const void* bias, int bias_dtype, int64_t gelu_col0, const void* residual, int64_t ldr,
+                const void* gate, int64_t gate_stride, int64_t rows_per_gate, void* workspace,
+                int64_t workspace_bytes, qf2_stream_t stream);
+/* Fused adaLN input (src/models/flux/mmdit.py:127-128, src/models/common/utilities.py:4-5):
+ * y = LayerNorm(x) * (1 + scale[b]) + shift[b] over rows of N (no affine, eps), b = row /
+ * rows_per_batch, shift/scale bf16 with row stride mod_stride; out QF2_BF16, or QF2_E4M3
+ * with a per-row scale in `scales` (ready for the FP8 GEMM).  N % 8 == 0, N <= 16384. */
+int qf2_ln_modulate(const void* x, int64_t ldx, int x_dtype, const void* shift, const void* scale, int64_t mod_stride,
+                    int64_t rows_per_batch, int64_t M, int64_t N, float eps, void* out, int64_t ldo, int out_dtype,
+                    float* scales, qf2_stream_t stream);
 
 /* No counterpart in the reference.  qf2_sageattn without a caller workspace, for
  * callers that cannot allocate device memory: programs that reserve all device memory

@@ -33,6 +33,11 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_int64, _P64, _P64, c_void_p, c_void_p, c_int64, _P64, _P64, c_void_p, _P64,
          c_int64, c_int64, c_int64, c_int, c_int, c_void_p],
     ),
+    "qf2_qkv_norm_rope": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64,
+         c_void_p, c_void_p, c_float, c_void_p, _P64, c_void_p],
+    ),
     "qf2_rmsnorm": (
         c_int,
         [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int64, c_int, c_int64, c_int64, c_float, c_int,
@@ -81,6 +86,17 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
          c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p],
+    ),
+    "qf2_gemm_ex": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+         c_void_p, c_void_p, c_void_p, c_int, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+         c_int64, c_void_p],
+    ),
+    "qf2_ln_modulate": (
+        c_int,
+        [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
+         c_int64, c_int, c_void_p, c_void_p],
     ),
     "qf2_sageattn_noalloc": (
         c_int,

@@ -50,9 +50,10 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
 
 def sageattn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tensor_layout: str = "HND",
              is_causal: bool = False, sm_scale: float | None = None, return_lse: bool = False,
-             **kwargs) -> torch.Tensor:
+             out: torch.Tensor | None = None, **kwargs) -> torch.Tensor:
     """INT8 QK^T / FP8 PV attention.  q [B, Hq, Sq, D] (HND) or [B, Sq, Hq, D] (NHD);
-    k, v with Hkv heads (Hq % Hkv == 0).  D = 128.  Returns a tensor in q's layout."""
+    k, v with Hkv heads (Hq % Hkv == 0).  D = 128.  Returns a tensor in q's layout;
+    `out` may be any strided view of that shape (16-byte aligned rows)."""
     if is_causal:
         raise QF2Error("causal masking is not on the DiT path (bidirectional attention only)")
     if return_lse:
@@ -73,7 +74,10 @@ def sageattn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tensor_layout: s
         raise QF2Error("k and v must have the same shape, and q/k/v the same dtype")
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    out = torch.empty_like(q)
+    if out is None:
+        out = torch.empty_like(q)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.stride(-1) != 1:
+        raise QF2Error("out must match q's shape and dtype with a contiguous last dim")
     lib = _lib.load()
     nbytes = lib.qf2_sage_workspace_bytes(B, Hq, Hkv, B * Sq, B * Skv, Sq, Skv, D)
     if nbytes < 0:

@@ -474,8 +474,8 @@ extern "C" int qf2_blocksparse_attn(const void* q, const int64_t* q_strides, con
   a.status = reinterpret_cast<int*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   QF2_CUDA_CHECK(cudaMemsetAsync(workspace, 0, sizeof(int), s));
-  QF2_CUDA_CHECK(
-      cudaFuncSetAttribute(blocksparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::alloc));
+  static std::atomic<uint64_t> attr_done{0};
+  QF2_CUDA_CHECK(qf2_set_smem_once(blocksparse_attn_kernel, Smem::alloc, &attr_done));
   blocksparse_attn_kernel<<<dim3((unsigned)nb, (unsigned)Hq, (unsigned)B), kThreads, Smem::alloc, s>>>(mq, mk, mv, a);
   QF2_LAUNCH_CHECK();
   return QF2_OK;

@@ -12,11 +12,12 @@
 //   warp 0     TMA producer: A box [128 B of K, 128 rows], B box [128 B of K, 256 rows],
 //              128-byte swizzle, 4-stage ring
 //   warp 1     MMA issuer: 4 x (M128 N256) per stage into one of two TMEM accumulators
-//   warps 2-5  epilogue: TMEM -> registers -> scales/bias -> global, overlapped with the
-//              next tile's main loop through the second accumulator
+//   warps 2-9  epilogue: TMEM -> registers -> scales/bias/GELU/gated residual -> global,
+//              overlapped with the next tile's main loop through the second accumulator
 #include "qf2_common.cuh"
 
 #include <algorithm>
+#include <climits>
 
 namespace qf2 {
 namespace gemm {
@@ -26,7 +27,8 @@ constexpr int kStages = 4;
 constexpr int kABytes = BM * 128;   // 128 rows x 128 bytes of K
 constexpr int kBBytes = BN * 128;   // 256 rows x 128 bytes of K
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;           // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpilogueWarps = 8;
 constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
 
 struct Smem {
@@ -48,8 +50,42 @@ struct Args {
   int bias_f32;   // 1: fp32 bias, 0: bf16 bias
   int d_f32;      // 1: fp32 output, 0: bf16 output
   int fp8;        // operand type: 1 e4m3, 0 bf16
+  int64_t gelu_col0;                 // GELU (tanh form) on columns >= gelu_col0
+  const __nv_bfloat16* residual;     // D = residual + gate * y when non-null
+  int64_t ldr;
+  const __nv_bfloat16* gate;         // per (row / rows_per_gate, column); null = 1
+  int64_t gate_stride, rows_per_gate;
+  int vec_ok;     // scale / bias / residual / gate rows 16-byte aligned: vector loads
   int* status;
 };
+
+QF2_DEV void load_f32x32(const float* p, float* o) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p + i));
+    o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+  }
+}
+
+QF2_DEV void load_bf16x32(const __nv_bfloat16* p, float* o) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p + i);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[i + j] = __bfloat162float(e[j]);
+  }
+}
+
+// GELU, tanh form, with the SFU tanh (tanh.approx.f32: ~2^-11 relative error, below
+// the bf16 rounding of the output)
+QF2_DEV float gelu_tanh_fast(float x) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * x * (1.0f + t);
+}
+
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, Args A) {
@@ -72,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, 4); }
+    for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, kEpilogueWarps); }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -163,7 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------- epilogue --
+    // 8 warps: lane quarter = warp & 3 (TMEM lanes / tile rows), column half = (warp - 2) / 4
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     int it = 0;
@@ -171,14 +209,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
       const int64_t m = (tile % mt) * BM + r;
-      const int64_t n0 = (tile / mt) * BN;
+      const int64_t n0 = (tile / mt) * BN + half * (BN / 2);
       if (!wwait(acc_full + buf, (uint32_t)((it >> 1) & 1))) { ok = false; break; }
       tc_fence_after();
       const float rs = (A.row_scale != nullptr && m < A.M) ? A.row_scale[m] : 1.0f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < BN / 64; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + lane_off + buf * BN + c * 32, v);
+        tmem_ld32(tmem + lane_off + buf * BN + half * (BN / 2) + c * 32, v);
         tmem_wait_ld();
         const int64_t nc = n0 + c * 32;
         if (m >= A.M || nc >= A.N) continue;
@@ -186,17 +224,56 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]) * rs;
         const int ncols = (int)min((int64_t)32, A.N - nc);
-        if (A.col_scale != nullptr) {
+        if (ncols == 32 && A.vec_ok) {
+          if (A.col_scale != nullptr) {
+            float cs[32];
+            load_f32x32(A.col_scale + nc, cs);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < ncols) o[i] *= __ldg(A.col_scale + nc + i);
-        }
-        if (A.bias != nullptr) {
+            for (int i = 0; i < 32; ++i) o[i] *= cs[i];
+          }
+          if (A.bias != nullptr) {
+            float bb[32];
+            if (A.bias_f32)
+              load_f32x32(reinterpret_cast<const float*>(A.bias) + nc, bb);
+            else
+              load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(A.bias) + nc, bb);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < ncols)
-              o[i] += A.bias_f32 ? __ldg(reinterpret_cast<const float*>(A.bias) + nc + i)
+            for (int i = 0; i < 32; ++i) o[i] += bb[i];
+          }
+          if (nc + 32 > A.gelu_col0) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nc + i >= A.gelu_col0) o[i] = gelu_tanh_fast(o[i]);
+          }
+          if (A.residual != nullptr) {
+            float rr[32], gg[32];
+            load_bf16x32(A.residual + m * A.ldr + nc, rr);
+            if (A.gate != nullptr) {
+              load_bf16x32(A.gate + (m / A.rows_per_gate) * A.gate_stride + nc, gg);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) gg[i] = 1.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = fmaf(gg[i], o[i], rr[i]);
+          }
+        } else {
+          // ragged or unaligned columns: element-wise with bounds
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i >= ncols) continue;
+            if (A.col_scale != nullptr) o[i] *= A.col_scale[nc + i];
+            if (A.bias != nullptr)
+              o[i] += A.bias_f32 ? reinterpret_cast<const float*>(A.bias)[nc + i]
                                  : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(A.bias)[nc + i]);
+            if (nc + i >= A.gelu_col0) o[i] = gelu_tanh_fast(o[i]);
+            if (A.residual != nullptr) {
+              const float g = A.gate != nullptr
+                                  ? __bfloat162float(A.gate[(m / A.rows_per_gate) * A.gate_stride + nc + i])
+                                  : 1.0f;
+              o[i] = fmaf(g, o[i], __bfloat162float(A.residual[m * A.ldr + nc + i]));
+            }
+          }
         }
         if (A.d_f32) {
           float* dst = reinterpret_cast<float*>(A.d) + m * A.ldd + nc;
@@ -252,15 +329,17 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) =
 
 using namespace qf2::gemm;
 
-extern "C" int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M,
-                        int64_t N, int64_t K, int ab_dtype, int d_dtype, const float* row_scale,
-                        const float* col_scale, const void* bias, int bias_dtype, void* workspace,
-                        int64_t workspace_bytes, qf2_stream_t stream) {
+extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M,
+                           int64_t N, int64_t K, int ab_dtype, int d_dtype, const float* row_scale,
+                           const float* col_scale, const void* bias, int bias_dtype, int64_t gelu_col0,
+                           const void* residual, int64_t ldr, const void* gate, int64_t gate_stride,
+                           int64_t rows_per_gate, void* workspace, int64_t workspace_bytes, qf2_stream_t stream) {
   if (!a || !b || !d) return QF2_ERR_ARG;
   if (ab_dtype != QF2_BF16 && ab_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
   if (d_dtype != QF2_BF16 && d_dtype != QF2_F32) return QF2_ERR_DTYPE;
   if (bias && bias_dtype != QF2_BF16 && bias_dtype != QF2_F32) return QF2_ERR_DTYPE;
   if (M <= 0 || N <= 0 || K <= 0 || (N % 8)) return QF2_ERR_SHAPE;
+  if (residual && (ldr < N || (gate && rows_per_gate <= 0))) return QF2_ERR_SHAPE;
   const int esz = ab_dtype == QF2_E4M3 ? 1 : 2;
   if (!al16(a) || !al16(b) || !al16(d) || (lda * esz) % 16 || (ldb * esz) % 16 || (ldd % 8) || lda < K || ldb < K ||
       ldd < N)
@@ -285,16 +364,32 @@ extern "C" int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, 
   args.bias_f32 = bias_dtype == QF2_F32;
   args.d_f32 = d_dtype == QF2_F32;
   args.fp8 = ab_dtype == QF2_E4M3;
+  args.gelu_col0 = gelu_col0 < 0 ? INT64_MAX : gelu_col0;
+  args.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
+  args.ldr = ldr;
+  args.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
+  args.gate_stride = gate_stride;
+  args.rows_per_gate = rows_per_gate > 0 ? rows_per_gate : 1;
+  args.vec_ok = al16(col_scale) && al16(bias) && al16(residual) && al16(gate) && (ldr % 8) == 0 &&
+                (gate_stride % 8) == 0;
   args.status = reinterpret_cast<int*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   QF2_CUDA_CHECK(cudaMemsetAsync(workspace, 0, sizeof(int), s));
-  QF2_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::alloc));
-  int dev = 0, sms = 148;
-  QF2_CUDA_CHECK(cudaGetDevice(&dev));
-  QF2_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  static std::atomic<uint64_t> attr_done{0};
+  QF2_CUDA_CHECK(qf2_set_smem_once(gemm_kernel, Smem::alloc, &attr_done));
+  int sms = 148;
+  QF2_CUDA_CHECK(qf2_sm_count(&sms));
   const int64_t ntiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms);
   gemm_kernel<<<grid, kThreads, Smem::alloc, s>>>(ma, mb, args);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
+}
+
+extern "C" int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M,
+                        int64_t N, int64_t K, int ab_dtype, int d_dtype, const float* row_scale,
+                        const float* col_scale, const void* bias, int bias_dtype, void* workspace,
+                        int64_t workspace_bytes, qf2_stream_t stream) {
+  return qf2_gemm_ex(a, lda, b, ldb, d, ldd, M, N, K, ab_dtype, d_dtype, row_scale, col_scale, bias, bias_dtype, -1,
+                     nullptr, 0, nullptr, 0, 1, workspace, workspace_bytes, stream);
 }

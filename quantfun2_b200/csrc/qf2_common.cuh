@@ -303,6 +303,39 @@ QF2_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
 }  // namespace qf2
 
+// -------------------------------------------------- host: per-device setup --
+#include <atomic>
+
+// Raises `kernel`'s dynamic shared memory limit the first time it is launched on the
+// current device (the attribute is per device; later calls cost one cudaGetDevice).
+template <typename K>
+inline cudaError_t qf2_set_smem_once(K* kernel, int bytes, std::atomic<uint64_t>* done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done->load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done->fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+// SM count of the current device, cached per device.
+inline cudaError_t qf2_sm_count(int* out) {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int v = cache[dev & 63].load(std::memory_order_relaxed);
+  if (v == 0) {
+    e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    cache[dev & 63].store(v, std::memory_order_relaxed);
+  }
+  *out = v;
+  return cudaSuccess;
+}
+
 // ------------------------------------------------------------- host: TMA --
 #include <cudaTypedefs.h>
 

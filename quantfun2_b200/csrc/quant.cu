@@ -46,6 +46,169 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   }
 }
 
+// Fast path: 16-bit rows with K % 8 == 0 and K <= 256 * 8 * kRowVecs, 16-byte aligned.
+// The row stays in registers (one HBM read), 16-byte loads, 8-byte e4m3 stores.
+constexpr int kRowVecs = 8;
+
+template <typename T>
+QF2_DEV float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) v = fmaxf(v, red[w]);
+  return v;
+}
+
+QF2_DEV float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[w];
+  return v;
+}
+
+// store 8 values of a row either as bf16 (16 bytes) or e4m3 (8 bytes, * inv)
+QF2_DEV void store8(void* out, int64_t off, const float* y, bool fp8, float inv) {
+  if (fp8) {
+    uint2 w;
+    w.x = (uint32_t)f32x2_to_e4m3x2(__fmul_rn(y[0], inv), __fmul_rn(y[1], inv)) |
+          ((uint32_t)f32x2_to_e4m3x2(__fmul_rn(y[2], inv), __fmul_rn(y[3], inv)) << 16);
+    w.y = (uint32_t)f32x2_to_e4m3x2(__fmul_rn(y[4], inv), __fmul_rn(y[5], inv)) |
+          ((uint32_t)f32x2_to_e4m3x2(__fmul_rn(y[6], inv), __fmul_rn(y[7], inv)) << 16);
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(out) + off) = w;
+  } else {
+    uint4 w;
+    uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 t = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+      wp[j] = *reinterpret_cast<uint32_t*>(&t);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + off) = w;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_vec_kernel(const T* __restrict__ x, int64_t ldx, int K, void* q,
+                                                                int64_t ldq, int fp8, float* __restrict__ scales) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * ldx;
+  const int nv = K / 8;
+  uint4 raw[kRowVecs];
+  float am = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowVecs; ++c) {
+    const int vi = threadIdx.x + c * 256;
+    raw[c] = vi < nv ? *reinterpret_cast<const uint4*>(xr + vi * 8) : make_uint4(0, 0, 0, 0);
+    const T* e = reinterpret_cast<const T*>(&raw[c]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(to_f32(e[j])));
+  }
+  am = block_max<T>(am, red);
+  const float inv = fp8 ? (am > 0.f ? __fdiv_rn(448.0f, am) : 1.0f) : 0.f;
+  const float sc = fp8 ? (am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f) : fmaxf(__fdiv_rn(am, 127.5f), FLT_EPSILON);
+  if (threadIdx.x == 0) scales[row] = sc;
+#pragma unroll
+  for (int c = 0; c < kRowVecs; ++c) {
+    const int vi = threadIdx.x + c * 256;
+    if (vi >= nv) continue;
+    const T* e = reinterpret_cast<const T*>(&raw[c]);
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = to_f32(e[j]);
+    if (fp8) {
+      store8(q, row * ldq + vi * 8, y, true, inv);
+    } else {
+      uint2 w = make_uint2(0u, 0u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int cc = max(-128, min(127, __float2int_rn(__fdiv_rn(y[j], sc))));
+        (j < 4 ? w.x : w.y) |= (uint32_t)(cc & 0xff) << ((j & 3) * 8);
+      }
+      *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(q) + row * ldq + vi * 8) = w;
+    }
+  }
+}
+
+// adaLN: y = LayerNorm(x) * (1 + scale[b]) + shift[b] (LayerNorm without affine, fp32
+// statistics), written as bf16 or as e4m3 with a per-row scale for the next GEMM.
+// Same row constraints as the fast quantizer.
+template <typename T>
+__global__ void __launch_bounds__(256) ln_modulate_kernel(const T* __restrict__ x, int64_t ldx, int N,
+                                                          const __nv_bfloat16* __restrict__ shift,
+                                                          const __nv_bfloat16* __restrict__ scale, int64_t mod_stride,
+                                                          int64_t rows_per_batch, float eps, void* out, int64_t ldo,
+                                                          int fp8, float* __restrict__ scales) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * ldx;
+  const int64_t bi = row / rows_per_batch;
+  const __nv_bfloat16* sh = shift + bi * mod_stride;
+  const __nv_bfloat16* scl = scale + bi * mod_stride;
+  const int nv = N / 8;
+  float v[kRowVecs][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowVecs; ++c) {
+    const int vi = threadIdx.x + c * 256;
+    uint4 raw = vi < nv ? *reinterpret_cast<const uint4*>(xr + vi * 8) : make_uint4(0, 0, 0, 0);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[c][j] = to_f32(e[j]);
+      sum += v[c][j];
+    }
+  }
+  const float mean = block_sum(sum, red) / (float)N;
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowVecs; ++c) {
+    const int vi = threadIdx.x + c * 256;
+    if (vi < nv) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[c][j] - mean;
+        sq = fmaf(d, d, sq);
+      }
+    }
+  }
+  const float rstd = rsqrtf(block_sum(sq, red) / (float)N + eps);
+  float am = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowVecs; ++c) {
+    const int vi = threadIdx.x + c * 256;
+    if (vi < nv) {
+      const uint4 a = *reinterpret_cast<const uint4*>(sh + vi * 8);
+      const uint4 b = *reinterpret_cast<const uint4*>(scl + vi * 8);
+      const __nv_bfloat16* ae = reinterpret_cast<const __nv_bfloat16*>(&a);
+      const __nv_bfloat16* be = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[c][j] = fmaf((v[c][j] - mean) * rstd, 1.0f + __bfloat162float(be[j]), __bfloat162float(ae[j]));
+        am = fmaxf(am, fabsf(v[c][j]));
+      }
+    }
+  }
+  float inv = 1.f;
+  if (fp8) {
+    am = block_max<T>(am, red);
+    inv = am > 0.f ? __fdiv_rn(448.0f, am) : 1.0f;
+    if (threadIdx.x == 0) scales[row] = am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f;
+  }
+#pragma unroll
+  for (int c = 0; c < kRowVecs; ++c) {
+    const int vi = threadIdx.x + c * 256;
+    if (vi < nv) store8(out, row * ldo + vi * 8, v[c], fp8 != 0, inv);
+  }
+}
+
 // code -> bf16 (exact for int8 and e4m3 codes)
 __global__ void __launch_bounds__(256) codes_to_bf16_kernel(const void* q, int64_t ldq, int fp8, int64_t M, int64_t K,
                                                             __nv_bfloat16* __restrict__ out, int64_t ldo) {
@@ -77,6 +240,18 @@ extern "C" int qf2_quantize_rows(const void* x, int64_t ldx, int x_dtype, int64_
   if (M > 0x7fffffff) return QF2_ERR_SHAPE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int fp8 = q_dtype == QF2_E4M3;
+  const bool vec = (x_dtype == QF2_BF16 || x_dtype == QF2_F16) && K % 8 == 0 && K <= 256 * 8 * kRowVecs &&
+                   (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx % 8) == 0 &&
+                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && (ldq % 8) == 0;
+  if (vec) {
+    if (x_dtype == QF2_BF16)
+      quantize_rows_vec_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, s>>>((const __nv_bfloat16*)x, ldx, (int)K, q,
+                                                                         ldq, fp8, scales);
+    else
+      quantize_rows_vec_kernel<__half><<<(unsigned)M, 256, 0, s>>>((const __half*)x, ldx, (int)K, q, ldq, fp8, scales);
+    QF2_LAUNCH_CHECK();
+    return QF2_OK;
+  }
   switch (x_dtype) {
     case QF2_F32: quantize_rows_kernel<float><<<(unsigned)M, 256, 0, s>>>((const float*)x, ldx, K, q, ldq, fp8, scales); break;
     case QF2_F16: quantize_rows_kernel<__half><<<(unsigned)M, 256, 0, s>>>((const __half*)x, ldx, K, q, ldq, fp8, scales); break;
@@ -102,6 +277,37 @@ extern "C" int qf2_codes_to_bf16(const void* q, int64_t ldq, int q_dtype, int64_
   if (blocks > 148 * 32) blocks = 148 * 32;
   codes_to_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, ldq, q_dtype == QF2_E4M3, M, K,
                                                          reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}
+
+extern "C" int qf2_ln_modulate(const void* x, int64_t ldx, int x_dtype, const void* shift, const void* scale,
+                               int64_t mod_stride, int64_t rows_per_batch, int64_t M, int64_t N, float eps, void* out,
+                               int64_t ldo, int out_dtype, float* scales, qf2_stream_t stream) {
+  using namespace qf2::quant;
+  if (!x || !shift || !scale || !out) return QF2_ERR_ARG;
+  if (x_dtype != QF2_BF16 && x_dtype != QF2_F16) return QF2_ERR_DTYPE;
+  if (out_dtype != QF2_BF16 && out_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
+  if (out_dtype == QF2_E4M3 && !scales) return QF2_ERR_ARG;
+  if (M < 0 || N <= 0 || N % 8 || N > 256 * 8 * kRowVecs || rows_per_batch <= 0 || M > 0x7fffffff)
+    return QF2_ERR_SHAPE;
+  const int osz = out_dtype == QF2_E4M3 ? 1 : 2;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(shift) & 15) ||
+      (reinterpret_cast<uintptr_t>(scale) & 15) || (reinterpret_cast<uintptr_t>(out) & (osz == 1 ? 7 : 15)) ||
+      (ldx % 8) || (mod_stride % 8) || (ldo % 8))
+    return QF2_ERR_ALIGN;
+  if (M == 0) return QF2_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* sh = reinterpret_cast<const __nv_bfloat16*>(shift);
+  const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(scale);
+  const int fp8 = out_dtype == QF2_E4M3;
+  if (x_dtype == QF2_BF16)
+    ln_modulate_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, s>>>((const __nv_bfloat16*)x, ldx, (int)N, sh, sc,
+                                                                   mod_stride, rows_per_batch, eps, out, ldo, fp8,
+                                                                   scales);
+  else
+    ln_modulate_kernel<__half><<<(unsigned)M, 256, 0, s>>>((const __half*)x, ldx, (int)N, sh, sc, mod_stride,
+                                                            rows_per_batch, eps, out, ldo, fp8, scales);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }

@@ -137,3 +137,109 @@ extern "C" int qf2_rope_apply(const void* xq, void* xq_out, int64_t Hq, const in
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }
+
+// ------------------------------------------------ fused QK RMSNorm + RoPE --
+// Replaces the per-head q_norm / k_norm (src/models/flux/mmdit.py:133-134,
+// src/models/common/attn.py:209-210) followed by rope_apply (:149 / :212): one pass over
+// the fused QKV projection output [rows, 3*H*D] (row = b * L + s).  q and k rows get
+// y = x * rsqrt(mean(x^2) + eps) * w (fp32) rotated by freqs[b, s, :], then rounded
+// once; v rows are copied.  Outputs are written through {batch, seq, head} strides,
+// so they can land at an offset inside a larger joint-sequence buffer.
+namespace qf2 {
+namespace rope {
+
+struct QkvDst {
+  __nv_bfloat16* p[3];
+  int64_t sb[3], ss[3], sh[3];
+};
+
+// 16 lanes per head row (8 elements each), 16 head rows per 256-thread CTA pass
+__global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld,
+                                                            int64_t rows, int64_t L, int H, QkvDst dst,
+                                                            const __nv_bfloat16* __restrict__ qw,
+                                                            const __nv_bfloat16* __restrict__ kw, float eps,
+                                                            const float2* __restrict__ freqs, int64_t fb, int64_t fs) {
+  constexpr int D = 128;
+  const int sub = threadIdx.x & 15, grp = threadIdx.x >> 4;
+  const int64_t units = rows * 3 * H;
+  // the loop bound is CTA-uniform so both 16-lane groups of a warp always reach the
+  // shuffles together; out-of-range groups compute on zeros and store nothing
+  for (int64_t base = (int64_t)blockIdx.x * 16; base < units; base += (int64_t)gridDim.x * 16) {
+    const int64_t u = base + grp;
+    const bool valid = u < units;
+    const int64_t row = valid ? u / (3 * H) : 0;
+    const int hr = valid ? (int)(u % (3 * H)) : 0;
+    const int kind = hr / H, head = hr % H;
+    const int64_t b = row / L, s = row % L;
+    const uint4 raw = valid ? *reinterpret_cast<const uint4*>(qkv + row * ld + (int64_t)hr * D + sub * 8)
+                            : make_uint4(0, 0, 0, 0);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float x[8];
+    float ss_ = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] = __bfloat162float(e[j]);
+      ss_ = fmaf(x[j], x[j], ss_);
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss_ += __shfl_xor_sync(0xffffffffu, ss_, o, 16);
+    if (!valid) continue;
+    uint4 outv = raw;
+    if (kind != 2) {
+      const float r = __frsqrt_rn(ss_ / (float)D + eps);
+      const __nv_bfloat16* w = (kind == 0 ? qw : kw) + sub * 8;
+      const float2* f = freqs + b * fb + s * fs + sub * 4;
+      uint32_t* op = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const float x0 = x[2 * p] * r * __bfloat162float(w[2 * p]);
+        const float x1 = x[2 * p + 1] * r * __bfloat162float(w[2 * p + 1]);
+        const float2 cs = __ldg(f + p);
+        const float re = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+        const float im = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+        __nv_bfloat162 t = __floats2bfloat162_rn(re, im);
+        op[p] = *reinterpret_cast<uint32_t*>(&t);
+      }
+    }
+    __nv_bfloat16* d = dst.p[kind] + b * dst.sb[kind] + s * dst.ss[kind] + (int64_t)head * dst.sh[kind] + sub * 8;
+    *reinterpret_cast<uint4*>(d) = outv;
+  }
+}
+
+}  // namespace rope
+}  // namespace qf2
+
+extern "C" int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_t L, int64_t H, int64_t D,
+                                 void* q_out, const int64_t* q_strides, void* k_out, const int64_t* k_strides,
+                                 void* v_out, const int64_t* v_strides, const void* q_weight, const void* k_weight,
+                                 float eps, const void* freqs_cis, const int64_t* freqs_strides, qf2_stream_t stream) {
+  using namespace qf2::rope;
+  if (!qkv || !q_out || !k_out || !v_out || !q_strides || !k_strides || !v_strides || !q_weight || !k_weight ||
+      !freqs_cis || !freqs_strides)
+    return QF2_ERR_ARG;
+  if (D != 128 || B <= 0 || L <= 0 || H <= 0) return QF2_ERR_SHAPE;
+  if (qkv_row_stride < 3 * H * D || qkv_row_stride % 8) return QF2_ERR_ALIGN;
+  const void* ps[4] = {qkv, q_out, k_out, v_out};
+  for (const void* p : ps)
+    if (!al(p, 16)) return QF2_ERR_ALIGN;
+  if (!al(q_weight, 16) || !al(k_weight, 16) || !al(freqs_cis, 16)) return QF2_ERR_ALIGN;
+  QkvDst dst;
+  const int64_t* st[3] = {q_strides, k_strides, v_strides};
+  void* outs[3] = {q_out, k_out, v_out};
+  for (int i = 0; i < 3; ++i) {
+    dst.p[i] = reinterpret_cast<__nv_bfloat16*>(outs[i]);
+    dst.sb[i] = st[i][0]; dst.ss[i] = st[i][1]; dst.sh[i] = st[i][2];
+    if ((dst.sb[i] % 8) || (dst.ss[i] % 8) || (dst.sh[i] % 8)) return QF2_ERR_ALIGN;
+  }
+  if (freqs_strides[0] % 2 || freqs_strides[1] % 2) return QF2_ERR_ALIGN;
+  const int64_t rows = B * L;
+  const int64_t units = rows * 3 * H;
+  int64_t blocks = (units + 15) / 16;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  qkv_norm_rope_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, rows, L, (int)H, dst,
+      reinterpret_cast<const __nv_bfloat16*>(q_weight), reinterpret_cast<const __nv_bfloat16*>(k_weight), eps,
+      reinterpret_cast<const float2*>(freqs_cis), freqs_strides[0], freqs_strides[1]);
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}

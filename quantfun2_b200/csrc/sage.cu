@@ -816,8 +816,8 @@ static int launch_attn(const Args& a) {
   P.out_bf16 = a.dtype == QF2_BF16;
   const int64_t mqt = (a.max_q + kTile - 1) / kTile;
   if (mqt == 0) return QF2_OK;
-  QF2_CUDA_CHECK(
-      cudaFuncSetAttribute(sage_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::alloc));
+  static std::atomic<uint64_t> attr_done{0};
+  QF2_CUDA_CHECK(qf2_set_smem_once(sage_attn_kernel, AttnSmem::alloc, &attr_done));
   sage_attn_kernel<<<dim3((unsigned)((mqt + 1) / 2), (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads,
                      AttnSmem::alloc, a.stream>>>(P);
   QF2_LAUNCH_CHECK();

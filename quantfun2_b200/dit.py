@@ -24,7 +24,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from .attention import sageattn
-from .kernels import rmsnorm_apply, rope_apply_
+from .kernels import qkv_norm_rope, rmsnorm_apply, rope_apply_
 from .quant import QLinear, quantize_rows
 
 
@@ -123,7 +123,9 @@ def qk_norm_rope(qkv: torch.Tensor, H: int, D: int, qn: torch.Tensor, kn: torch.
 
 # ---------------------------------------------------------------- Flux ------
 class FluxDoubleBlock(nn.Module):
-    """src/models/flux/mmdit.py:62-166 (img and txt streams, joint attention)."""
+    """src/models/flux/mmdit.py:62-166 (img and txt streams, joint attention).
+    adaLN LayerNorm+modulate is fused with the activation quantizer of the next linear;
+    GELU and the gated residual adds run in the GEMM epilogues."""
 
     def __init__(self, dim, heads, mlp_ratio, mode, device, gen=None):
         super().__init__()
@@ -138,48 +140,69 @@ class FluxDoubleBlock(nn.Module):
         ones = torch.ones(self.hd, device=device, dtype=torch.bfloat16)
         self.norms = [ones.clone() for _ in range(4)]  # img q, img k, txt q, txt k RMSNorm weights
 
+    def _pre(self, x, mod, qkv_lin, qn, kn, freqs, q, k, v):
+        """adaLN -> qkv projection -> fused q/k RMSNorm + RoPE into the joint q/k/v buffers."""
+        B, L, D = x.shape
+        a = qkv_lin.prep_ln_modulate(x.view(-1, D), mod[:, 0:D], mod[:, D:2 * D], L)
+        qkv_norm_rope(qkv_lin.run(*a).view(B, L, -1), self.heads, qn, kn, freqs, q, k, v)
+
+    def _post(self, x, attn_out, mod, proj, mlp1, mlp2):
+        B, L, D = x.shape
+        x2 = x.view(-1, D)
+        # x += gate1 * proj(attn); x += gate2 * mlp2(gelu(mlp1(modulate(LN(x), shift2, scale2))))
+        proj.run(*proj.prep(attn_out.reshape(-1, D)), out=x2, residual=x2, gate=mod[:, 2 * D:3 * D], rows_per_gate=L)
+        h = mlp1.run(*mlp1.prep_ln_modulate(x2, mod[:, 3 * D:4 * D], mod[:, 4 * D:5 * D], L), gelu_col0=0)
+        mlp2.run(*mlp2.prep(h), out=x2, residual=x2, gate=mod[:, 5 * D:6 * D], rows_per_gate=L)
+        return x
+
     def forward(self, img, txt, vec, freqs, sp: SeqParallel, txt_local: int):
         B = img.shape[0]
-        im = self.img_mod(F.silu(vec)).unsqueeze(1).chunk(6, dim=-1)
-        tm = self.txt_mod(F.silu(vec)).unsqueeze(1).chunk(6, dim=-1)
-        iq, ik, iv = qk_norm_rope(self.img_qkv(modulate(layer_norm(img), im[0], im[1])), self.heads, self.hd,
-                                  self.norms[0], self.norms[1], freqs[:, txt_local:])
-        tq, tk, tv = qk_norm_rope(self.txt_qkv(modulate(layer_norm(txt), tm[0], tm[1])), self.heads, self.hd,
-                                  self.norms[2], self.norms[3], freqs[:, :txt_local])
-        q, k, v = torch.cat([tq, iq], 1), torch.cat([tk, ik], 1), torch.cat([tv, iv], 1)
+        sv = F.silu(vec)
+        im, tm = self.img_mod(sv), self.txt_mod(sv)  # [B, 6 * dim]
+        T = txt_local
+        L = T + img.shape[1]
+        q, k, v = (torch.empty(B, L, self.heads, self.hd, dtype=torch.bfloat16, device=img.device) for _ in range(3))
+        self._pre(txt, tm, self.txt_qkv, self.norms[2], self.norms[3], freqs[:, :T], q[:, :T], k[:, :T], v[:, :T])
+        self._pre(img, im, self.img_qkv, self.norms[0], self.norms[1], freqs[:, T:], q[:, T:], k[:, T:], v[:, T:])
         a = ulysses_attention(q, k, v, sp).reshape(B, -1, self.dim)
-        ta, ia = a[:, :txt_local], a[:, txt_local:]
-        img = torch.addcmul(img, im[2], self.img_proj(ia))
-        img = torch.addcmul(img, im[5], self.img_mlp2(F.gelu(self.img_mlp1(modulate(layer_norm(img), im[3], im[4])),
-                                                             approximate="tanh")))
-        txt = torch.addcmul(txt, tm[2], self.txt_proj(ta))
-        txt = torch.addcmul(txt, tm[5], self.txt_mlp2(F.gelu(self.txt_mlp1(modulate(layer_norm(txt), tm[3], tm[4])),
-                                                             approximate="tanh")))
+        img = self._post(img, a[:, txt_local:], im, self.img_proj, self.img_mlp1, self.img_mlp2)
+        txt = self._post(txt, a[:, :txt_local], tm, self.txt_proj, self.txt_mlp1, self.txt_mlp2)
         return img, txt
 
 
 class FluxSingleBlock(nn.Module):
-    """src/models/flux/mmdit.py:169-231 (fused qkv + MLP input, fused output)."""
+    """src/models/flux/mmdit.py:169-231 (fused qkv + MLP input, fused output).  linear_1 is
+    held as its qkv and MLP row blocks; the MLP block writes GELU(.) and the attention writes
+    its output straight into the two column ranges of linear_2's input, so no concat runs."""
 
     def __init__(self, dim, heads, mlp_ratio, mode, device, gen=None):
         super().__init__()
         self.dim, self.heads, self.hd = dim, heads, dim // heads
         self.mlp = int(dim * mlp_ratio)
         self.mod = random_qlinear(dim, 3 * dim, mode, device, gen=gen)
-        self.linear1 = random_qlinear(dim, 3 * dim + self.mlp, mode, device, gen=gen)
+        self.linear1_qkv = random_qlinear(dim, 3 * dim, mode, device, gen=gen)
+        self.linear1_mlp = random_qlinear(dim, self.mlp, mode, device, gen=gen)
         self.linear2 = random_qlinear(dim + self.mlp, dim, mode, device, gen=gen)
         self.qn = torch.ones(self.hd, device=device, dtype=torch.bfloat16)
         self.kn = torch.ones(self.hd, device=device, dtype=torch.bfloat16)
 
     def forward(self, x, vec, freqs, sp: SeqParallel):
-        B, L, _ = x.shape
-        shift, scale, gate = self.mod(F.silu(vec)).unsqueeze(1).chunk(3, dim=-1)
-        h = self.linear1(modulate(layer_norm(x), shift, scale))
-        qkv, mlp = h.split([3 * self.dim, self.mlp], dim=-1)
-        q, k, v = qk_norm_rope(qkv, self.heads, self.hd, self.qn, self.kn, freqs)
-        a = ulysses_attention(q, k, v, sp).reshape(B, L, self.dim)
-        out = self.linear2(torch.cat([a, F.gelu(mlp, approximate="tanh")], dim=-1))
-        return torch.addcmul(x, gate, out)
+        B, L, D = x.shape
+        x2 = x.view(-1, D)
+        mod = self.mod(F.silu(vec))  # [B, 3 * dim]: shift, scale, gate
+        a = self.linear1_qkv.prep_ln_modulate(x2, mod[:, 0:D], mod[:, D:2 * D], L)
+        qkv = self.linear1_qkv.run(*a)
+        cat = torch.empty(B * L, D + self.mlp, dtype=torch.bfloat16, device=x.device)
+        self.linear1_mlp.run(*a, out=cat[:, D:], gelu_col0=0)
+        q, k, v = (torch.empty(B, L, self.heads, self.hd, dtype=torch.bfloat16, device=x.device) for _ in range(3))
+        qkv_norm_rope(qkv.view(B, L, -1), self.heads, self.qn, self.kn, freqs, q, k, v)
+        attn_view = cat[:, :D].view(B, L, self.heads, self.hd)
+        if sp.world == 1:
+            sageattn(q, k, v, tensor_layout="NHD", out=attn_view)
+        else:
+            attn_view.copy_(ulysses_attention(q, k, v, sp))
+        self.linear2.run(*self.linear2.prep(cat), out=x2, residual=x2, gate=mod[:, 2 * D:3 * D], rows_per_gate=L)
+        return x
 
 
 class FluxDiT(nn.Module):
@@ -214,13 +237,13 @@ class FluxDiT(nn.Module):
         """img/txt: this rank's shard of the image and text tokens (txt first in the joint
         sequence); freqs: complex RoPE factors of the rank's joint-sequence shard."""
         sp = sp or SeqParallel()
-        img, txt = self.img_in(img), self.txt_in(txt)
+        img, txt = self.img_in(img).contiguous(), self.txt_in(txt).contiguous()
         vec = self.time_in2(F.silu(self.time_in1(self.timestep_embedding(t))))
         vec = vec + self.vec_in2(F.silu(self.vec_in1(y)))
         txt_local = txt.shape[1]
         for blk in self.double_blocks:
             img, txt = blk(img, txt, vec, freqs, sp, txt_local)
-        x = torch.cat([txt, img], dim=1)
+        x = torch.cat([txt, img], dim=1).contiguous()
         for blk in self.single_blocks:
             x = blk(x, vec, freqs, sp)
         img = x[:, txt_local:]

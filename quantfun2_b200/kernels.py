@@ -29,6 +29,7 @@ __all__ = [
     "rmsnorm_apply",
     "inplace_softmax",
     "topk_attn",
+    "qkv_norm_rope",
     "QF2Error",
 ]
 
@@ -180,3 +181,22 @@ def topk_attn(xq, xk, xv, mask, fn, HEAD_DIM, scale=None, TOP_K=256, POS_DICT=No
         POS_DICT = block_topk_select(xq, xk, keep, tensor_layout="NHD")
     out = blocksparse_attn(xq, xk, xv, POS_DICT, sm_scale=scale, tensor_layout="NHD")
     return out, POS_DICT
+
+
+def qkv_norm_rope(qkv: torch.Tensor, H: int, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                  freqs_cis: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
+                  eps: float = 1e-6) -> None:
+    """Fused per-head RMSNorm of q and k, RoPE of q and k, copy of v.
+    qkv [B, L, 3*H*128] bf16 -> q_out / k_out / v_out [B, L, H, 128] views (any strides
+    with 16-byte rows, e.g. slices of a joint txt+img buffer)."""
+    require_device(qkv)
+    B, L, _ = qkv.shape
+    q2 = qkv.reshape(B * L, -1)
+    if q2.stride(-1) != 1:
+        q2 = q2.contiguous()
+    fc, fs = _freqs_view(freqs_cis.to(qkv.device), B, L, 64)
+    st = lambda t: i64(t.stride(0), t.stride(1), t.stride(2))  # noqa: E731
+    check(_lib.load().qf2_qkv_norm_rope(
+        q2.data_ptr(), q2.stride(0), B, L, H, 128, q_out.data_ptr(), st(q_out), k_out.data_ptr(), st(k_out),
+        v_out.data_ptr(), st(v_out), q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(), float(eps),
+        fc.data_ptr(), i64(*fs), stream_ptr(qkv.device)), "qf2_qkv_norm_rope")

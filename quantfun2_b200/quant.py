@@ -26,7 +26,7 @@ from . import _lib
 from ._lib import QF2Error, check, require_device, stream_ptr
 
 __all__ = ["qdtype", "QLinear", "qint8", "qfloat8", "qfloat8_w8a8", "quantize_model", "linear_inserter",
-           "quantize_rows", "codes_to_bf16", "gemm"]
+           "quantize_rows", "codes_to_bf16", "gemm", "ln_modulate"]
 
 
 def _ws(device) -> torch.Tensor:
@@ -59,9 +59,13 @@ def codes_to_bf16(q: torch.Tensor, fmt: str) -> torch.Tensor:
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=None, fp8: bool = False,
-         out_dtype=torch.bfloat16) -> torch.Tensor:
+         out_dtype=torch.bfloat16, out: torch.Tensor | None = None, gelu_col0: int = -1,
+         residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, rows_per_gate: int = 1) -> torch.Tensor:
     """D = (a . b^T) * row_scale[:, None] * col_scale[None, :] + bias on tcgen05.
-    a [M, K], b [N, K]: bf16, or uint8 e4m3 codes with fp8=True."""
+    a [M, K], b [N, K]: bf16, or uint8 e4m3 codes with fp8=True.
+    Fused epilogue: GELU (tanh) on columns >= gelu_col0; D = residual + gate * D when
+    residual is given (gate [rows/rows_per_gate, N] bf16, may be a strided view).  `out`
+    may be a row-strided 2-D view (for instance a column slice of a larger buffer)."""
     require_device(a)
     M, K = a.shape
     N = b.shape[0]
@@ -71,7 +75,14 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
         a = a.contiguous()
     if b.stride(-1) != 1:
         b = b.contiguous()
-    out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    elif out.shape != (M, N) or out.stride(-1) != 1 or out.dtype != out_dtype:
+        raise QF2Error("out must be an [M, N] row-strided view of the output dtype")
+    if residual is not None and (residual.stride(-1) != 1 or residual.dtype != torch.bfloat16):
+        raise QF2Error("residual must be a bf16 row-strided [M, N] view")
+    if gate is not None and (gate.stride(-1) != 1 or gate.dtype != torch.bfloat16):
+        raise QF2Error("gate must be a bf16 row-strided view")
     bias_dt = _lib.QF2_F32
     if bias is not None:
         bias = bias.contiguous()
@@ -79,14 +90,36 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
         if bias.dtype not in (torch.bfloat16, torch.float32):
             bias = bias.float()
     ws = _ws(a.device)
-    check(_lib.load().qf2_gemm(
+    check(_lib.load().qf2_gemm_ex(
         a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), out.data_ptr(), out.stride(0), M, N, K,
         _lib.QF2_E4M3 if fp8 else _lib.QF2_BF16, _lib.QF2_F32 if out_dtype == torch.float32 else _lib.QF2_BF16,
         row_scale.data_ptr() if row_scale is not None else None,
         col_scale.data_ptr() if col_scale is not None else None,
-        bias.data_ptr() if bias is not None else None, bias_dt, ws.data_ptr(), 256, stream_ptr(a.device)),
-        "qf2_gemm")
+        bias.data_ptr() if bias is not None else None, bias_dt, int(gelu_col0),
+        residual.data_ptr() if residual is not None else None, residual.stride(0) if residual is not None else 0,
+        gate.data_ptr() if gate is not None else None, gate.stride(0) if gate is not None else 0,
+        int(rows_per_gate), ws.data_ptr(), 256, stream_ptr(a.device)),
+        "qf2_gemm_ex")
     return out
+
+
+def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_per_batch: int, fmt: str = "bf16",
+                eps: float = 1e-6):
+    """LayerNorm(x) * (1 + scale) + shift over the last dim of x [M, N] (shift/scale
+    [M / rows_per_batch, N] bf16 views).  fmt "bf16" -> bf16 [M, N]; "e4m3" -> (uint8 codes,
+    fp32 per-row scales) ready for the FP8 GEMM."""
+    require_device(x)
+    M, N = x.shape
+    fp8 = fmt == "e4m3"
+    out = torch.empty(M, N, dtype=torch.uint8 if fp8 else torch.bfloat16, device=x.device)
+    scales = torch.empty(M, dtype=torch.float32, device=x.device) if fp8 else None
+    if shift.stride(-1) != 1 or scale.stride(-1) != 1 or shift.stride(0) != scale.stride(0):
+        raise QF2Error("shift and scale must be row-strided views with a common stride")
+    check(_lib.load().qf2_ln_modulate(
+        x.data_ptr(), x.stride(0), _lib.dtype_code(x.dtype), shift.data_ptr(), scale.data_ptr(), shift.stride(0),
+        int(rows_per_batch), M, N, float(eps), out.data_ptr(), N, _lib.QF2_E4M3 if fp8 else _lib.QF2_BF16,
+        scales.data_ptr() if fp8 else None, stream_ptr(x.device)), "qf2_ln_modulate")
+    return (out, scales) if fp8 else out
 
 
 class QLinear(nn.Module):
@@ -112,17 +145,34 @@ class QLinear(nn.Module):
         bias = None if lin.bias is None else lin.bias.detach().to(w.device, torch.bfloat16)
         return cls(codes, scale, bias, mode, lin.in_features, lin.out_features)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        shape = x.shape
-        x2 = x.reshape(-1, shape[-1])
+    @property
+    def fp8_activations(self) -> bool:
+        return self.mode == "fp8_w8a8"
+
+    def prep(self, x2: torch.Tensor):
+        """Activation operand for this linear: (e4m3 codes, per-row scales) or (bf16, None)."""
         if x2.dtype != torch.bfloat16:
             x2 = x2.to(torch.bfloat16)
-        if self.mode == "fp8_w8a8":
-            xq, xs = quantize_rows(x2, "e4m3")
-            y = gemm(xq, self.codes, row_scale=xs, col_scale=self.scale, bias=self.bias, fp8=True)
-        else:
-            wb = codes_to_bf16(self.codes, "int8" if self.mode == "int8" else "e4m3")
-            y = gemm(x2, wb, col_scale=self.scale, bias=self.bias)
+        if self.fp8_activations:
+            return quantize_rows(x2, "e4m3")
+        return x2, None
+
+    def prep_ln_modulate(self, x2, shift, scale, rows_per_batch):
+        """Fused LayerNorm + modulate producing this linear's activation operand."""
+        if self.fp8_activations:
+            return ln_modulate(x2, shift, scale, rows_per_batch, "e4m3")
+        return ln_modulate(x2, shift, scale, rows_per_batch, "bf16"), None
+
+    def run(self, a: torch.Tensor, row_scale, **epilogue) -> torch.Tensor:
+        """GEMM on a prepared operand; epilogue kwargs as in `gemm` (out, gelu_col0, residual, gate...)."""
+        if self.fp8_activations:
+            return gemm(a, self.codes, row_scale=row_scale, col_scale=self.scale, bias=self.bias, fp8=True, **epilogue)
+        wb = codes_to_bf16(self.codes, "int8" if self.mode == "int8" else "e4m3")
+        return gemm(a, wb, col_scale=self.scale, bias=self.bias, **epilogue)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        y = self.run(*self.prep(x.reshape(-1, shape[-1])))
         return y.reshape(*shape[:-1], self.out_features)
 
     def extra_repr(self) -> str:

@@ -58,8 +58,8 @@ def ref_forward(m, img, txt, t, y, freqs):
     x = torch.cat([txt, img], 1)
     for b in m.single_blocks:
         s, c, g = lin(b.mod, F.silu(vec)).unsqueeze(1).chunk(3, -1)
-        h = lin(b.linear1, mod(ln(x), s, c))
-        qkv, mlp = h.split([3 * b.dim, b.mlp], -1)
+        xm = mod(ln(x), s, c)
+        qkv, mlp = lin(b.linear1_qkv, xm), lin(b.linear1_mlp, xm)
         a = attn(qkv, b.heads, b.hd).reshape(x.shape[0], -1, b.dim)
         x = x + g * lin(b.linear2, torch.cat([a, F.gelu(mlp, approximate="tanh")], -1))
     img = x[:, T:]

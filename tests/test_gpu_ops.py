@@ -132,3 +132,30 @@ def test_softmax_golden_and_long_rows(cuda, golden):
     r = ops.softmax_lastdim(z.numpy())
     out = inplace_softmax(z.to(cuda)).cpu().numpy()
     np.testing.assert_allclose(out, r, rtol=1e-5, atol=1e-9)
+
+
+def test_qkv_norm_rope_fused(cuda):
+    """Fused q/k RMSNorm + RoPE + v copy into offset views of joint buffers."""
+    from quantfun2_b200.kernels import qkv_norm_rope
+
+    g = torch.Generator().manual_seed(8)
+    B, L, H, D, off = 2, 70, 3, 128, 5
+    qkv = (torch.randn(B, L, 3 * H * D, generator=g) * 2).bfloat16()
+    qw = (torch.rand(D, generator=g) + 0.5).bfloat16()
+    kw = (torch.rand(D, generator=g) + 0.5).bfloat16()
+    ang = torch.rand(B, L, D // 2, generator=g) * 6
+    f = torch.polar(torch.ones_like(ang), ang)
+    q, k, v = (torch.zeros(B, L + off, H, D, dtype=torch.bfloat16, device=cuda) for _ in range(3))
+    qkv_norm_rope(qkv.to(cuda), H, qw.to(cuda), kw.to(cuda), f.to(cuda), q[:, off:], k[:, off:], v[:, off:])
+    x = qkv.float().view(B, L, 3, H, D)
+
+    def ref(t, w):
+        n = t.double() * torch.rsqrt(t.double().pow(2).mean(-1, keepdim=True) + 1e-6) * w.double()
+        c = torch.view_as_complex(n.reshape(B, L, H, D // 2, 2).contiguous()) * f.to(torch.complex128)[:, :, None]
+        return torch.view_as_real(c).reshape(B, L, H, D)
+
+    for got, want in ((q, ref(x[:, :, 0], qw)), (k, ref(x[:, :, 1], kw))):
+        err = (got[:, off:].float().cpu().double() - want).abs().max().item()
+        assert err < 0.02 * want.abs().max().item()
+        assert not got[:, :off].any()
+    assert torch.equal(v[:, off:].cpu(), qkv.view(B, L, 3, H, D)[:, :, 2])

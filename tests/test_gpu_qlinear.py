@@ -102,3 +102,43 @@ def test_quantize_model_swaps_linears(cuda):
     y = qm(x.to(cuda).bfloat16()).float().cpu()
     cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
     assert cos > 0.999
+
+
+def test_gemm_fused_gelu_residual_gate(cuda):
+    from quantfun2_b200.quant import gemm
+
+    g = torch.Generator(device=cuda).manual_seed(3)
+    M, N, K, L = 300, 512, 256, 150   # two "batches" of 150 rows for the gate
+    a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    b = torch.randn(N, K, device=cuda, generator=g).bfloat16()
+    res = torch.randn(M, N, device=cuda, generator=g).bfloat16()
+    gate_full = torch.randn(2, 3 * N, device=cuda, generator=g).bfloat16()
+    gate = gate_full[:, N:2 * N]                       # strided view, as the DiT blocks pass it
+    y = (a.double() @ b.double().T)
+    y = torch.where(torch.arange(N, device=cuda) >= 100, torch.nn.functional.gelu(y, approximate="tanh"), y)
+    ref = res.double() + gate.double().repeat_interleave(L, 0) * y
+    out = res.clone()
+    gemm(a, b, gelu_col0=100, residual=out, gate=gate, rows_per_gate=L, out=out)   # in place
+    assert rel_err(out.float().cpu(), ref.cpu()) < 8e-3
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+def test_ln_modulate(cuda, fmt):
+    from quantfun2_b200.quant import ln_modulate
+
+    g = torch.Generator(device=cuda).manual_seed(4)
+    B, L, N = 2, 100, 3072
+    x = (torch.randn(B * L, N, device=cuda, generator=g) * 3 + 1).bfloat16()
+    mod = torch.randn(B, 6 * N, device=cuda, generator=g).bfloat16()
+    shift, scale = mod[:, N:2 * N], mod[:, 4 * N:5 * N]
+    ref = torch.nn.functional.layer_norm(x.double(), (N,), eps=1e-6)
+    ref = ref * (1 + scale.double().repeat_interleave(L, 0)) + shift.double().repeat_interleave(L, 0)
+    out = ln_modulate(x, shift, scale, L, fmt)
+    if fmt == "bf16":
+        assert rel_err(out.float().cpu(), ref.cpu()) < 8e-3
+    else:
+        codes, s = out
+        got = torch.from_numpy(e4m3_bits_to_f32(codes.cpu().numpy())) * s.cpu()[:, None]
+        assert rel_err(got, ref.cpu()) < 0.07
+        am = ref.abs().amax(1).cpu()
+        assert torch.allclose(s.cpu().double(), am / 448, rtol=1e-3)
