@@ -53,6 +53,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-flux", action="store_true")
+    p.add_argument("--no-lumina", action="store_true")
     return p.parse_args()
 
 
@@ -203,6 +204,23 @@ def run_flux_step(rank: int, world: int, dev, warmup: int = 2, steps: int = 5) -
     tl, il = T // world, I // world
     img_l, txt_l = img[:, rank * il:(rank + 1) * il].contiguous(), txt[:, rank * tl:(rank + 1) * tl].contiguous()
     f_l = torch.cat([freqs[:, rank * tl:(rank + 1) * tl], freqs[:, T + rank * il:T + (rank + 1) * il]], 1).contiguous()
+    fwd = lambda: model(img_l, txt_l, t, y, f_l, sp)  # noqa: E731
+    r = _time_forward(fwd, world, dev, warmup, steps)
+    del model
+    torch.cuda.empty_cache()
+    fl = flux_step_flops(T + I)
+    sec = r.pop("sec")
+    res = {"ms_per_step": sec * 1e3, "tflops": fl / sec / 1e12, "flops_per_step": fl, "tokens": T + I, **r,
+           "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU",
+           "linears": "FP8 e4m3 W8A8 (per-token activation, per-channel weight scales)",
+           "attention": "Sage INT8 QK / FP8 PV"}
+    return res
+
+
+def _time_forward(fwd, world: int, dev, warmup: int, steps: int) -> dict:
+    """Warm up, time `steps` eager forwards, then capture one forward as a CUDA graph and
+    time its replays (CUDA events on the launching stream; max over ranks)."""
+
     def timed(fn):
         if world > 1:
             torch.distributed.barrier()
@@ -220,13 +238,13 @@ def run_flux_step(rank: int, world: int, dev, warmup: int = 2, steps: int = 5) -
             sec = float(tt[0])
         return sec
 
-    fwd = lambda: model(img_l, txt_l, t, y, f_l, sp)  # noqa: E731
+    graph_error = None
     with torch.inference_mode():
         for _ in range(warmup):
             fwd()
         eager = timed(fwd)
-        # the whole step as one CUDA graph: the ~2000 launches of a step replay without
-        # host-side launch cost (the step is otherwise bound by Python/launch overhead)
+        # the whole step as one CUDA graph: the thousands of launches of a step replay
+        # without host-side launch cost
         graph, sec, out = None, eager, None
         try:
             side = torch.cuda.Stream()
@@ -245,18 +263,39 @@ def run_flux_step(rank: int, world: int, dev, warmup: int = 2, steps: int = 5) -
             out = fwd()
             graph_error = f"{type(e).__name__}: {e}"[:200]
         finite = bool(torch.isfinite(out.float()).all())
-    res_graph = graph is not None
-    del graph, model
-    torch.cuda.empty_cache()
-    fl = flux_step_flops(T + I)
-    res = {"ms_per_step": sec * 1e3, "tflops": fl / sec / 1e12, "flops_per_step": fl, "tokens": T + I,
-           "steps": steps, "warmup": warmup, "cuda_graph": res_graph, "eager_ms_per_step": eager * 1e3,
-           "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU",
-           "linears": "FP8 e4m3 W8A8 (per-token activation, per-channel weight scales)",
-           "attention": "Sage INT8 QK / FP8 PV", "output_finite": finite}
-    if not res_graph:
+    res = {"sec": sec, "steps": steps, "warmup": warmup, "cuda_graph": graph is not None,
+           "eager_ms_per_step": eager * 1e3, "output_finite": finite}
+    if graph_error:
         res["graph_error"] = graph_error
+    del graph
     return res
+
+
+def run_lumina_step(rank: int, world: int, dev, batch: int = 1, warmup: int = 2, steps: int = 5) -> dict:
+    """One Lumina-Image-2.0-2B-shaped forward (26 layers + 2 + 2 refiners, dim 2304, 24 / 8
+    heads of 96, SwiGLU 6144, 4096 img + 256 caption tokens, INT8 weight-only linears, Sage
+    attention) on `batch` samples per rank.  Ranks are batch-parallel: each denoises its own
+    samples, no collective in the step."""
+    from quantfun2_b200.lumina import LuminaDiT, lumina_step_flops
+
+    Lc, side = 256, 64
+    Li = side * side
+    model = LuminaDiT(device=dev, seed=0)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)  # each rank its own samples
+    img = torch.randn(batch, Li, 64, device=dev, generator=g).bfloat16()
+    cap = torch.randn(batch, Lc, 2304, device=dev, generator=g).bfloat16()
+    t = torch.rand(batch, device=dev, generator=g)
+    freqs = model.make_freqs(batch, Lc, side, side, dev)
+    r = _time_forward(lambda: model(img, t, cap, freqs), world, dev, warmup, steps)
+    del model
+    torch.cuda.empty_cache()
+    fl = lumina_step_flops(batch)
+    sec = r.pop("sec")
+    return {"ms_per_step": sec * 1e3, "tflops_per_gpu": fl / sec / 1e12, "flops_per_step_per_gpu": fl,
+            "batch_per_gpu": batch, "global_batch": batch * world, "samples_per_s": batch * world / sec,
+            "tokens": Lc + Li, **r, "parallelism": f"batch-parallel dp{world}" if world > 1 else "single GPU",
+            "linears": "INT8 weight-only (per-channel scales), bf16 activations",
+            "attention": "Sage INT8 QK / FP8 PV, GQA 24/8, head_dim 96 zero-padded to 128"}
 
 
 def run_ours(args, rank: int, world: int, dev):
@@ -362,6 +401,16 @@ def run_ours(args, rank: int, world: int, dev):
         del q, k, v, out, ws
         torch.cuda.empty_cache()
         flux = run_flux_step(rank, world, dev)
+    # ---- the Lumina-shaped denoise step (batch-parallel: one sample per rank; on one GPU
+    # also the 8-sample batch)
+    lumina = None
+    if not args.no_lumina:
+        if flux is None:
+            del q, k, v, out, ws
+            torch.cuda.empty_cache()
+        lumina = {"b1_per_gpu": run_lumina_step(rank, world, dev, batch=1)}
+        if world == 1:
+            lumina["b8_single_gpu"] = run_lumina_step(rank, world, dev, batch=8, warmup=1, steps=3)
 
     if rank != 0:
         return
@@ -403,6 +452,7 @@ def run_ours(args, rank: int, world: int, dev):
         "gpu_launches": 4 * args.steps,
         "clocks": clocks,
         "flux_step": flux,
+        "lumina_step": lumina,
     }
     print(json.dumps(line), flush=True)
 

@@ -80,14 +80,17 @@ int qf2_rope_apply(const void* xq, void* xq_out, int64_t Hq, const int64_t* xq_s
 
 /* Fused per-head q/k RMSNorm + RoPE on a fused QKV projection output, replacing the
  * q_norm / k_norm + rope_apply sequence of the attention blocks (src/models/flux/mmdit.py
- * :133-149, src/models/common/attn.py:209-212): qkv [B*L, 3*H*D] bf16 (row stride
- * qkv_row_stride); q and k rows -> x * rsqrt(mean(x^2) + eps) * w, rotated by
- * freqs_cis[b, s] (complex64, strides {batch, seq} in complex elements), rounded once;
- * v copied.  Outputs through {batch, seq, head} element strides.  D = 128, bf16. */
-int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_t L, int64_t H, int64_t D,
-                      void* q_out, const int64_t* q_strides, void* k_out, const int64_t* k_strides, void* v_out,
-                      const int64_t* v_strides, const void* q_weight, const void* k_weight, float eps,
-                      const void* freqs_cis, const int64_t* freqs_strides, qf2_stream_t stream);
+ * :133-149, src/models/common/attn.py:209-212): qkv [B*L, (Hq + 2*Hkv)*D] bf16 (q heads,
+ * k heads, v heads; row stride qkv_row_stride); q and k rows -> x * rsqrt(mean(x^2) +
+ * eps) * w, rotated by freqs_cis[b, s] (complex64, strides {batch, seq} in complex
+ * elements), rounded once; v copied.  Outputs through {batch, seq, head} element
+ * strides with head dim Dout >= D (extra columns written as zero, e.g. head_dim 96
+ * padded to the attention kernel's 128).  D, Dout multiples of 8, <= 128; bf16. */
+int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_t L, int64_t Hq, int64_t Hkv,
+                      int64_t D, int64_t Dout, void* q_out, const int64_t* q_strides, void* k_out,
+                      const int64_t* k_strides, void* v_out, const int64_t* v_strides, const void* q_weight,
+                      const void* k_weight, float eps, const void* freqs_cis, const int64_t* freqs_strides,
+                      qf2_stream_t stream);
 
 /* ------------------------------------------------------------- RMSNorm --
  * Replaces rmsnorm_apply (src/kernels/__init__.py:73-80) and the Triton
@@ -103,6 +106,18 @@ int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_
 int qf2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, const void* weight, int w_dtype, void* out,
                 int64_t out_row_stride, int out_dtype, int64_t M, int64_t N, float eps, int mode,
                 qf2_stream_t stream);
+
+/* Gated residual + RMSNorm-modulate of the Lumina joint block (src/models/lumina/image_two/
+ * model.py:82-101), one pass over rows of `dim` bf16 (dim a multiple of 256, <= 4096;
+ * contiguous rows; batch b = row / rows_per_batch):
+ *   if y:  x = bf16(x + g * RMSNorm(y; w_post, eps_post))   g = tanh(gate[b]) when
+ *          gate_tanh, gate[b] otherwise, 1 without gate; w_post NULL = no norm on y
+ *   if h:  h = bf16(RMSNorm(x; w_pre, eps_pre) * (1 + scale[b]))   (scale NULL = 0)
+ * gate / scale rows are gate_stride / scale_stride elements apart. */
+int qf2_rms_gate_residual(const void* y, void* x, void* h, int64_t rows, int64_t dim, int64_t rows_per_batch,
+                          const void* w_post, float eps_post, const void* gate, int64_t gate_stride, int gate_tanh,
+                          const void* w_pre, float eps_pre, const void* scale, int64_t scale_stride,
+                          qf2_stream_t stream);
 
 /* ------------------------------------------------------------- softmax --
  * Replaces inplace_softmax (src/kernels/__init__.py:83-87) and
@@ -217,10 +232,13 @@ int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, in
  * y = (A . B^T) * row_scale * col_scale + bias;  y = gelu_tanh(y) on columns >= gelu_col0
  * (gelu_col0 < 0: none);  D = residual + gate[m / rows_per_gate][n] * y when residual is
  * non-NULL (bf16, row stride ldr; gate bf16 with row stride gate_stride, NULL = 1).
- * D may alias residual. */
+ * D may alias residual.  glu != 0 fuses the SwiGLU of src/models/common/nextdit.py:124-125:
+ * B's rows come in groups of 256 = [128 rows of w1 | the matching 128 rows of w3], and
+ * D[m, 128 j + i] = silu(y[m, 256 j + i]) * y[m, 256 j + 128 + i] (N % 256 == 0, D has
+ * N / 2 bf16 columns, no residual, no GELU). */
 int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M, int64_t N,
                 int64_t K, int ab_dtype, int d_dtype, const float* row_scale, const float* col_scale,
-                const void* bias, int bias_dtype, int64_t gelu_col0, const void* residual, int64_t ldr,
+                const void* bias, int bias_dtype, int64_t gelu_col0, int glu, const void* residual, int64_t ldr,
                 const void* gate, int64_t gate_stride, int64_t rows_per_gate, void* workspace,
                 int64_t workspace_bytes, qf2_stream_t stream);
 /* Fused adaLN input (src/models/flux/mmdit.py:127-128, src/models/common/utilities.py:4-5):

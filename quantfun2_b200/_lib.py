@@ -33,10 +33,15 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_int64, _P64, _P64, c_void_p, c_void_p, c_int64, _P64, _P64, c_void_p, _P64,
          c_int64, c_int64, c_int64, c_int, c_int, c_void_p],
     ),
+    "qf2_rms_gate_residual": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int,
+         c_void_p, c_float, c_void_p, c_int64, c_void_p],
+    ),
     "qf2_qkv_norm_rope": (
         c_int,
-        [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64,
-         c_void_p, c_void_p, c_float, c_void_p, _P64, c_void_p],
+        [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, _P64, c_void_p, _P64,
+         c_void_p, _P64, c_void_p, c_void_p, c_float, c_void_p, _P64, c_void_p],
     ),
     "qf2_rmsnorm": (
         c_int,
@@ -90,8 +95,8 @@ SIGNATURES = {
     "qf2_gemm_ex": (
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
-         c_void_p, c_void_p, c_void_p, c_int, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p,
-         c_int64, c_void_p],
+         c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64,
+         c_void_p, c_int64, c_void_p],
     ),
     "qf2_ln_modulate": (
         c_int,

@@ -55,6 +55,7 @@ struct Args {
   int64_t ldr;
   const __nv_bfloat16* gate;         // per (row / rows_per_gate, column); null = 1
   int64_t gate_stride, rows_per_gate;
+  int glu;        // SwiGLU: per 256-column tile, [128 gate | 128 up] -> 128 output columns
   int vec_ok;     // scale / bias / residual / gate rows 16-byte aligned: vector loads
   int* status;
 };
@@ -84,6 +85,32 @@ QF2_DEV float gelu_tanh_fast(float x) {
   float t;
   asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
   return 0.5f * x * (1.0f + t);
+}
+
+// SiLU through the SFU tanh: x * sigmoid(x) = 0.5 x (1 + tanh(x / 2))
+QF2_DEV float silu_fast(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return 0.5f * x * (1.0f + t);
+}
+
+// scale + bias of 32 accumulator columns starting at source column n (vector loads)
+QF2_DEV void scale_bias32(const Args& A, int64_t n, float* o) {
+  if (A.col_scale != nullptr) {
+    float cs[32];
+    load_f32x32(A.col_scale + n, cs);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] *= cs[i];
+  }
+  if (A.bias != nullptr) {
+    float bb[32];
+    if (A.bias_f32)
+      load_f32x32(reinterpret_cast<const float*>(A.bias) + n, bb);
+    else
+      load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(A.bias) + n, bb);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] += bb[i];
+  }
 }
 
 
@@ -213,6 +240,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!wwait(acc_full + buf, (uint32_t)((it >> 1) & 1))) { ok = false; break; }
       tc_fence_after();
       const float rs = (A.row_scale != nullptr && m < A.M) ? A.row_scale[m] : 1.0f;
+      if (A.glu) {
+        // output columns (tile_n * 128 + half * 64 + c * 32 ...): gate at accumulator
+        // column half * 64 + c * 32, up 128 columns further (N % 256 == 0, vec_ok)
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t vg[32], vu[32];
+          const int col = half * 64 + c * 32;
+          tmem_ld32(tmem + lane_off + buf * BN + col, vg);
+          tmem_ld32(tmem + lane_off + buf * BN + 128 + col, vu);
+          tmem_wait_ld();
+          if (m >= A.M) continue;
+          const int64_t ns = (tile / mt) * BN + col;
+          float g[32], u[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            g[i] = __uint_as_float(vg[i]) * rs;
+            u[i] = __uint_as_float(vu[i]) * rs;
+          }
+          scale_bias32(A, ns, g);
+          scale_bias32(A, ns + 128, u);
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(A.d) + m * A.ldd + (tile / mt) * (BN / 2) + col;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              __nv_bfloat162 t = __floats2bfloat162_rn(silu_fast(g[i + 2 * j]) * u[i + 2 * j],
+                                                       silu_fast(g[i + 2 * j + 1]) * u[i + 2 * j + 1]);
+              wp[j] = *reinterpret_cast<uint32_t*>(&t);
+            }
+            *reinterpret_cast<uint4*>(dst + i) = w;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + buf);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 64; ++c) {
         uint32_t v[32];
@@ -225,21 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]) * rs;
         const int ncols = (int)min((int64_t)32, A.N - nc);
         if (ncols == 32 && A.vec_ok) {
-          if (A.col_scale != nullptr) {
-            float cs[32];
-            load_f32x32(A.col_scale + nc, cs);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= cs[i];
-          }
-          if (A.bias != nullptr) {
-            float bb[32];
-            if (A.bias_f32)
-              load_f32x32(reinterpret_cast<const float*>(A.bias) + nc, bb);
-            else
-              load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(A.bias) + nc, bb);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] += bb[i];
-          }
+          scale_bias32(A, nc, o);
           if (nc + 32 > A.gelu_col0) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
@@ -331,7 +383,7 @@ using namespace qf2::gemm;
 
 extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M,
                            int64_t N, int64_t K, int ab_dtype, int d_dtype, const float* row_scale,
-                           const float* col_scale, const void* bias, int bias_dtype, int64_t gelu_col0,
+                           const float* col_scale, const void* bias, int bias_dtype, int64_t gelu_col0, int glu,
                            const void* residual, int64_t ldr, const void* gate, int64_t gate_stride,
                            int64_t rows_per_gate, void* workspace, int64_t workspace_bytes, qf2_stream_t stream) {
   if (!a || !b || !d) return QF2_ERR_ARG;
@@ -340,9 +392,10 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
   if (bias && bias_dtype != QF2_BF16 && bias_dtype != QF2_F32) return QF2_ERR_DTYPE;
   if (M <= 0 || N <= 0 || K <= 0 || (N % 8)) return QF2_ERR_SHAPE;
   if (residual && (ldr < N || (gate && rows_per_gate <= 0))) return QF2_ERR_SHAPE;
+  if (glu && (N % BN || residual || gelu_col0 >= 0 || d_dtype != QF2_BF16)) return QF2_ERR_SHAPE;
   const int esz = ab_dtype == QF2_E4M3 ? 1 : 2;
   if (!al16(a) || !al16(b) || !al16(d) || (lda * esz) % 16 || (ldb * esz) % 16 || (ldd % 8) || lda < K || ldb < K ||
-      ldd < N)
+      ldd < (glu ? N / 2 : N))
     return QF2_ERR_ALIGN;
   if (!workspace || workspace_bytes < 256 || !al16(workspace)) return QF2_ERR_WORKSPACE;
   const CUtensorMapDataType tdt =
@@ -370,8 +423,10 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
   args.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
   args.gate_stride = gate_stride;
   args.rows_per_gate = rows_per_gate > 0 ? rows_per_gate : 1;
+  args.glu = glu != 0;
   args.vec_ok = al16(col_scale) && al16(bias) && al16(residual) && al16(gate) && (ldr % 8) == 0 &&
                 (gate_stride % 8) == 0;
+  if (glu && !args.vec_ok) return QF2_ERR_ALIGN;
   args.status = reinterpret_cast<int*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   QF2_CUDA_CHECK(cudaMemsetAsync(workspace, 0, sizeof(int), s));
@@ -390,6 +445,6 @@ extern "C" int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, 
                         int64_t N, int64_t K, int ab_dtype, int d_dtype, const float* row_scale,
                         const float* col_scale, const void* bias, int bias_dtype, void* workspace,
                         int64_t workspace_bytes, qf2_stream_t stream) {
-  return qf2_gemm_ex(a, lda, b, ldb, d, ldd, M, N, K, ab_dtype, d_dtype, row_scale, col_scale, bias, bias_dtype, -1,
+  return qf2_gemm_ex(a, lda, b, ldb, d, ldd, M, N, K, ab_dtype, d_dtype, row_scale, col_scale, bias, bias_dtype, -1, 0,
                      nullptr, 0, nullptr, 0, 1, workspace, workspace_bytes, stream);
 }

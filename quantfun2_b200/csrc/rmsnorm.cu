@@ -196,3 +196,181 @@ extern "C" int qf2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, con
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }
+
+// ------------------------------------------- gated residual + RMSNorm modulate --
+// The glue of the Lumina joint block (src/models/lumina/image_two/model.py:82-101):
+//   x = x + g * RMSNorm_post(y)          g = tanh(gate[b]) (or gate, or 1)
+//   h = RMSNorm_pre(x) * (1 + scale[b])  (the next linear's input)
+// in one pass: a warp owns a row of NV * 256 bf16 (NV 16-byte vectors per lane), y and x
+// are read once, x is rounded to bf16 once and stored, h is computed from that rounded
+// x (as the reference's next norm sees it) and stored.  Math in fp32.
+namespace qf2 {
+namespace rms {
+
+struct GateResArgs {
+  const __nv_bfloat16* y;
+  __nv_bfloat16* x;
+  __nv_bfloat16* h;
+  int64_t rows, rows_per_batch;
+  const __nv_bfloat16* w_post;
+  float eps_post;
+  const __nv_bfloat16* gate;
+  int64_t gate_stride;
+  int gate_tanh;
+  const __nv_bfloat16* w_pre;
+  float eps_pre;
+  const __nv_bfloat16* scale;
+  int64_t scale_stride;
+};
+
+QF2_DEV void ld8(const __nv_bfloat16* p, float* f) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = __bfloat162float(e[i]);
+}
+
+QF2_DEV void st8(__nv_bfloat16* p, const float* f) {
+  uint4 v;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 t = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&t);
+  }
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+QF2_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) gate_residual_kernel(GateResArgs a) {
+  constexpr int D = NV * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const int64_t b = row / a.rows_per_batch;
+  float xv[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) ld8(a.x + row * D + (i * 32 + lane) * 8, xv[i]);
+  if (a.y != nullptr) {
+    float yv[NV][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      ld8(a.y + row * D + (i * 32 + lane) * 8, yv[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(yv[i][j], yv[i][j], ss);
+    }
+    const float r = a.w_post != nullptr ? __frsqrt_rn(warp_sum(ss) / (float)D + a.eps_post) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      float w[8], g[8];
+      if (a.w_post != nullptr) {
+        ld8(a.w_post + c, w);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = 1.0f;
+      }
+      if (a.gate != nullptr) {
+        ld8(a.gate + b * a.gate_stride + c, g);
+        if (a.gate_tanh) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) g[j] = tanhf(g[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] = 1.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        xv[i][j] = __bfloat162float(__float2bfloat16_rn(fmaf(g[j], yv[i][j] * r * w[j], xv[i][j])));
+      st8(a.x + row * D + c, xv[i]);
+    }
+  }
+  if (a.h != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(xv[i][j], xv[i][j], ss);
+    const float r = __frsqrt_rn(warp_sum(ss) / (float)D + a.eps_pre);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      float w[8], s[8], o[8];
+      if (a.w_pre != nullptr) {
+        ld8(a.w_pre + c, w);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = 1.0f;
+      }
+      if (a.scale != nullptr) {
+        ld8(a.scale + b * a.scale_stride + c, s);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = xv[i][j] * r * w[j] * (1.0f + s[j]);
+      st8(a.h + row * D + c, o);
+    }
+  }
+}
+
+template <int NV>
+static void launch_gate_residual(const GateResArgs& a, cudaStream_t st) {
+  gate_residual_kernel<NV><<<(unsigned)((a.rows + 7) / 8), 256, 0, st>>>(a);
+}
+
+}  // namespace rms
+}  // namespace qf2
+
+extern "C" int qf2_rms_gate_residual(const void* y, void* x, void* h, int64_t rows, int64_t dim,
+                                     int64_t rows_per_batch, const void* w_post, float eps_post, const void* gate,
+                                     int64_t gate_stride, int gate_tanh, const void* w_pre, float eps_pre,
+                                     const void* scale, int64_t scale_stride, qf2_stream_t stream) {
+  using namespace qf2::rms;
+  if (!x || (!y && !h)) return QF2_ERR_ARG;
+  if (rows < 0 || dim <= 0 || dim % 256 || rows_per_batch <= 0) return QF2_ERR_SHAPE;
+  if (rows == 0) return QF2_OK;
+  const void* ps[] = {y, x, h, w_post, gate, w_pre, scale};
+  for (const void* p : ps)
+    if (p && (reinterpret_cast<uintptr_t>(p) & 15)) return QF2_ERR_ALIGN;
+  if ((gate && gate_stride % 8) || (scale && scale_stride % 8)) return QF2_ERR_ALIGN;
+  GateResArgs a;
+  a.y = reinterpret_cast<const __nv_bfloat16*>(y);
+  a.x = reinterpret_cast<__nv_bfloat16*>(x);
+  a.h = reinterpret_cast<__nv_bfloat16*>(h);
+  a.rows = rows;
+  a.rows_per_batch = rows_per_batch;
+  a.w_post = reinterpret_cast<const __nv_bfloat16*>(w_post);
+  a.eps_post = eps_post;
+  a.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
+  a.gate_stride = gate_stride;
+  a.gate_tanh = gate_tanh;
+  a.w_pre = reinterpret_cast<const __nv_bfloat16*>(w_pre);
+  a.eps_pre = eps_pre;
+  a.scale = reinterpret_cast<const __nv_bfloat16*>(scale);
+  a.scale_stride = scale_stride;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dim / 256) {
+    case 1: launch_gate_residual<1>(a, st); break;
+    case 2: launch_gate_residual<2>(a, st); break;
+    case 3: launch_gate_residual<3>(a, st); break;
+    case 4: launch_gate_residual<4>(a, st); break;
+    case 6: launch_gate_residual<6>(a, st); break;
+    case 8: launch_gate_residual<8>(a, st); break;
+    case 9: launch_gate_residual<9>(a, st); break;
+    case 12: launch_gate_residual<12>(a, st); break;
+    case 16: launch_gate_residual<16>(a, st); break;
+    default: return QF2_ERR_SHAPE;
+  }
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}

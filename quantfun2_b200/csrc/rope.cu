@@ -141,10 +141,12 @@ extern "C" int qf2_rope_apply(const void* xq, void* xq_out, int64_t Hq, const in
 // ------------------------------------------------ fused QK RMSNorm + RoPE --
 // Replaces the per-head q_norm / k_norm (src/models/flux/mmdit.py:133-134,
 // src/models/common/attn.py:209-210) followed by rope_apply (:149 / :212): one pass over
-// the fused QKV projection output [rows, 3*H*D] (row = b * L + s).  q and k rows get
-// y = x * rsqrt(mean(x^2) + eps) * w (fp32) rotated by freqs[b, s, :], then rounded
-// once; v rows are copied.  Outputs are written through {batch, seq, head} strides,
-// so they can land at an offset inside a larger joint-sequence buffer.
+// the fused QKV projection output [rows, (Hq + 2*Hkv)*D] (row = b * L + s; q heads, then
+// k heads, then v heads).  q and k rows get y = x * rsqrt(mean(x^2) + eps) * w (fp32)
+// rotated by freqs[b, s, :], then rounded once; v rows are copied.  Outputs are written
+// through {batch, seq, head} strides with head dim Dout >= D (columns D..Dout-1 zero),
+// so they can land inside a larger joint-sequence buffer and be padded to the
+// attention kernel's head dim.
 namespace qf2 {
 namespace rope {
 
@@ -155,24 +157,27 @@ struct QkvDst {
 
 // 16 lanes per head row (8 elements each), 16 head rows per 256-thread CTA pass
 __global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld,
-                                                            int64_t rows, int64_t L, int H, QkvDst dst,
-                                                            const __nv_bfloat16* __restrict__ qw,
+                                                            int64_t rows, int64_t L, int Hq, int Hkv, int D, int Dout,
+                                                            QkvDst dst, const __nv_bfloat16* __restrict__ qw,
                                                             const __nv_bfloat16* __restrict__ kw, float eps,
                                                             const float2* __restrict__ freqs, int64_t fb, int64_t fs) {
-  constexpr int D = 128;
   const int sub = threadIdx.x & 15, grp = threadIdx.x >> 4;
-  const int64_t units = rows * 3 * H;
+  const int Ht = Hq + 2 * Hkv;
+  const int64_t units = rows * Ht;
+  const int nin = D / 8, nout = Dout / 8;
   // the loop bound is CTA-uniform so both 16-lane groups of a warp always reach the
   // shuffles together; out-of-range groups compute on zeros and store nothing
   for (int64_t base = (int64_t)blockIdx.x * 16; base < units; base += (int64_t)gridDim.x * 16) {
     const int64_t u = base + grp;
     const bool valid = u < units;
-    const int64_t row = valid ? u / (3 * H) : 0;
-    const int hr = valid ? (int)(u % (3 * H)) : 0;
-    const int kind = hr / H, head = hr % H;
+    const int64_t row = valid ? u / Ht : 0;
+    const int hr = valid ? (int)(u % Ht) : 0;
+    const int kind = hr < Hq ? 0 : (hr < Hq + Hkv ? 1 : 2);
+    const int head = kind == 0 ? hr : (kind == 1 ? hr - Hq : hr - Hq - Hkv);
     const int64_t b = row / L, s = row % L;
-    const uint4 raw = valid ? *reinterpret_cast<const uint4*>(qkv + row * ld + (int64_t)hr * D + sub * 8)
-                            : make_uint4(0, 0, 0, 0);
+    const bool live = valid && sub < nin;
+    const uint4 raw = live ? *reinterpret_cast<const uint4*>(qkv + row * ld + (int64_t)hr * D + sub * 8)
+                           : make_uint4(0, 0, 0, 0);
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
     float x[8];
     float ss_ = 0.f;
@@ -183,9 +188,9 @@ __global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16*
     }
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) ss_ += __shfl_xor_sync(0xffffffffu, ss_, o, 16);
-    if (!valid) continue;
-    uint4 outv = raw;
-    if (kind != 2) {
+    if (!valid || sub >= nout) continue;
+    uint4 outv = raw;  // zeros on the padding lanes
+    if (kind != 2 && live) {
       const float r = __frsqrt_rn(ss_ / (float)D + eps);
       const __nv_bfloat16* w = (kind == 0 ? qw : kw) + sub * 8;
       const float2* f = freqs + b * fb + s * fs + sub * 4;
@@ -209,16 +214,18 @@ __global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16*
 }  // namespace rope
 }  // namespace qf2
 
-extern "C" int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_t L, int64_t H, int64_t D,
-                                 void* q_out, const int64_t* q_strides, void* k_out, const int64_t* k_strides,
-                                 void* v_out, const int64_t* v_strides, const void* q_weight, const void* k_weight,
-                                 float eps, const void* freqs_cis, const int64_t* freqs_strides, qf2_stream_t stream) {
+extern "C" int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_t L, int64_t Hq,
+                                 int64_t Hkv, int64_t D, int64_t Dout, void* q_out, const int64_t* q_strides,
+                                 void* k_out, const int64_t* k_strides, void* v_out, const int64_t* v_strides,
+                                 const void* q_weight, const void* k_weight, float eps, const void* freqs_cis,
+                                 const int64_t* freqs_strides, qf2_stream_t stream) {
   using namespace qf2::rope;
   if (!qkv || !q_out || !k_out || !v_out || !q_strides || !k_strides || !v_strides || !q_weight || !k_weight ||
       !freqs_cis || !freqs_strides)
     return QF2_ERR_ARG;
-  if (D != 128 || B <= 0 || L <= 0 || H <= 0) return QF2_ERR_SHAPE;
-  if (qkv_row_stride < 3 * H * D || qkv_row_stride % 8) return QF2_ERR_ALIGN;
+  if (D % 8 || D <= 0 || D > 128 || Dout < D || Dout % 8 || Dout > 128 || B <= 0 || L <= 0 || Hq <= 0 || Hkv <= 0)
+    return QF2_ERR_SHAPE;
+  if (qkv_row_stride < (Hq + 2 * Hkv) * D || qkv_row_stride % 8) return QF2_ERR_ALIGN;
   const void* ps[4] = {qkv, q_out, k_out, v_out};
   for (const void* p : ps)
     if (!al(p, 16)) return QF2_ERR_ALIGN;
@@ -233,11 +240,11 @@ extern "C" int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_
   }
   if (freqs_strides[0] % 2 || freqs_strides[1] % 2) return QF2_ERR_ALIGN;
   const int64_t rows = B * L;
-  const int64_t units = rows * 3 * H;
+  const int64_t units = rows * (Hq + 2 * Hkv);
   int64_t blocks = (units + 15) / 16;
   if (blocks > 148 * 32) blocks = 148 * 32;
   qkv_norm_rope_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, rows, L, (int)H, dst,
+      reinterpret_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, rows, L, (int)Hq, (int)Hkv, (int)D, (int)Dout, dst,
       reinterpret_cast<const __nv_bfloat16*>(q_weight), reinterpret_cast<const __nv_bfloat16*>(k_weight), eps,
       reinterpret_cast<const float2*>(freqs_cis), freqs_strides[0], freqs_strides[1]);
   QF2_LAUNCH_CHECK();

@@ -30,6 +30,7 @@ __all__ = [
     "inplace_softmax",
     "topk_attn",
     "qkv_norm_rope",
+    "rms_gate_residual",
     "QF2Error",
 ]
 
@@ -185,18 +186,50 @@ def topk_attn(xq, xk, xv, mask, fn, HEAD_DIM, scale=None, TOP_K=256, POS_DICT=No
 
 def qkv_norm_rope(qkv: torch.Tensor, H: int, q_weight: torch.Tensor, k_weight: torch.Tensor,
                   freqs_cis: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
-                  eps: float = 1e-6) -> None:
+                  eps: float = 1e-6, Hkv: int | None = None) -> None:
     """Fused per-head RMSNorm of q and k, RoPE of q and k, copy of v.
-    qkv [B, L, 3*H*128] bf16 -> q_out / k_out / v_out [B, L, H, 128] views (any strides
-    with 16-byte rows, e.g. slices of a joint txt+img buffer)."""
+    qkv [B, L, (H + 2*Hkv)*head_dim] bf16 (q heads, then k heads, then v heads) ->
+    q_out [B, L, H, Dout], k_out / v_out [B, L, Hkv, Dout] views (any strides with 16-byte
+    rows, e.g. slices of a joint txt+img buffer); Dout >= head_dim is zero-padded."""
     require_device(qkv)
-    B, L, _ = qkv.shape
+    Hkv = H if Hkv is None else Hkv
+    B, L, W = qkv.shape
+    head_dim = W // (H + 2 * Hkv)
+    Dout = q_out.shape[-1]
     q2 = qkv.reshape(B * L, -1)
     if q2.stride(-1) != 1:
         q2 = q2.contiguous()
-    fc, fs = _freqs_view(freqs_cis.to(qkv.device), B, L, 64)
+    fc, fs = _freqs_view(freqs_cis.to(qkv.device), B, L, head_dim // 2)
     st = lambda t: i64(t.stride(0), t.stride(1), t.stride(2))  # noqa: E731
     check(_lib.load().qf2_qkv_norm_rope(
-        q2.data_ptr(), q2.stride(0), B, L, H, 128, q_out.data_ptr(), st(q_out), k_out.data_ptr(), st(k_out),
-        v_out.data_ptr(), st(v_out), q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(), float(eps),
-        fc.data_ptr(), i64(*fs), stream_ptr(qkv.device)), "qf2_qkv_norm_rope")
+        q2.data_ptr(), q2.stride(0), B, L, H, Hkv, head_dim, Dout, q_out.data_ptr(), st(q_out), k_out.data_ptr(),
+        st(k_out), v_out.data_ptr(), st(v_out), q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(),
+        float(eps), fc.data_ptr(), i64(*fs), stream_ptr(qkv.device)), "qf2_qkv_norm_rope")
+
+
+def rms_gate_residual(x: torch.Tensor, y: torch.Tensor | None = None, h: torch.Tensor | None = None,
+                      rows_per_batch: int | None = None, w_post: torch.Tensor | None = None, eps_post: float = 1e-5,
+                      gate: torch.Tensor | None = None, gate_tanh: bool = True, w_pre: torch.Tensor | None = None,
+                      eps_pre: float = 1e-5, scale: torch.Tensor | None = None) -> torch.Tensor | None:
+    """The Lumina joint block's glue (src/models/lumina/image_two/model.py:82-101) in one pass
+    over contiguous bf16 rows x [M, dim] (dim % 256 == 0):
+        x += g * RMSNorm(y; w_post)      (in place; g = tanh(gate[b]) / gate[b] / 1)
+        h  = RMSNorm(x; w_pre) * (1 + scale[b])
+    gate / scale: [M / rows_per_batch, dim] bf16 views (row-strided).  Returns h."""
+    require_device(x)
+    M, dim = x.shape
+    rpb = M if rows_per_batch is None else rows_per_batch
+    for t in (x, y, h):
+        if t is not None and (not t.is_contiguous() or t.dtype != torch.bfloat16 or t.shape != (M, dim)):
+            raise QF2Error("x, y, h must be contiguous bf16 [M, dim]")
+    for t in (gate, scale):
+        if t is not None and (t.stride(-1) != 1 or t.dtype != torch.bfloat16):
+            raise QF2Error("gate / scale must be bf16 row-strided views")
+    p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    wp = None if w_post is None else w_post.to(torch.bfloat16).contiguous()
+    wq = None if w_pre is None else w_pre.to(torch.bfloat16).contiguous()
+    check(_lib.load().qf2_rms_gate_residual(
+        p(y), x.data_ptr(), p(h), M, dim, rpb, p(wp), float(eps_post), p(gate),
+        0 if gate is None else gate.stride(0), int(bool(gate_tanh)), p(wq), float(eps_pre), p(scale),
+        0 if scale is None else scale.stride(0), stream_ptr(x.device)), "qf2_rms_gate_residual")
+    return h

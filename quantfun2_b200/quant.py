@@ -26,7 +26,7 @@ from . import _lib
 from ._lib import QF2Error, check, require_device, stream_ptr
 
 __all__ = ["qdtype", "QLinear", "qint8", "qfloat8", "qfloat8_w8a8", "quantize_model", "linear_inserter",
-           "quantize_rows", "codes_to_bf16", "gemm", "ln_modulate"]
+           "quantize_rows", "codes_to_bf16", "gemm", "ln_modulate", "glu_interleave"]
 
 
 def _ws(device) -> torch.Tensor:
@@ -60,12 +60,15 @@ def codes_to_bf16(q: torch.Tensor, fmt: str) -> torch.Tensor:
 
 def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=None, fp8: bool = False,
          out_dtype=torch.bfloat16, out: torch.Tensor | None = None, gelu_col0: int = -1,
-         residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, rows_per_gate: int = 1) -> torch.Tensor:
+         residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, rows_per_gate: int = 1,
+         glu: bool = False) -> torch.Tensor:
     """D = (a . b^T) * row_scale[:, None] * col_scale[None, :] + bias on tcgen05.
     a [M, K], b [N, K]: bf16, or uint8 e4m3 codes with fp8=True.
     Fused epilogue: GELU (tanh) on columns >= gelu_col0; D = residual + gate * D when
-    residual is given (gate [rows/rows_per_gate, N] bf16, may be a strided view).  `out`
-    may be a row-strided 2-D view (for instance a column slice of a larger buffer)."""
+    residual is given (gate [rows/rows_per_gate, N] bf16, may be a strided view); with
+    glu=True b holds SwiGLU weights in `glu_interleave` order and D = silu(gate) * up
+    [M, N/2].  `out` may be a row-strided 2-D view (for instance a column slice of a
+    larger buffer)."""
     require_device(a)
     M, K = a.shape
     N = b.shape[0]
@@ -75,9 +78,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
         a = a.contiguous()
     if b.stride(-1) != 1:
         b = b.contiguous()
+    No = N // 2 if glu else N
     if out is None:
-        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
-    elif out.shape != (M, N) or out.stride(-1) != 1 or out.dtype != out_dtype:
+        out = torch.empty(M, No, dtype=out_dtype, device=a.device)
+    elif out.shape != (M, No) or out.stride(-1) != 1 or out.dtype != out_dtype:
         raise QF2Error("out must be an [M, N] row-strided view of the output dtype")
     if residual is not None and (residual.stride(-1) != 1 or residual.dtype != torch.bfloat16):
         raise QF2Error("residual must be a bf16 row-strided [M, N] view")
@@ -95,12 +99,23 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
         _lib.QF2_E4M3 if fp8 else _lib.QF2_BF16, _lib.QF2_F32 if out_dtype == torch.float32 else _lib.QF2_BF16,
         row_scale.data_ptr() if row_scale is not None else None,
         col_scale.data_ptr() if col_scale is not None else None,
-        bias.data_ptr() if bias is not None else None, bias_dt, int(gelu_col0),
+        bias.data_ptr() if bias is not None else None, bias_dt, int(gelu_col0), int(bool(glu)),
         residual.data_ptr() if residual is not None else None, residual.stride(0) if residual is not None else 0,
         gate.data_ptr() if gate is not None else None, gate.stride(0) if gate is not None else 0,
         int(rows_per_gate), ws.data_ptr(), 256, stream_ptr(a.device)),
         "qf2_gemm_ex")
     return out
+
+
+def glu_interleave(w1: torch.Tensor, w3: torch.Tensor) -> torch.Tensor:
+    """Rows of the SwiGLU gate (w1) and up (w3) projections [hidden, in] stacked in the
+    order the glu epilogue reads them: for each 128-row block j, w1[128j:128j+128] then
+    w3[128j:128j+128].  hidden % 128 == 0.  Works on codes, scales and biases alike."""
+    if w1.shape != w3.shape or w1.shape[0] % 128:
+        raise QF2Error("w1 / w3 must have equal shapes with hidden % 128 == 0")
+    h = w1.shape[0]
+    tail = w1.shape[1:]
+    return torch.stack([w1.reshape(h // 128, 128, *tail), w3.reshape(h // 128, 128, *tail)], 1).reshape(2 * h, *tail)
 
 
 def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_per_batch: int, fmt: str = "bf16",
