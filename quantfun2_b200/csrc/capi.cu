@@ -26,12 +26,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 }
 
 static bool make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
-                      const cuuint64_t* gdim, const cuuint64_t* gstr, const cuuint32_t* bdim) {
+                      const cuuint64_t* gdim, const cuuint64_t* gstr, const cuuint32_t* bdim,
+                      CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tmap_encoder();
   if (encode == nullptr) return false;
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUresult r = encode(map, dtype, rank, const_cast<void*>(base), gdim, gstr, bdim, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -50,6 +51,14 @@ bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* b
   const cuuint64_t gstr[1] = {stride_bytes};
   const cuuint32_t bdim[2] = {box[0], box[1]};
   return make_tmap(map, dtype, 2, base, gdim, gstr, bdim);
+}
+
+bool qf2_make_tmap_2d_sw64(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
+                           uint64_t stride_bytes, const uint32_t box[2]) {
+  const cuuint64_t gdim[2] = {dims[0], dims[1]};
+  const cuuint64_t gstr[1] = {stride_bytes};
+  const cuuint32_t bdim[2] = {box[0], box[1]};
+  return make_tmap(map, dtype, 2, base, gdim, gstr, bdim, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 extern "C" const char* qf2_version(void) { return "quantfun2-b200 0.1.0 (sm_100a)"; }

@@ -103,6 +103,80 @@ QF2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// ------------------------------------------------------- CTA pairs (2-SM) --
+// Rank of this CTA in its cluster.
+QF2_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the object at local shared address `addr` in CTA `rank`.
+QF2_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by a shared::cluster address.
+QF2_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// All threads of all CTAs of the cluster.
+QF2_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 2-D tiled TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier of either CTA of the pair (shared::cluster address).  No multicast.
+QF2_DEV void tma_load_2d_pair(void* smem_dst, const void* tmap, int32_t x, int32_t y, uint32_t bar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(bar_cluster_addr)
+      : "memory");
+}
+
+QF2_DEV void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+QF2_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+QF2_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrive on the mbarrier at a shared::cluster address once every tcgen05 operation of
+// the pair issued so far by this thread has completed.
+QF2_DEV void tc_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+               : "memory");
+}
+
+// M256 pair MMAs: A rows 0-127 / B rows (N half 0) from the issuing CTA's shared memory,
+// A rows 128-255 / B N half 1 from the peer's at the same offsets; D split across the
+// two CTAs' TMEM (128 lanes each).
+QF2_DEV void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+QF2_DEV void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // ------------------------------------------------------------- bulk copies --
 // 1-D bulk copy global -> shared, completion counted on an mbarrier (tx bytes).
 QF2_DEV void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
@@ -139,6 +213,22 @@ QF2_DEV void tma_load_4d(void* smem_dst, const void* tmap, int32_t x, int32_t y,
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
       : "memory");
 }
+
+// 2-D tiled TMA store shared -> global (bulk group completion); out-of-bounds parts of
+// the box are not written.
+QF2_DEV void tma_store_2d(const void* tmap, const void* smem_src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+QF2_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's bulk groups still read their shared-memory source.
+template <int N>
+QF2_DEV void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until all of this thread's bulk groups have completed.
+QF2_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 QF2_DEV void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
@@ -347,6 +437,10 @@ bool qf2_make_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* b
 // Same, 2-D (dims innermost first, byte stride of dim 1).
 bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
                       uint64_t stride_bytes, const uint32_t box[2]);
+
+// Same, 2-D with 64-byte swizzle (output staging tiles of 64-byte rows).
+bool qf2_make_tmap_2d_sw64(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
+                           uint64_t stride_bytes, const uint32_t box[2]);
 
 // Records the CUDA error behind a QF2_ERR_LAUNCH for qf2_last_error().
 void qf2_record_cuda_error(cudaError_t e, const char* where);

@@ -229,7 +229,7 @@ def rms_gate_residual(x: torch.Tensor, y: torch.Tensor | None = None, h: torch.T
     wp = None if w_post is None else w_post.to(torch.bfloat16).contiguous()
     wq = None if w_pre is None else w_pre.to(torch.bfloat16).contiguous()
     check(_lib.load().qf2_rms_gate_residual(
-        p(y), x.data_ptr(), p(h), M, dim, rpb, p(wp), float(eps_post), p(gate),
-        0 if gate is None else gate.stride(0), int(bool(gate_tanh)), p(wq), float(eps_pre), p(scale),
+        p(y), x.data_ptr(), p(h), M, dim, rpb, p(wp), float(eps_post or 0.0), p(gate),
+        0 if gate is None else gate.stride(0), int(bool(gate_tanh)), p(wq), float(eps_pre or 0.0), p(scale),
         0 if scale is None else scale.stride(0), stream_ptr(x.device)), "qf2_rms_gate_residual")
     return h

@@ -206,7 +206,9 @@ class LuminaDiT(nn.Module):
         fscale = mods_all[:, 4 * D * (n_ref + n_main):4 * D * (n_ref + n_main) + D]
         self._run(self.layers, x, [mod(n_ref + i) for i in range(n_main)], freqs)
         # final layer: LayerNorm (no affine, eps 1e-6) * (1 + scale) -> linear (nextdit.py:63-78)
-        hf = ln_modulate(x[:, Lc:].reshape(B * Li, D), torch.zeros_like(fscale), fscale, Li)
+        fmod = torch.zeros(B, 2 * D, dtype=torch.bfloat16, device=x.device)  # [shift = 0 | scale]
+        fmod[:, D:] = fscale
+        hf = ln_modulate(x[:, Lc:].reshape(B * Li, D), fmod[:, :D], fmod[:, D:], Li)
         return self.final_linear.run(hf, None).view(B, Li, -1)
 
     def make_freqs(self, B: int, cap_len: int, h: int, w: int, device) -> torch.Tensor:

@@ -43,10 +43,14 @@ def test_gemm_swiglu_epilogue(cuda):
     up = (a.double() @ w3.double().T) * cs3.double() + b3.double()
     ref = gt * torch.sigmoid(gt) * up
     err = (out.double() - ref).abs()
-    # fp32 accumulation + SFU tanh (2^-11 relative) + one bf16 rounding
-    bound = 2 * _bf16_ulp(ref) + 1e-3 * (gt.abs() + 1) * up.abs()
+    # one bf16 rounding + SFU tanh (2^-11 absolute) + fp32 accumulation of K products
+    bound = 2 * _bf16_ulp(ref) + 1e-3 * (gt.abs() + 1) * up.abs() + 1e-5 * (gt.abs() + 1) * (up.abs() + 1)
     assert out.shape == (M, Hd)
-    assert bool((err <= bound).all()), f"max err {err.max().item()}"
+    bad = (err > bound).nonzero()
+    if len(bad):
+        i, j = bad[0].tolist()
+        pytest.fail(f"{len(bad)} elements out of bound; first at ({i}, {j}): out {out[i, j].item()} ref "
+                    f"{ref[i, j].item()} gate {gt[i, j].item()} up {up[i, j].item()} max err {err.max().item()}")
 
 
 def test_rms_gate_residual(cuda):

@@ -48,6 +48,32 @@ def test_gemm_bf16(cuda, mnk):
     assert rel_err(d16.float().cpu(), (a.double() @ b.double().T).cpu()) < 8e-3
 
 
+@pytest.mark.parametrize("n", [2304, 3840, 1000, 384, 96])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_gemm_pair_tile_widths(cuda, n, fp8):
+    """CTA-pair path (M > 128) over output widths that select 256 / 192 / 128-column
+    tiles and ragged last tiles; bf16 output through the TMA-store epilogue."""
+    from quantfun2_b200.quant import gemm, quantize_rows
+
+    M, K = 4352 + 40, 384
+    g = torch.Generator(device=cuda).manual_seed(n)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = torch.randn(n, K, device=cuda, generator=g).bfloat16()
+    bias = torch.randn(n, device=cuda, generator=g).bfloat16()
+    if fp8:
+        xq, xs = quantize_rows(x, "e4m3")
+        wq, ws = quantize_rows(w, "e4m3")
+        d = gemm(xq, wq, row_scale=xs, col_scale=ws, bias=bias, fp8=True)
+        xf = torch.from_numpy(e4m3_bits_to_f32(xq.cpu().numpy())).double().to(cuda) * xs.double()[:, None]
+        wf = torch.from_numpy(e4m3_bits_to_f32(wq.cpu().numpy())).double().to(cuda) * ws.double()[:, None]
+        ref = xf @ wf.T + bias.double()
+    else:
+        d = gemm(x, w, bias=bias)
+        ref = x.double() @ w.double().T + bias.double()
+    assert d.shape == (M, n)
+    assert rel_err(d.float().cpu(), ref.cpu()) < 8e-3
+
+
 @pytest.mark.parametrize("mnk", [(128, 256, 128), (300, 776, 272), (4608, 3072, 3072)])
 def test_gemm_e4m3(cuda, mnk):
     from quantfun2_b200.quant import gemm, quantize_rows
