@@ -10,9 +10,13 @@ FP8 PV, fp32 accumulation).  Metric: attention TFLOPS = 4*B*H*S^2*D / time.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-The JSON line also carries "flux_step": the ms per Flux-dev-shaped denoise step
-(19 double + 38 single blocks, 4608 tokens, FP8 linears + Sage attention), split
-over the N ranks with Ulysses head-parallel attention when N > 1.
+The JSON line also carries
+  "flux_step":   ms per Flux-dev-shaped denoise step (19 double + 38 single blocks,
+                 FP8 linears + Sage attention) at 4608 and 16,896 tokens, split over the
+                 N ranks with Ulysses head-parallel attention when N > 1;
+  "lumina_step": ms per Lumina-Image-2.0-2B-shaped step (INT8 weight-only linears),
+                 one sample per rank (batch-parallel), and the 8-sample batch on one GPU;
+  "blocksparse": the top-k block-sparse attention workload (S=16384, keep 12.5 %), N=1.
 
 N > 1 is launched by torchrun, one rank per GPU; each rank runs its own B=2
 problem (independent sequences, no collective on the data path: weak scaling).
@@ -54,6 +58,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-flux", action="store_true")
     p.add_argument("--no-lumina", action="store_true")
+    p.add_argument("--no-blocksparse", action="store_true")
+    p.add_argument("--profile", action="store_true",
+                   help="for ncu runs: no clock soak, no cuBLAS peak, no CPU baseline, no 8-sample Lumina batch")
     return p.parse_args()
 
 
@@ -183,38 +190,101 @@ def make_inputs(dev, seed):
     return q.bfloat16(), k.bfloat16(), v.bfloat16()
 
 
-def run_flux_step(rank: int, world: int, dev, warmup: int = 2, steps: int = 5) -> dict:
-    """One Flux-dev-shaped forward (19 double + 38 single blocks, hidden 3072, 24 x 128 heads,
-    4096 img + 512 txt tokens, FP8 W8A8 linears, Sage attention) per step; with N ranks the
-    joint sequence is split N ways and attention runs head-parallel (Ulysses all-to-all)."""
+def run_flux_step(rank: int, world: int, dev, sides=(64, 128), warmup: int = 2, steps: int = 5) -> dict:
+    """Flux-dev-shaped forwards (19 double + 38 single blocks, hidden 3072, 24 x 128 heads,
+    512 txt tokens + a side x side image-token grid, FP8 W8A8 linears, Sage attention):
+    side 64 -> 4608 tokens (the metric's shape), side 128 -> 16,896 tokens (2048^2 latent).
+    With N ranks the joint sequence is split N ways and attention runs head-parallel
+    (Ulysses all-to-all).  One model, one entry per image side."""
     from quantfun2_b200.dit import FluxDiT, SeqParallel, flux_position_ids, flux_step_flops, rope_freqs
 
-    T, side = 512, 64
-    I = side * side
-    if T % world or I % world or 24 % world:
-        return {"skipped": f"{world} ranks do not divide 512 txt / 4096 img tokens and 24 heads"}
+    T = 512
+    if T % world or 24 % world:
+        return {"skipped": f"{world} ranks do not divide 512 txt tokens and 24 heads"}
     model = FluxDiT(device=dev, seed=0)
     sp = SeqParallel(torch.distributed.group.WORLD if world > 1 else None)
-    g = torch.Generator(device=dev).manual_seed(0)  # identical inputs on every rank
-    img = torch.randn(1, I, 64, device=dev, generator=g).bfloat16()
-    txt = torch.randn(1, T, 4096, device=dev, generator=g).bfloat16()
-    t = torch.rand(1, device=dev, generator=g)
-    y = torch.randn(1, 768, device=dev, generator=g).bfloat16()
-    freqs = rope_freqs(flux_position_ids(1, T, side, side, dev), (16, 56, 56))
-    tl, il = T // world, I // world
-    img_l, txt_l = img[:, rank * il:(rank + 1) * il].contiguous(), txt[:, rank * tl:(rank + 1) * tl].contiguous()
-    f_l = torch.cat([freqs[:, rank * tl:(rank + 1) * tl], freqs[:, T + rank * il:T + (rank + 1) * il]], 1).contiguous()
-    fwd = lambda: model(img_l, txt_l, t, y, f_l, sp)  # noqa: E731
-    r = _time_forward(fwd, world, dev, warmup, steps)
+    out = {}
+    for side in sides:
+        I = side * side
+        g = torch.Generator(device=dev).manual_seed(0)  # identical inputs on every rank
+        img = torch.randn(1, I, 64, device=dev, generator=g).bfloat16()
+        txt = torch.randn(1, T, 4096, device=dev, generator=g).bfloat16()
+        t = torch.rand(1, device=dev, generator=g)
+        y = torch.randn(1, 768, device=dev, generator=g).bfloat16()
+        freqs = rope_freqs(flux_position_ids(1, T, side, side, dev), (16, 56, 56))
+        tl, il = T // world, I // world
+        img_l, txt_l = img[:, rank * il:(rank + 1) * il].contiguous(), txt[:, rank * tl:(rank + 1) * tl].contiguous()
+        f_l = torch.cat([freqs[:, rank * tl:(rank + 1) * tl], freqs[:, T + rank * il:T + (rank + 1) * il]],
+                        1).contiguous()
+        fwd = lambda: model(img_l, txt_l, t, y, f_l, sp)  # noqa: E731
+        nsteps = steps if I <= 4096 else max(2, steps // 2)
+        r = _time_forward(fwd, world, dev, warmup if I <= 4096 else 1, nsteps)
+        del img, txt, img_l, txt_l, f_l, freqs
+        torch.cuda.empty_cache()
+        fl = flux_step_flops(T + I)
+        sec = r.pop("sec")
+        out[f"tokens_{T + I}"] = {
+            "ms_per_step": sec * 1e3, "tflops": fl / sec / 1e12, "flops_per_step": fl, "tokens": T + I, **r,
+            "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU",
+            "linears": "FP8 e4m3 W8A8 (per-token activation, per-channel weight scales)",
+            "attention": "Sage INT8 QK / FP8 PV"}
     del model
     torch.cuda.empty_cache()
-    fl = flux_step_flops(T + I)
-    sec = r.pop("sec")
-    res = {"ms_per_step": sec * 1e3, "tflops": fl / sec / 1e12, "flops_per_step": fl, "tokens": T + I, **r,
-           "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU",
-           "linears": "FP8 e4m3 W8A8 (per-token activation, per-channel weight scales)",
-           "attention": "Sage INT8 QK / FP8 PV"}
-    return res
+    return out
+
+
+def run_blocksparse(dev, S: int = 16384, H: int = 24, D: int = 128, keep_frac: float = 0.125, warmup: int = 3,
+                    steps: int = 10) -> dict:
+    """Top-k block-sparse attention at B=1, H=24, D=128, S=16384, bf16, 128-token blocks,
+    keeping 12.5 % of the key blocks: block pooling + scores + top-k selection + exact
+    softmax attention over the kept blocks.  Seeded inputs: Q, K, V ~ N(0, 1), each query
+    block's rows shifted by 2.0 along a random unit direction that 4 random key blocks
+    share (the query-aligned hot blocks)."""
+    from quantfun2_b200.attention import block_topk_select, blocksparse_attn
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    nb = S // 128
+    keep = max(1, math.ceil(keep_frac * nb))
+    q = torch.randn(1, H, S, D, device=dev, generator=g)
+    k = torch.randn(1, H, S, D, device=dev, generator=g)
+    v = torch.randn(1, H, S, D, device=dev, generator=g).bfloat16()
+    u = torch.randn(1, H, nb, D, device=dev, generator=g)
+    u = 2.0 * u / u.norm(dim=-1, keepdim=True)
+    q.view(1, H, nb, 128, D).add_(u[:, :, :, None, :])
+    hot = torch.rand(1, H, nb, nb, device=dev, generator=g).argsort(dim=-1)[..., :4]  # 4 distinct key blocks
+    kadd = torch.zeros(1, H, nb, D, device=dev)
+    kadd.scatter_add_(2, hot.reshape(1, H, nb * 4, 1).expand(-1, -1, -1, D),
+                      u[:, :, :, None, :].expand(-1, -1, -1, 4, -1).reshape(1, H, nb * 4, D))
+    k.view(1, H, nb, 128, D).add_(kadd[:, :, :, None, :])
+    q, k = q.bfloat16(), k.bfloat16()
+    del kadd, u, hot
+
+    def step():
+        idx = block_topk_select(q, k, keep)
+        return blocksparse_attn(q, k, v, idx)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record()
+    for _ in range(steps):
+        idx = block_topk_select(q, k, keep)
+    e[1].record()
+    for _ in range(steps):
+        o = blocksparse_attn(q, k, v, idx)
+    e[2].record()
+    torch.cuda.synchronize()
+    sel = e[0].elapsed_time(e[1]) / steps / 1e3
+    att = e[1].elapsed_time(e[2]) / steps / 1e3
+    fl = 4.0 * H * S * (keep * 128) * D
+    finite = bool(torch.isfinite(o.float()).all())
+    del q, k, v, o, idx
+    torch.cuda.empty_cache()
+    return {"workload": f"B=1 H={H} S={S} D={D} bf16, 128-token blocks, keep {keep}/{nb}",
+            "ms_per_step": (sel + att) * 1e3, "select_ms": sel * 1e3, "attention_ms": att * 1e3,
+            "kept_attention_flops": fl, "attention_tflops": fl / att / 1e12,
+            "step_tflops": fl / (sel + att) / 1e12, "output_finite": finite, "steps": steps}
 
 
 def _time_forward(fwd, world: int, dev, warmup: int, steps: int) -> dict:
@@ -323,7 +393,7 @@ def run_ours(args, rank: int, world: int, dev):
 
     flops_step = 4.0 * B * H * S * S * D
     peaks = measured_peaks()
-    fp8_peak = fp8_gemm_peak_tflops(dev) if rank == 0 else None
+    fp8_peak = fp8_gemm_peak_tflops(dev) if rank == 0 and not args.profile else None
 
     sampler = ClockSampler(dev.index or 0) if rank == 0 else None
     if sampler:
@@ -333,7 +403,7 @@ def run_ours(args, rank: int, world: int, dev):
         attn()
     # keep the GPU busy ~1.5 s before timing so the clock record covers steady load
     t_soak = time.time()
-    while time.time() - t_soak < 1.5:
+    while not args.profile and time.time() - t_soak < 1.5:
         for _ in range(20):
             quant()
             attn()
@@ -409,14 +479,18 @@ def run_ours(args, rank: int, world: int, dev):
             del q, k, v, out, ws
             torch.cuda.empty_cache()
         lumina = {"b1_per_gpu": run_lumina_step(rank, world, dev, batch=1)}
-        if world == 1:
+        if world == 1 and not args.profile:
             lumina["b8_single_gpu"] = run_lumina_step(rank, world, dev, batch=8, warmup=1, steps=3)
+    # ---- top-k block-sparse attention (one GPU's workload; rank 0 only)
+    blocksparse = None
+    if not args.no_blocksparse and rank == 0:
+        blocksparse = run_blocksparse(dev)
 
     if rank != 0:
         return
     # ---- CPU baseline: the reference's SDPA branch on a bounded sample (rank 0, N=1 only)
     cpu = None
-    if world == 1:
+    if world == 1 and not args.profile:
         from oracle.baseline import sdpa_cpu_sample
 
         sdpa_cpu_sample(heads=1, S=S, D=D)
@@ -453,6 +527,7 @@ def run_ours(args, rank: int, world: int, dev):
         "clocks": clocks,
         "flux_step": flux,
         "lumina_step": lumina,
+        "blocksparse": blocksparse,
     }
     print(json.dumps(line), flush=True)
 

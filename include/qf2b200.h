@@ -108,7 +108,7 @@ int qf2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, const void* we
                 qf2_stream_t stream);
 
 /* Gated residual + RMSNorm-modulate of the Lumina joint block (src/models/lumina/image_two/
- * model.py:82-101), one pass over rows of `dim` bf16 (dim a multiple of 256, <= 4096;
+ * model.py:82-101), one pass over rows of `dim` bf16 (dim a multiple of 256, <= 8192;
  * contiguous rows; batch b = row / rows_per_batch):
  *   if y:  x = bf16(x + g * RMSNorm(y; w_post, eps_post))   g = tanh(gate[b]) when
  *          gate_tanh, gate[b] otherwise, 1 without gate; w_post NULL = no norm on y

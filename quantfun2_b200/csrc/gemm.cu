@@ -599,11 +599,12 @@ static cudaError_t pair_setup(bool fp8, int* clusters) {
 }
 
 // Tile width of the CTA-pair kernel: among 256 / 192 / 128 the one with the least
-// estimated time, rounds of the persistent grid x per-tile cost (narrower tiles move more
-// bytes per FLOP: relative per-column costs 1.0 / 1.04 / 1.12).
+// estimated time, rounds of the persistent grid x per-tile cost.  Narrower tiles keep
+// fewer MMA cycles in flight per stage against the same TMA latency; measured per-column
+// costs on bf16 and e4m3 problems of 2304-15360 columns are about 1.0 / 1.25 / 1.8.
 static int pick_bn(int64_t M, int64_t N, int clusters) {
   const int cand[3] = {256, 192, 128};
-  const double cost[3] = {1.0, 1.04, 1.12};
+  const double cost[3] = {1.0, 1.25, 1.8};
   const int64_t mt = (M + 2 * BM - 1) / (2 * BM);
   int best = 256;
   double best_t = 1e300;

@@ -362,15 +362,27 @@ QF2_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: 
 // Low byte holds `lo`.
 QF2_DEV uint16_t f32x2_to_e4m3x2(float lo, float hi) {
   uint16_t r;
-  asm volatile("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(lo), "f"(hi));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(lo), "f"(hi));
   return r;
 }
 
 // ex2.approx: 2^x on the SFU.
 QF2_DEV float fast_exp2(float x) {
   float y;
-  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// e4m3 codes of four non-negative fp32 values already scaled by 2^-120, without the
+// conversion unit: after the scaling the fp32 exponent field equals the e4m3 exponent
+// (fp32 subnormals reproduce e4m3 subnormals), so the code is bits [27:20] of the fp32
+// pattern rounded at bit 20 (half up).  Valid for scaled values below 464 * 2^-120.
+// Shifting left by 4 puts each code in byte 3; three byte permutes gather them (first
+// value in the lowest byte, like cvt.rn.satfinite.e4m3x2).
+QF2_DEV uint32_t e4m3x4_from_scaled(float a, float b, float c, float d) {
+  const uint32_t ua = (__float_as_uint(a) << 4) + 0x800000u, ub = (__float_as_uint(b) << 4) + 0x800000u;
+  const uint32_t uc = (__float_as_uint(c) << 4) + 0x800000u, ud = (__float_as_uint(d) << 4) + 0x800000u;
+  return __byte_perm(__byte_perm(ua, ub, 0x0073), __byte_perm(uc, ud, 0x0073), 0x5410);
 }
 
 template <typename T>

@@ -201,9 +201,10 @@ extern "C" int qf2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, con
 // The glue of the Lumina joint block (src/models/lumina/image_two/model.py:82-101):
 //   x = x + g * RMSNorm_post(y)          g = tanh(gate[b]) (or gate, or 1)
 //   h = RMSNorm_pre(x) * (1 + scale[b])  (the next linear's input)
-// in one pass: a warp owns a row of NV * 256 bf16 (NV 16-byte vectors per lane), y and x
-// are read once, x is rounded to bf16 once and stored, h is computed from that rounded
-// x (as the reference's next norm sees it) and stored.  Math in fp32.
+// in one pass: one CTA per row, one 8-element (16-byte) vector of y and x per thread
+// (dim / 8 threads), sums of squares reduced through shared memory; x is rounded to bf16
+// once and stored, h is computed from that rounded x (as the reference's next norm sees
+// it) and stored.  Math in fp32.
 namespace qf2 {
 namespace rms {
 
@@ -212,6 +213,7 @@ struct GateResArgs {
   __nv_bfloat16* x;
   __nv_bfloat16* h;
   int64_t rows, rows_per_batch;
+  int dim;
   const __nv_bfloat16* w_post;
   float eps_post;
   const __nv_bfloat16* gate;
@@ -241,91 +243,76 @@ QF2_DEV void st8(__nv_bfloat16* p, const float* f) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
-QF2_DEV float warp_sum(float v) {
+// sum over the CTA (blockDim.x a multiple of 32, <= 1024); `red` holds 32 floats
+QF2_DEV float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
 }
 
-template <int NV>
-__global__ void __launch_bounds__(256) gate_residual_kernel(GateResArgs a) {
-  constexpr int D = NV * 256;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= a.rows) return;
+__global__ void __launch_bounds__(1024) gate_residual_kernel(GateResArgs a) {
+  __shared__ float red[2][32];
+  const int64_t row = blockIdx.x;
   const int64_t b = row / a.rows_per_batch;
-  float xv[NV][8];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) ld8(a.x + row * D + (i * 32 + lane) * 8, xv[i]);
+  const int c = threadIdx.x * 8;
+  float xv[8];
+  ld8(a.x + row * a.dim + c, xv);
   if (a.y != nullptr) {
-    float yv[NV][8];
+    float yv[8], w[8], g[8];
+    ld8(a.y + row * a.dim + c, yv);
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      ld8(a.y + row * D + (i * 32 + lane) * 8, yv[i]);
+    for (int j = 0; j < 8; ++j) ss = fmaf(yv[j], yv[j], ss);
+    if (a.w_post != nullptr) {
+      ld8(a.w_post + c, w);
+    } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(yv[i][j], yv[i][j], ss);
+      for (int j = 0; j < 8; ++j) w[j] = 1.0f;
     }
-    const float r = a.w_post != nullptr ? __frsqrt_rn(warp_sum(ss) / (float)D + a.eps_post) : 1.0f;
+    if (a.gate != nullptr) {
+      ld8(a.gate + b * a.gate_stride + c, g);
+      if (a.gate_tanh) {
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = (i * 32 + lane) * 8;
-      float w[8], g[8];
-      if (a.w_post != nullptr) {
-        ld8(a.w_post + c, w);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = 1.0f;
+        for (int j = 0; j < 8; ++j) g[j] = tanhf(g[j]);
       }
-      if (a.gate != nullptr) {
-        ld8(a.gate + b * a.gate_stride + c, g);
-        if (a.gate_tanh) {
+    } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) g[j] = tanhf(g[j]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) g[j] = 1.0f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        xv[i][j] = __bfloat162float(__float2bfloat16_rn(fmaf(g[j], yv[i][j] * r * w[j], xv[i][j])));
-      st8(a.x + row * D + c, xv[i]);
+      for (int j = 0; j < 8; ++j) g[j] = 1.0f;
     }
+    const float tot = block_sum(ss, red[0]);
+    const float r = a.w_post != nullptr ? __frsqrt_rn(tot / (float)a.dim + a.eps_post) : 1.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xv[j] = __bfloat162float(__float2bfloat16_rn(fmaf(g[j], yv[j] * r * w[j], xv[j])));
+    st8(a.x + row * a.dim + c, xv);
   }
   if (a.h != nullptr) {
+    float w[8], sc[8], o[8];
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
+    for (int j = 0; j < 8; ++j) ss = fmaf(xv[j], xv[j], ss);
+    if (a.w_pre != nullptr) {
+      ld8(a.w_pre + c, w);
+    } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(xv[i][j], xv[i][j], ss);
-    const float r = __frsqrt_rn(warp_sum(ss) / (float)D + a.eps_pre);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = (i * 32 + lane) * 8;
-      float w[8], s[8], o[8];
-      if (a.w_pre != nullptr) {
-        ld8(a.w_pre + c, w);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = 1.0f;
-      }
-      if (a.scale != nullptr) {
-        ld8(a.scale + b * a.scale_stride + c, s);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s[j] = 0.0f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = xv[i][j] * r * w[j] * (1.0f + s[j]);
-      st8(a.h + row * D + c, o);
+      for (int j = 0; j < 8; ++j) w[j] = 1.0f;
     }
+    if (a.scale != nullptr) {
+      ld8(a.scale + b * a.scale_stride + c, sc);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sc[j] = 0.0f;
+    }
+    const float tot = block_sum(ss, red[1]);
+    const float r = __frsqrt_rn(tot / (float)a.dim + a.eps_pre);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = xv[j] * r * w[j] * (1.0f + sc[j]);
+    st8(a.h + row * a.dim + c, o);
   }
-}
-
-template <int NV>
-static void launch_gate_residual(const GateResArgs& a, cudaStream_t st) {
-  gate_residual_kernel<NV><<<(unsigned)((a.rows + 7) / 8), 256, 0, st>>>(a);
 }
 
 }  // namespace rms
@@ -337,7 +324,7 @@ extern "C" int qf2_rms_gate_residual(const void* y, void* x, void* h, int64_t ro
                                      const void* scale, int64_t scale_stride, qf2_stream_t stream) {
   using namespace qf2::rms;
   if (!x || (!y && !h)) return QF2_ERR_ARG;
-  if (rows < 0 || dim <= 0 || dim % 256 || rows_per_batch <= 0) return QF2_ERR_SHAPE;
+  if (rows < 0 || dim <= 0 || dim % 256 || dim > 8192 || rows_per_batch <= 0) return QF2_ERR_SHAPE;
   if (rows == 0) return QF2_OK;
   const void* ps[] = {y, x, h, w_post, gate, w_pre, scale};
   for (const void* p : ps)
@@ -358,19 +345,10 @@ extern "C" int qf2_rms_gate_residual(const void* y, void* x, void* h, int64_t ro
   a.eps_pre = eps_pre;
   a.scale = reinterpret_cast<const __nv_bfloat16*>(scale);
   a.scale_stride = scale_stride;
+  a.dim = (int)dim;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  switch (dim / 256) {
-    case 1: launch_gate_residual<1>(a, st); break;
-    case 2: launch_gate_residual<2>(a, st); break;
-    case 3: launch_gate_residual<3>(a, st); break;
-    case 4: launch_gate_residual<4>(a, st); break;
-    case 6: launch_gate_residual<6>(a, st); break;
-    case 8: launch_gate_residual<8>(a, st); break;
-    case 9: launch_gate_residual<9>(a, st); break;
-    case 12: launch_gate_residual<12>(a, st); break;
-    case 16: launch_gate_residual<16>(a, st); break;
-    default: return QF2_ERR_SHAPE;
-  }
+  if (rows > 0x7fffffff) return QF2_ERR_SHAPE;
+  gate_residual_kernel<<<(unsigned)rows, (unsigned)(dim / 8), 0, st>>>(a);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }

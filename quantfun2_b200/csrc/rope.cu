@@ -165,49 +165,64 @@ __global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16*
   const int Ht = Hq + 2 * Hkv;
   const int64_t units = rows * Ht;
   const int nin = D / 8, nout = Dout / 8;
+  constexpr int U = 2;  // head rows per 16-lane group per pass, loads issued together
   // the loop bound is CTA-uniform so both 16-lane groups of a warp always reach the
   // shuffles together; out-of-range groups compute on zeros and store nothing
-  for (int64_t base = (int64_t)blockIdx.x * 16; base < units; base += (int64_t)gridDim.x * 16) {
-    const int64_t u = base + grp;
-    const bool valid = u < units;
-    const int64_t row = valid ? u / Ht : 0;
-    const int hr = valid ? (int)(u % Ht) : 0;
-    const int kind = hr < Hq ? 0 : (hr < Hq + Hkv ? 1 : 2);
-    const int head = kind == 0 ? hr : (kind == 1 ? hr - Hq : hr - Hq - Hkv);
-    const int64_t b = row / L, s = row % L;
-    const bool live = valid && sub < nin;
-    const uint4 raw = live ? *reinterpret_cast<const uint4*>(qkv + row * ld + (int64_t)hr * D + sub * 8)
-                           : make_uint4(0, 0, 0, 0);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
-    float x[8];
-    float ss_ = 0.f;
+  for (int64_t base = (int64_t)blockIdx.x * 16 * U; base < units; base += (int64_t)gridDim.x * 16 * U) {
+    uint4 raw[U];
+    int64_t row[U];
+    int hr[U];
+    bool valid[U];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      x[j] = __bfloat162float(e[j]);
-      ss_ = fmaf(x[j], x[j], ss_);
+    for (int q = 0; q < U; ++q) {
+      const int64_t u = base + q * 16 + grp;
+      valid[q] = u < units;
+      // 32-bit division (units < 2^31 is checked on the host): 64-bit division by a
+      // runtime divisor costs more than the rest of the row's work
+      const uint32_t u32 = valid[q] ? (uint32_t)u : 0u;
+      row[q] = (int64_t)(u32 / (uint32_t)Ht);
+      hr[q] = (int)(u32 - (uint32_t)row[q] * (uint32_t)Ht);
+      raw[q] = (valid[q] && sub < nin)
+                   ? *reinterpret_cast<const uint4*>(qkv + row[q] * ld + (int64_t)hr[q] * D + sub * 8)
+                   : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss_ += __shfl_xor_sync(0xffffffffu, ss_, o, 16);
-    if (!valid || sub >= nout) continue;
-    uint4 outv = raw;  // zeros on the padding lanes
-    if (kind != 2 && live) {
-      const float r = __frsqrt_rn(ss_ / (float)D + eps);
-      const __nv_bfloat16* w = (kind == 0 ? qw : kw) + sub * 8;
-      const float2* f = freqs + b * fb + s * fs + sub * 4;
-      uint32_t* op = reinterpret_cast<uint32_t*>(&outv);
+    for (int q = 0; q < U; ++q) {
+      const int kind = hr[q] < Hq ? 0 : (hr[q] < Hq + Hkv ? 1 : 2);
+      const int head = kind == 0 ? hr[q] : (kind == 1 ? hr[q] - Hq : hr[q] - Hq - Hkv);
+      const uint32_t b32 = (uint32_t)row[q] / (uint32_t)L;
+      const int64_t b = b32, s = (int64_t)((uint32_t)row[q] - b32 * (uint32_t)L);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[q]);
+      float x[8];
+      float ss_ = 0.f;
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const float x0 = x[2 * p] * r * __bfloat162float(w[2 * p]);
-        const float x1 = x[2 * p + 1] * r * __bfloat162float(w[2 * p + 1]);
-        const float2 cs = __ldg(f + p);
-        const float re = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-        const float im = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-        __nv_bfloat162 t = __floats2bfloat162_rn(re, im);
-        op[p] = *reinterpret_cast<uint32_t*>(&t);
+      for (int j = 0; j < 8; ++j) {
+        x[j] = __bfloat162float(e[j]);
+        ss_ = fmaf(x[j], x[j], ss_);
       }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss_ += __shfl_xor_sync(0xffffffffu, ss_, o, 16);
+      if (!valid[q] || sub >= nout) continue;
+      uint4 outv = raw[q];  // zeros on the padding lanes
+      if (kind != 2 && sub < nin) {
+        const float r = __frsqrt_rn(ss_ / (float)D + eps);
+        const __nv_bfloat16* w = (kind == 0 ? qw : kw) + sub * 8;
+        const float2* f = freqs + b * fb + s * fs + sub * 4;
+        uint32_t* op = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float x0 = x[2 * p] * r * __bfloat162float(w[2 * p]);
+          const float x1 = x[2 * p + 1] * r * __bfloat162float(w[2 * p + 1]);
+          const float2 cs = __ldg(f + p);
+          const float re = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+          const float im = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+          __nv_bfloat162 t = __floats2bfloat162_rn(re, im);
+          op[p] = *reinterpret_cast<uint32_t*>(&t);
+        }
+      }
+      __nv_bfloat16* d = dst.p[kind] + b * dst.sb[kind] + s * dst.ss[kind] + (int64_t)head * dst.sh[kind] + sub * 8;
+      *reinterpret_cast<uint4*>(d) = outv;
     }
-    __nv_bfloat16* d = dst.p[kind] + b * dst.sb[kind] + s * dst.ss[kind] + (int64_t)head * dst.sh[kind] + sub * 8;
-    *reinterpret_cast<uint4*>(d) = outv;
   }
 }
 
@@ -241,8 +256,9 @@ extern "C" int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_
   if (freqs_strides[0] % 2 || freqs_strides[1] % 2) return QF2_ERR_ALIGN;
   const int64_t rows = B * L;
   const int64_t units = rows * (Hq + 2 * Hkv);
-  int64_t blocks = (units + 15) / 16;
-  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (units >= (int64_t)1 << 31 || L >= (int64_t)1 << 31) return QF2_ERR_SHAPE;
+  int64_t blocks = (units + 31) / 32;
+  if (blocks > 148 * 16) blocks = 148 * 16;
   qkv_norm_rope_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, rows, L, (int)Hq, (int)Hkv, (int)D, (int)Dout, dst,
       reinterpret_cast<const __nv_bfloat16*>(q_weight), reinterpret_cast<const __nv_bfloat16*>(k_weight), eps,

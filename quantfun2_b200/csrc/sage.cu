@@ -310,7 +310,7 @@ struct AttnSmem {
   static constexpr int p = kv + kStages * 2 * kTileBytes;       // one P tile per Q tile
   static constexpr int kscale = p + 2 * kTileBytes;             // up to kMaxKvTiles x 16 B
   static constexpr int bars = kscale + kMaxKvTiles * 16;
-  static constexpr int nbars = 1 + 2 * kStages + 2 * 4 + 1;
+  static constexpr int nbars = 1 + 2 * kStages + 2 * 5 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int total = misc + 64;
   static constexpr int alloc = total + 1024;  // slack for manual 1024-B alignment
@@ -411,7 +411,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   uint64_t* bar_s_empty = bar_s_full + 2;          // [2]
   uint64_t* bar_p_full = bar_s_empty + 2;          // [2 tiles]
   uint64_t* bar_o_done = bar_p_full + 2;           // [2 tiles]: PV_t(i) completed
-  uint64_t* bar_drain = bar_o_done + 2;
+  uint64_t* bar_pp = bar_o_done + 2;
+  uint64_t* bar_drain = bar_pp + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + AttnSmem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + AttnSmem::misc + 8);
 
@@ -425,6 +426,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       mbar_init(bar_s_empty + t, 4);
       mbar_init(bar_p_full + t, 4);
       mbar_init(bar_o_done + t, 1);
+      mbar_init(bar_pp + t, 4);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -607,6 +609,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       const float2 sc0v = make_float2(sc0, sc0), sc1v = make_float2(sc1, sc1);
       // P_t was last read by PV_t(j-1); its completion also orders the O rescale below
       if (j >= 1 && !wwait(bar_o_done + t, (j - 1) & 1)) { ok = false; break; }
+      if (ntile == 2) {
+        if (t == 1 && !wwait(bar_pp, j & 1)) { ok = false; break; }
+        if (t == 0 && j >= 1 && !wwait(bar_pp + 1, (j - 1) & 1)) { ok = false; break; }
+      }
       uint8_t* pdst = sP + t * kTileBytes;
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
@@ -626,6 +632,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         *reinterpret_cast<uint4*>(pdst + swz(row, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l_run += acc.x + acc.y;
+      if (ntile == 2) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_pp + t);
+      }
       if (rescale && j > 0) {
         // O holds sum_{i<j} P_i V_i against the old max (PV(j-1) completed above);
         // PV(j) is only issued after p_full(j) below
