@@ -60,6 +60,8 @@ def parse():
     p.add_argument("--no-flux", action="store_true")
     p.add_argument("--no-lumina", action="store_true")
     p.add_argument("--no-blocksparse", action="store_true")
+    p.add_argument("--flux-sides", default="64,128",
+                   help="image-token grid sides of the Flux step (64 -> 4608 tokens, 128 -> 16,896)")
     p.add_argument("--profile", action="store_true",
                    help="for ncu runs: no clock soak, no cuBLAS peak, no CPU baseline, no 8-sample Lumina batch")
     return p.parse_args()
@@ -471,7 +473,7 @@ def run_ours(args, rank: int, world: int, dev):
     if not args.no_flux:
         del q, k, v, out, ws
         torch.cuda.empty_cache()
-        flux = run_flux_step(rank, world, dev)
+        flux = run_flux_step(rank, world, dev, sides=tuple(int(x) for x in args.flux_sides.split(",")))
     # ---- the Lumina-shaped denoise step (batch-parallel: one sample per rank; on one GPU
     # also the 8-sample batch)
     lumina = None

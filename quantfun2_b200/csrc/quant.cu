@@ -94,17 +94,17 @@ QF2_DEV void store8(void* out, int64_t off, const float* y, bool fp8, float inv)
   }
 }
 
-template <typename T>
+template <typename T, int NV>
 __global__ void __launch_bounds__(256) quantize_rows_vec_kernel(const T* __restrict__ x, int64_t ldx, int K, void* q,
                                                                 int64_t ldq, int fp8, float* __restrict__ scales) {
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * ldx;
   const int nv = K / 8;
-  uint4 raw[kRowVecs];
+  uint4 raw[NV];
   float am = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowVecs; ++c) {
+  for (int c = 0; c < NV; ++c) {
     const int vi = threadIdx.x + c * 256;
     raw[c] = vi < nv ? *reinterpret_cast<const uint4*>(xr + vi * 8) : make_uint4(0, 0, 0, 0);
     const T* e = reinterpret_cast<const T*>(&raw[c]);
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(256) quantize_rows_vec_kernel(const T* __restr
   const float sc = fp8 ? (am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f) : fmaxf(__fdiv_rn(am, 127.5f), FLT_EPSILON);
   if (threadIdx.x == 0) scales[row] = sc;
 #pragma unroll
-  for (int c = 0; c < kRowVecs; ++c) {
+  for (int c = 0; c < NV; ++c) {
     const int vi = threadIdx.x + c * 256;
     if (vi >= nv) continue;
     const T* e = reinterpret_cast<const T*>(&raw[c]);
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(256) quantize_rows_vec_kernel(const T* __restr
 // adaLN: y = LayerNorm(x) * (1 + scale[b]) + shift[b] (LayerNorm without affine, fp32
 // statistics), written as bf16 or as e4m3 with a per-row scale for the next GEMM.
 // Same row constraints as the fast quantizer.
-template <typename T>
+template <typename T, int NV>
 __global__ void __launch_bounds__(256) ln_modulate_kernel(const T* __restrict__ x, int64_t ldx, int N,
                                                           const __nv_bfloat16* __restrict__ shift,
                                                           const __nv_bfloat16* __restrict__ scale, int64_t mod_stride,
@@ -153,10 +153,10 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const T* __restrict__ 
   const __nv_bfloat16* sh = shift + bi * mod_stride;
   const __nv_bfloat16* scl = scale + bi * mod_stride;
   const int nv = N / 8;
-  float v[kRowVecs][8];
+  float v[NV][8];
   float sum = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowVecs; ++c) {
+  for (int c = 0; c < NV; ++c) {
     const int vi = threadIdx.x + c * 256;
     uint4 raw = vi < nv ? *reinterpret_cast<const uint4*>(xr + vi * 8) : make_uint4(0, 0, 0, 0);
     const T* e = reinterpret_cast<const T*>(&raw);
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const T* __restrict__ 
   const float mean = block_sum(sum, red) / (float)N;
   float sq = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowVecs; ++c) {
+  for (int c = 0; c < NV; ++c) {
     const int vi = threadIdx.x + c * 256;
     if (vi < nv) {
 #pragma unroll
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const T* __restrict__ 
   const float rstd = rsqrtf(block_sum(sq, red) / (float)N + eps);
   float am = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowVecs; ++c) {
+  for (int c = 0; c < NV; ++c) {
     const int vi = threadIdx.x + c * 256;
     if (vi < nv) {
       const uint4 a = *reinterpret_cast<const uint4*>(sh + vi * 8);
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const T* __restrict__ 
     if (threadIdx.x == 0) scales[row] = am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f;
   }
 #pragma unroll
-  for (int c = 0; c < kRowVecs; ++c) {
+  for (int c = 0; c < NV; ++c) {
     const int vi = threadIdx.x + c * 256;
     if (vi < nv) store8(out, row * ldo + vi * 8, v[c], fp8 != 0, inv);
   }
@@ -258,6 +258,39 @@ __global__ void __launch_bounds__(256) codes_to_bf16_vec_kernel(const uint8_t* _
   }
 }
 
+// Rows are held in registers, NV 16-byte vectors per thread of 256: the smallest NV that
+// covers the row keeps the register count (and so the number of resident rows per SM) up.
+static int vecs_per_thread(int64_t n) {
+  const int64_t v = (n / 8 + 255) / 256;
+  return v <= 1 ? 1 : v <= 2 ? 2 : v <= 4 ? 4 : 8;
+}
+
+template <typename T>
+static void launch_rows(int nv, const T* x, int64_t ldx, int K, void* q, int64_t ldq, int fp8, float* scales,
+                        int64_t M, cudaStream_t s) {
+  switch (nv) {
+    case 1: quantize_rows_vec_kernel<T, 1><<<(unsigned)M, 256, 0, s>>>(x, ldx, K, q, ldq, fp8, scales); break;
+    case 2: quantize_rows_vec_kernel<T, 2><<<(unsigned)M, 256, 0, s>>>(x, ldx, K, q, ldq, fp8, scales); break;
+    case 4: quantize_rows_vec_kernel<T, 4><<<(unsigned)M, 256, 0, s>>>(x, ldx, K, q, ldq, fp8, scales); break;
+    default: quantize_rows_vec_kernel<T, 8><<<(unsigned)M, 256, 0, s>>>(x, ldx, K, q, ldq, fp8, scales); break;
+  }
+}
+
+template <typename T>
+static void launch_ln(int nv, const T* x, int64_t ldx, int N, const __nv_bfloat16* sh, const __nv_bfloat16* sc,
+                      int64_t mod_stride, int64_t rpb, float eps, void* out, int64_t ldo, int fp8, float* scales,
+                      int64_t M, cudaStream_t s) {
+#define QF2_LN(V) ln_modulate_kernel<T, V><<<(unsigned)M, 256, 0, s>>>(x, ldx, N, sh, sc, mod_stride, rpb, eps, out, \
+                                                                     ldo, fp8, scales)
+  switch (nv) {
+    case 1: QF2_LN(1); break;
+    case 2: QF2_LN(2); break;
+    case 4: QF2_LN(4); break;
+    default: QF2_LN(8); break;
+  }
+#undef QF2_LN
+}
+
 }  // namespace quant
 }  // namespace qf2
 
@@ -276,10 +309,9 @@ extern "C" int qf2_quantize_rows(const void* x, int64_t ldx, int x_dtype, int64_
                    (reinterpret_cast<uintptr_t>(q) & 7) == 0 && (ldq % 8) == 0;
   if (vec) {
     if (x_dtype == QF2_BF16)
-      quantize_rows_vec_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, s>>>((const __nv_bfloat16*)x, ldx, (int)K, q,
-                                                                         ldq, fp8, scales);
+      launch_rows<__nv_bfloat16>(vecs_per_thread(K), (const __nv_bfloat16*)x, ldx, (int)K, q, ldq, fp8, scales, M, s);
     else
-      quantize_rows_vec_kernel<__half><<<(unsigned)M, 256, 0, s>>>((const __half*)x, ldx, (int)K, q, ldq, fp8, scales);
+      launch_rows<__half>(vecs_per_thread(K), (const __half*)x, ldx, (int)K, q, ldq, fp8, scales, M, s);
     QF2_LAUNCH_CHECK();
     return QF2_OK;
   }
@@ -344,12 +376,11 @@ extern "C" int qf2_ln_modulate(const void* x, int64_t ldx, int x_dtype, const vo
   const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(scale);
   const int fp8 = out_dtype == QF2_E4M3;
   if (x_dtype == QF2_BF16)
-    ln_modulate_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, s>>>((const __nv_bfloat16*)x, ldx, (int)N, sh, sc,
-                                                                   mod_stride, rows_per_batch, eps, out, ldo, fp8,
-                                                                   scales);
+    launch_ln<__nv_bfloat16>(vecs_per_thread(N), (const __nv_bfloat16*)x, ldx, (int)N, sh, sc, mod_stride,
+                             rows_per_batch, eps, out, ldo, fp8, scales, M, s);
   else
-    ln_modulate_kernel<__half><<<(unsigned)M, 256, 0, s>>>((const __half*)x, ldx, (int)N, sh, sc, mod_stride,
-                                                            rows_per_batch, eps, out, ldo, fp8, scales);
+    launch_ln<__half>(vecs_per_thread(N), (const __half*)x, ldx, (int)N, sh, sc, mod_stride, rows_per_batch, eps, out,
+                      ldo, fp8, scales, M, s);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }

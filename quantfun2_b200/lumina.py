@@ -108,10 +108,10 @@ class LuminaBlock(nn.Module):
         qkv_norm_rope(qkv.view(B, L, -1), H, self.q_norm, self.k_norm, freqs, q, k, v, eps=1e-6, Hkv=Hk)
         o = sageattn(q, k, v, tensor_layout="NHD", sm_scale=1.0 / math.sqrt(self.hd))
         y = self.wo.run(o.view(B * L, H * hp), None)
-        rms_gate_residual(x2, y, h, L, self.attention_norm2, self.eps, g_msa, True, self.ffn_norm1, self.eps, s_mlp)
+        rms_gate_residual(x2, y, h, L, self.attention_norm2, self.eps, g_msa, False, self.ffn_norm1, self.eps, s_mlp)
         f = self.w13.run(h, None, glu=True)
         y = self.w2.run(f, None)
-        rms_gate_residual(x2, y, h if next_norm is not None else None, L, self.ffn_norm2, self.eps, g_mlp, True,
+        rms_gate_residual(x2, y, h if next_norm is not None else None, L, self.ffn_norm2, self.eps, g_mlp, False,
                           next_norm, next_eps, next_scale)
         return x
 
@@ -190,6 +190,10 @@ class LuminaDiT(nn.Module):
         D = self.dim
         temb = self.t_mlp2(F.silu(self.t_mlp1(self.timestep_embedding(t))))  # [B, tdim]
         mods_all = self.adaLN(F.silu(temb))  # [B, (n_mod * 4 + 1) * dim]
+        # tanh of every gate once per step, in bf16 like the reference's gate.tanh()
+        # (model.py:87, 94); the fused residual pass then takes the gates as they are
+        n_mod_all = (mods_all.shape[1] - D) // (4 * D)
+        mods_all[:, :4 * D * n_mod_all].view(B, n_mod_all, 4, D)[:, :, 1::2].tanh_()
         n_ref = len(self.noise_refiner)
         mod = lambda i: mods_all[:, 4 * D * i:4 * D * (i + 1)]  # noqa: E731
         # caption embedder: RMSNorm + linear (model.py:210-212)
