@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   uint64_t* bar_s_empty = bar_s_full + 2;          // [2]
   uint64_t* bar_p_full = bar_s_empty + 2;          // [2 tiles]
   uint64_t* bar_o_done = bar_p_full + 2;           // [2 tiles]: PV_t(i) completed
-  uint64_t* bar_pp = bar_o_done + 2;
+  uint64_t* bar_pp = bar_o_done + 2;              // [2 tiles]: softmax t is far enough into its exp pass
   uint64_t* bar_drain = bar_pp + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + AttnSmem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + AttnSmem::misc + 8);
@@ -609,7 +609,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       const float2 sc0v = make_float2(sc0, sc0), sc1v = make_float2(sc1, sc1);
       // P_t was last read by PV_t(j-1); its completion also orders the O rescale below
       if (j >= 1 && !wwait(bar_o_done + t, (j - 1) & 1)) { ok = false; break; }
-      if (ntile == 2) {
+      if (ntile == 2) {  // ping-pong (see the arrive in the exp pass below)
         if (t == 1 && !wwait(bar_pp, j & 1)) { ok = false; break; }
         if (t == 0 && j >= 1 && !wwait(bar_pp + 1, (j - 1) & 1)) { ok = false; break; }
       }
@@ -630,12 +630,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
           w[q4] = (uint32_t)f32x2_to_e4m3x2(p01.x, p01.y) | ((uint32_t)f32x2_to_e4m3x2(p23.x, p23.y) << 16);
         }
         *reinterpret_cast<uint4*>(pdst + swz(row, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
+        // ping-pong of the two softmax warpgroups over the SFU: tile 1's exp pass of
+        // iteration j starts when tile 0's is three quarters done, tile 0's of j + 1 when
+        // tile 1's is (measured: the exp pass of one warpgroup alone does not fill the
+        // SFU, two fully overlapped ones leave it idle during the max passes)
+        if (ntile == 2 && chunk == 5) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_pp + t);
+        }
       }
       l_run += acc.x + acc.y;
-      if (ntile == 2) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_pp + t);
-      }
       if (rescale && j > 0) {
         // O holds sum_{i<j} P_i V_i against the old max (PV(j-1) completed above);
         // PV(j) is only issued after p_full(j) below
