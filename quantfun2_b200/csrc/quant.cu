@@ -209,6 +209,92 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const T* __restrict__ 
   }
 }
 
+// Same operation, one warp per row for N % 256 == 0 (NV = N / 256 vectors per lane): the
+// statistics are warp shuffles (no CTA-wide barrier between the load and the store) and
+// the row is re-read from L1 in the later passes instead of being held in registers, so
+// many rows stay resident per SM.  Mean and variance come from sums shifted by the row's
+// first element (stable when the mean is large against the spread).
+QF2_DEV float warp_allsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+QF2_DEV float warp_allmax(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(256, 2) ln_modulate_warp_kernel(const T* __restrict__ x, int64_t ldx, int64_t M,
+                                                                  const __nv_bfloat16* __restrict__ shift,
+                                                                  const __nv_bfloat16* __restrict__ scale,
+                                                                  int64_t mod_stride, int64_t rows_per_batch,
+                                                                  float eps, void* out, int64_t ldo, int fp8,
+                                                                  float* __restrict__ scales) {
+  constexpr int N = NV * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const T* xr = x + row * ldx;
+  const int64_t bi = row / rows_per_batch;
+  const __nv_bfloat16* sh = shift + bi * mod_stride;
+  const __nv_bfloat16* scl = scale + bi * mod_stride;
+  const float x0 = to_f32(xr[0]);
+  float s1 = 0.f, s2 = 0.f;
+  {
+    uint4 raw[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) raw[i] = *reinterpret_cast<const uint4*>(xr + (i * 32 + lane) * 8);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const T* e = reinterpret_cast<const T*>(&raw[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = to_f32(e[j]) - x0;
+        s1 += d;
+        s2 = fmaf(d, d, s2);
+      }
+    }
+  }
+  const float m1 = warp_allsum(s1) / (float)N;
+  const float var = fmaxf(warp_allsum(s2) / (float)N - m1 * m1, 0.f);
+  const float mean = x0 + m1;
+  const float rstd = rsqrtf(var + eps);
+  auto modulated = [&](int i, float* y) {
+    const int c = (i * 32 + lane) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(sh + c));
+    const uint4 bsc = __ldg(reinterpret_cast<const uint4*>(scl + c));
+    const __nv_bfloat16* ae = reinterpret_cast<const __nv_bfloat16*>(&a);
+    const __nv_bfloat16* be = reinterpret_cast<const __nv_bfloat16*>(&bsc);
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      y[j] = fmaf((to_f32(e[j]) - mean) * rstd, 1.0f + __bfloat162float(be[j]), __bfloat162float(ae[j]));
+  };
+  float inv = 1.f;
+  if (fp8) {
+    float am = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < NV; ++i) {
+      float y[8];
+      modulated(i, y);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(y[j]));
+    }
+    am = warp_allmax(am);
+    inv = am > 0.f ? __fdiv_rn(448.0f, am) : 1.0f;
+    if (lane == 0) scales[row] = am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f;
+  }
+#pragma unroll 4
+  for (int i = 0; i < NV; ++i) {
+    float y[8];
+    modulated(i, y);
+    store8(out, row * ldo + (i * 32 + lane) * 8, y, fp8 != 0, inv);
+  }
+}
+
 // code -> bf16 (exact for int8 and e4m3 codes)
 __global__ void __launch_bounds__(256) codes_to_bf16_kernel(const void* q, int64_t ldq, int fp8, int64_t M, int64_t K,
                                                             __nv_bfloat16* __restrict__ out, int64_t ldo) {
@@ -280,6 +366,24 @@ template <typename T>
 static void launch_ln(int nv, const T* x, int64_t ldx, int N, const __nv_bfloat16* sh, const __nv_bfloat16* sc,
                       int64_t mod_stride, int64_t rpb, float eps, void* out, int64_t ldo, int fp8, float* scales,
                       int64_t M, cudaStream_t s) {
+  if (N % 256 == 0 && N / 256 <= 16) {
+    const unsigned grid = (unsigned)((M + 7) / 8);
+#define QF2_LNW(V) ln_modulate_warp_kernel<T, V><<<grid, 256, 0, s>>>(x, ldx, M, sh, sc, mod_stride, rpb, eps, out, \
+                                                                     ldo, fp8, scales)
+    switch (N / 256) {
+      case 1: QF2_LNW(1); return;
+      case 2: QF2_LNW(2); return;
+      case 3: QF2_LNW(3); return;
+      case 4: QF2_LNW(4); return;
+      case 6: QF2_LNW(6); return;
+      case 8: QF2_LNW(8); return;
+      case 9: QF2_LNW(9); return;
+      case 12: QF2_LNW(12); return;
+      case 16: QF2_LNW(16); return;
+      default: break;
+    }
+#undef QF2_LNW
+  }
 #define QF2_LN(V) ln_modulate_kernel<T, V><<<(unsigned)M, 256, 0, s>>>(x, ldx, N, sh, sc, mod_stride, rpb, eps, out, \
                                                                      ldo, fp8, scales)
   switch (nv) {

@@ -315,6 +315,109 @@ __global__ void __launch_bounds__(1024) gate_residual_kernel(GateResArgs a) {
   }
 }
 
+// One warp per row (dim = NV * 256): y is read once into registers for its sum of squares,
+// the updated x is kept packed (bf16) for the second norm, and the per-channel vectors
+// (weights, gate, scale) come from L1.  No CTA-wide barrier.
+QF2_DEV float warp_sum32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256, 2) gate_residual_warp_kernel(GateResArgs a) {
+  constexpr int D = NV * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const int64_t b = row / a.rows_per_batch;
+  uint4 xn[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) xn[i] = *reinterpret_cast<const uint4*>(a.x + row * D + (i * 32 + lane) * 8);
+  if (a.y != nullptr) {
+    uint4 yr[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) yr[i] = *reinterpret_cast<const uint4*>(a.y + row * D + (i * 32 + lane) * 8);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&yr[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(__bfloat162float(e[j]), __bfloat162float(e[j]), ss);
+    }
+    const float r = a.w_post != nullptr ? __frsqrt_rn(warp_sum32(ss) / (float)D + a.eps_post) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      float xv[8], yv[8], w[8], g[8];
+      const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xn[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[j] = __bfloat162float(xe[j]);
+      const __nv_bfloat16* ye = reinterpret_cast<const __nv_bfloat16*>(&yr[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) yv[j] = __bfloat162float(ye[j]);
+      if (a.w_post != nullptr) {
+        ld8(a.w_post + c, w);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = 1.0f;
+      }
+      if (a.gate != nullptr) {
+        ld8(a.gate + b * a.gate_stride + c, g);
+        if (a.gate_tanh) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) asm("tanh.approx.f32 %0, %1;" : "=f"(g[j]) : "f"(g[j]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] = 1.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[j] = fmaf(g[j], yv[j] * r * w[j], xv[j]);
+      uint32_t* wp = reinterpret_cast<uint32_t*>(&xn[i]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __nv_bfloat162 t = __floats2bfloat162_rn(xv[2 * q], xv[2 * q + 1]);
+        wp[q] = *reinterpret_cast<uint32_t*>(&t);
+      }
+      *reinterpret_cast<uint4*>(a.x + row * D + c) = xn[i];
+    }
+  }
+  if (a.h != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&xn[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(__bfloat162float(e[j]), __bfloat162float(e[j]), ss);
+    }
+    const float r = __frsqrt_rn(warp_sum32(ss) / (float)D + a.eps_pre);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      float xv[8], w[8], sc[8], o[8];
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&xn[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[j] = __bfloat162float(e[j]);
+      if (a.w_pre != nullptr) {
+        ld8(a.w_pre + c, w);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = 1.0f;
+      }
+      if (a.scale != nullptr) {
+        ld8(a.scale + b * a.scale_stride + c, sc);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sc[j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = xv[j] * r * w[j] * (1.0f + sc[j]);
+      st8(a.h + row * D + c, o);
+    }
+  }
+}
+
 }  // namespace rms
 }  // namespace qf2
 
@@ -348,7 +451,12 @@ extern "C" int qf2_rms_gate_residual(const void* y, void* x, void* h, int64_t ro
   a.dim = (int)dim;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (rows > 0x7fffffff) return QF2_ERR_SHAPE;
-  gate_residual_kernel<<<(unsigned)rows, (unsigned)(dim / 8), 0, st>>>(a);
+  switch (dim / 256) {
+    case 8: gate_residual_warp_kernel<8><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(a); break;
+    case 9: gate_residual_warp_kernel<9><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(a); break;
+    case 12: gate_residual_warp_kernel<12><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(a); break;
+    default: gate_residual_kernel<<<(unsigned)rows, (unsigned)(dim / 8), 0, st>>>(a); break;
+  }
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }

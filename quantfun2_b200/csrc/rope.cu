@@ -155,74 +155,87 @@ struct QkvDst {
   int64_t sb[3], ss[3], sh[3];
 };
 
-// 16 lanes per head row (8 elements each), 16 head rows per 256-thread CTA pass
-__global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld,
+// One CTA per token row: 16 groups of 16 lanes; group g handles head rows g, g + 16, ...
+// (up to 8 passes, Hq + 2 Hkv <= 128), lane `sub` holds 8 elements of its head row.  The
+// token's RoPE factors and the q / k norm weights are per-lane constants loaded once; all
+// of the row's loads are issued before any arithmetic.
+constexpr int kQkvPasses = 8;
+
+QF2_DEV void unpack_bf16x8(const uint4& v, float* f) {
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = __bfloat162float(e[j]);
+}
+
+template <int NP>
+__global__ void __launch_bounds__(256, 4) qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld,
                                                             int64_t rows, int64_t L, int Hq, int Hkv, int D, int Dout,
                                                             QkvDst dst, const __nv_bfloat16* __restrict__ qw,
                                                             const __nv_bfloat16* __restrict__ kw, float eps,
                                                             const float2* __restrict__ freqs, int64_t fb, int64_t fs) {
   const int sub = threadIdx.x & 15, grp = threadIdx.x >> 4;
   const int Ht = Hq + 2 * Hkv;
-  const int64_t units = rows * Ht;
+  const int npass = (Ht + 15) >> 4;
+  const int64_t row = blockIdx.x;
+  const uint32_t b32 = (uint32_t)row / (uint32_t)L;
+  const int64_t b = b32, s = (int64_t)((uint32_t)row - b32 * (uint32_t)L);
   const int nin = D / 8, nout = Dout / 8;
-  constexpr int U = 2;  // head rows per 16-lane group per pass, loads issued together
-  // the loop bound is CTA-uniform so both 16-lane groups of a warp always reach the
-  // shuffles together; out-of-range groups compute on zeros and store nothing
-  for (int64_t base = (int64_t)blockIdx.x * 16 * U; base < units; base += (int64_t)gridDim.x * 16 * U) {
-    uint4 raw[U];
-    int64_t row[U];
-    int hr[U];
-    bool valid[U];
+  const bool lane_in = sub < nin;
+  uint4 raw[NP];
 #pragma unroll
-    for (int q = 0; q < U; ++q) {
-      const int64_t u = base + q * 16 + grp;
-      valid[q] = u < units;
-      // 32-bit division (units < 2^31 is checked on the host): 64-bit division by a
-      // runtime divisor costs more than the rest of the row's work
-      const uint32_t u32 = valid[q] ? (uint32_t)u : 0u;
-      row[q] = (int64_t)(u32 / (uint32_t)Ht);
-      hr[q] = (int)(u32 - (uint32_t)row[q] * (uint32_t)Ht);
-      raw[q] = (valid[q] && sub < nin)
-                   ? *reinterpret_cast<const uint4*>(qkv + row[q] * ld + (int64_t)hr[q] * D + sub * 8)
-                   : make_uint4(0, 0, 0, 0);
-    }
+  for (int u = 0; u < NP; ++u) {
+    const int hr = grp + 16 * u;
+    raw[u] = (u < npass && hr < Ht && lane_in)
+                 ? *reinterpret_cast<const uint4*>(qkv + row * ld + (int64_t)hr * D + sub * 8)
+                 : make_uint4(0, 0, 0, 0);
+  }
+  float2 cs[4];
+  uint4 wq = make_uint4(0, 0, 0, 0), wk = make_uint4(0, 0, 0, 0);
+  if (lane_in) {
+    const float2* f = freqs + b * fb + s * fs + sub * 4;
 #pragma unroll
-    for (int q = 0; q < U; ++q) {
-      const int kind = hr[q] < Hq ? 0 : (hr[q] < Hq + Hkv ? 1 : 2);
-      const int head = kind == 0 ? hr[q] : (kind == 1 ? hr[q] - Hq : hr[q] - Hq - Hkv);
-      const uint32_t b32 = (uint32_t)row[q] / (uint32_t)L;
-      const int64_t b = b32, s = (int64_t)((uint32_t)row[q] - b32 * (uint32_t)L);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[q]);
-      float x[8];
-      float ss_ = 0.f;
+    for (int p = 0; p < 4; ++p) cs[p] = __ldg(f + p);
+    wq = __ldg(reinterpret_cast<const uint4*>(qw + sub * 8));
+    wk = __ldg(reinterpret_cast<const uint4*>(kw + sub * 8));
+  } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        x[j] = __bfloat162float(e[j]);
-        ss_ = fmaf(x[j], x[j], ss_);
+    for (int p = 0; p < 4; ++p) cs[p] = make_float2(0.f, 0.f);
+  }
+#pragma unroll
+  for (int u = 0; u < NP; ++u) {
+    if (u >= npass) break;  // CTA-uniform: every lane reaches the shuffles below
+    const int hr = grp + 16 * u;
+    float x[8];
+    unpack_bf16x8(raw[u], x);
+    float ss_ = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss_ = fmaf(x[j], x[j], ss_);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss_ += __shfl_xor_sync(0xffffffffu, ss_, o, 16);
+    if (hr >= Ht || sub >= nout) continue;
+    const int kind = hr < Hq ? 0 : (hr < Hq + Hkv ? 1 : 2);
+    const int head = kind == 0 ? hr : (kind == 1 ? hr - Hq : hr - Hq - Hkv);
+    uint4 outv = raw[u];  // zeros on the padding lanes
+    if (kind != 2 && lane_in) {
+      const float r = __frsqrt_rn(ss_ / (float)D + eps);
+      float w[8];
+      unpack_bf16x8(kind == 0 ? wq : wk, w);
+      uint32_t* op = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const float x0 = x[2 * p] * r * w[2 * p];
+        const float x1 = x[2 * p + 1] * r * w[2 * p + 1];
+        const float re = __fsub_rn(__fmul_rn(x0, cs[p].x), __fmul_rn(x1, cs[p].y));
+        const float im = __fadd_rn(__fmul_rn(x0, cs[p].y), __fmul_rn(x1, cs[p].x));
+        __nv_bfloat162 t = __floats2bfloat162_rn(re, im);
+        op[p] = *reinterpret_cast<uint32_t*>(&t);
       }
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ss_ += __shfl_xor_sync(0xffffffffu, ss_, o, 16);
-      if (!valid[q] || sub >= nout) continue;
-      uint4 outv = raw[q];  // zeros on the padding lanes
-      if (kind != 2 && sub < nin) {
-        const float r = __frsqrt_rn(ss_ / (float)D + eps);
-        const __nv_bfloat16* w = (kind == 0 ? qw : kw) + sub * 8;
-        const float2* f = freqs + b * fb + s * fs + sub * 4;
-        uint32_t* op = reinterpret_cast<uint32_t*>(&outv);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float x0 = x[2 * p] * r * __bfloat162float(w[2 * p]);
-          const float x1 = x[2 * p + 1] * r * __bfloat162float(w[2 * p + 1]);
-          const float2 cs = __ldg(f + p);
-          const float re = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-          const float im = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-          __nv_bfloat162 t = __floats2bfloat162_rn(re, im);
-          op[p] = *reinterpret_cast<uint32_t*>(&t);
-        }
-      }
-      __nv_bfloat16* d = dst.p[kind] + b * dst.sb[kind] + s * dst.ss[kind] + (int64_t)head * dst.sh[kind] + sub * 8;
-      *reinterpret_cast<uint4*>(d) = outv;
     }
+    // select by kind without indexing the parameter arrays (keeps them out of local memory)
+    __nv_bfloat16* d = kind == 0 ? dst.p[0] + b * dst.sb[0] + s * dst.ss[0] + (int64_t)head * dst.sh[0]
+                     : kind == 1 ? dst.p[1] + b * dst.sb[1] + s * dst.ss[1] + (int64_t)head * dst.sh[1]
+                                 : dst.p[2] + b * dst.sb[2] + s * dst.ss[2] + (int64_t)head * dst.sh[2];
+    *reinterpret_cast<uint4*>(d + sub * 8) = outv;
   }
 }
 
@@ -257,9 +270,10 @@ extern "C" int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_
   const int64_t rows = B * L;
   const int64_t units = rows * (Hq + 2 * Hkv);
   if (units >= (int64_t)1 << 31 || L >= (int64_t)1 << 31) return QF2_ERR_SHAPE;
-  int64_t blocks = (units + 31) / 32;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  qkv_norm_rope_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  if (Hq + 2 * Hkv > 16 * kQkvPasses) return QF2_ERR_SHAPE;
+  const int npass = (int)((Hq + 2 * Hkv + 15) / 16);
+  auto kern = npass <= 3 ? qkv_norm_rope_kernel<3> : npass <= 5 ? qkv_norm_rope_kernel<5> : qkv_norm_rope_kernel<8>;
+  kern<<<(unsigned)rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, rows, L, (int)Hq, (int)Hkv, (int)D, (int)Dout, dst,
       reinterpret_cast<const __nv_bfloat16*>(q_weight), reinterpret_cast<const __nv_bfloat16*>(k_weight), eps,
       reinterpret_cast<const float2*>(freqs_cis), freqs_strides[0], freqs_strides[1]);

@@ -30,7 +30,7 @@ constexpr int kTile = 128;          // tokens per tile (MMA M and N)
 constexpr int kHeadDim = 128;       // D
 constexpr int kTileBytes = 16384;   // 128 rows x 128 bytes of 8-bit codes
 constexpr int kQuantBlock = 64;     // tokens per INT8 scale block
-constexpr int kStatChunk = 512;     // tokens per stats partial
+constexpr int kStatChunk = 512;     // tokens per stats partial (one CTA, 32 tokens per thread)
 constexpr int kStages = 4;          // K/V smem ring depth
 constexpr int kMaxKvTiles = 512;    // k-scale smem capacity (65536 tokens)
 constexpr float kLog2_448 = 8.807354922057604f;
@@ -86,7 +86,7 @@ struct Workspace {
 // ----------------------------------------------------------------- stats --
 // grid (nch, Hkv, batch), 256 threads: thread = (row slot 0..15, 8-channel chunk 0..15)
 template <typename T>
-__global__ void __launch_bounds__(256) sage_stats_kernel(const T* __restrict__ k, Strides3 ks_, const T* __restrict__ v,
+__global__ void __launch_bounds__(256, 3) sage_stats_kernel(const T* __restrict__ k, Strides3 ks_, const T* __restrict__ v,
                                                          Strides3 vs_, SeqGeom g, int Hkv, Workspace ws) {
   const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const SeqInfo si = seq_k(g, b);
@@ -98,18 +98,41 @@ __global__ void __launch_bounds__(256) sage_stats_kernel(const T* __restrict__ k
   for (int j = 0; j < 8; ++j) { sum[j] = 0.0; amax[j] = 0.f; }
   if (t_begin < si.len) {
     const int64_t t_end = si.len < t_begin + kStatChunk ? si.len : t_begin + kStatChunk;
-    for (int64_t t = t_begin + slot; t < t_end; t += 16) {
-      const int64_t tok = si.tok0 + t;
-      const T* kr = k + (int64_t)b * ks_.b + (int64_t)h * ks_.h + tok * ks_.s + c8 * 8;
-      const T* vr = v + (int64_t)b * vs_.b + (int64_t)h * vs_.h + tok * vs_.s + c8 * 8;
-      const uint4 kk = *reinterpret_cast<const uint4*>(kr);
-      const uint4 vv = *reinterpret_cast<const uint4*>(vr);
-      const T* ke = reinterpret_cast<const T*>(&kk);
-      const T* ve = reinterpret_cast<const T*>(&vv);
+    const T* kb = k + (int64_t)b * ks_.b + (int64_t)h * ks_.h + c8 * 8;
+    const T* vb = v + (int64_t)b * vs_.b + (int64_t)h * vs_.h + c8 * 8;
+    // 4 tokens per batch, the next batch's 8 loads issued before this batch's arithmetic
+    constexpr int kBatch = 4, kBatches = kStatChunk / (16 * kBatch);
+    uint4 kc[kBatch], vc[kBatch], kn[kBatch], vn[kBatch];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        sum[j] += (double)to_f32(ke[j]);
-        amax[j] = fmaxf(amax[j], fabsf(to_f32(ve[j])));
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t t = t_begin + slot + u * 16;
+      const bool in = t < t_end;
+      kc[u] = in ? *reinterpret_cast<const uint4*>(kb + (si.tok0 + t) * ks_.s) : make_uint4(0, 0, 0, 0);
+      vc[u] = in ? *reinterpret_cast<const uint4*>(vb + (si.tok0 + t) * vs_.s) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll 1
+    for (int bt = 0; bt < kBatches; ++bt) {
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t t = t_begin + slot + ((bt + 1) * kBatch + u) * 16;
+        const bool in = bt + 1 < kBatches && t < t_end;
+        kn[u] = in ? *reinterpret_cast<const uint4*>(kb + (si.tok0 + t) * ks_.s) : make_uint4(0, 0, 0, 0);
+        vn[u] = in ? *reinterpret_cast<const uint4*>(vb + (si.tok0 + t) * vs_.s) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const T* ke = reinterpret_cast<const T*>(&kc[u]);
+        const T* ve = reinterpret_cast<const T*>(&vc[u]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          sum[j] += (double)to_f32(ke[j]);
+          amax[j] = fmaxf(amax[j], fabsf(to_f32(ve[j])));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        kc[u] = kn[u];
+        vc[u] = vn[u];
       }
     }
   }
@@ -167,7 +190,7 @@ QF2_DEV void unpack8(const uint4& raw, float* f) {
 // V tile: thread = (channel pair 0..63, 32-token group 0..3); writes rows of V^T.
 //   code = e4m3(v * (448 / amax_channel)).
 template <typename T>
-__global__ void __launch_bounds__(256) sage_quant_kernel(const T* __restrict__ q, Strides3 qs_, const T* __restrict__ k,
+__global__ void __launch_bounds__(256, 4) sage_quant_kernel(const T* __restrict__ q, Strides3 qs_, const T* __restrict__ k,
                                                          Strides3 ks_, const T* __restrict__ v, Strides3 vs_, SeqGeom g,
                                                          int Hq, int Hkv, float qmul, Workspace ws) {
   const int tile = blockIdx.x, job = blockIdx.y, b = blockIdx.z;
