@@ -10,8 +10,9 @@
 //   3. blocksparse_attn_kernel  exact softmax attention of each 128-row query block over
 //                               its kept key blocks: TMA tiles (bf16/fp16, 128-byte
 //                               swizzle) fetched by block index, tcgen05.mma kind::f16
-//                               QK^T into TMEM (double-buffered S), P through shared
-//                               memory, PV with V read as an MN-major operand, fp32 O in TMEM.
+//                               QK^T into TMEM (double-buffered S), P through two shared
+//                               memory buffers, PV with V read as an MN-major operand,
+//                               fp32 O in TMEM; 8 softmax warps, lazy rescale.
 #include "qf2_common.cuh"
 
 #include <algorithm>
@@ -88,20 +89,30 @@ __global__ void __launch_bounds__(128) blocktopk_select_kernel(const float* __re
 }
 
 // ------------------------------------------------------------- attention --
-constexpr int kThreads = 192;   // warp 0 producer, warp 1 MMA, warps 2-5 softmax
+// One CTA per 128-row query block: warp 0 TMA producer (Q once, K/V of each kept block
+// into a 2-stage ring), warp 1 MMA issuer (QK^T into a double-buffered S in TMEM, PV into
+// O in TMEM), warps 2-9 softmax.  A row's 128 scores are split over two softmax threads
+// of the same TMEM lane quarter (warps w and w + 4), 64 columns each, so two warps per
+// SM sub-partition feed the SFU; the halves exchange row maxima through shared memory.
+// Lazy rescale: the running max moves (and O is rescaled) only when a block's max
+// exceeds it by more than kTau (log2 units); P (bf16/fp16, at most 2^kTau) goes through
+// two shared-memory buffers so the next block's exps do not wait for the last PV.
+constexpr int kThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-9 softmax
 constexpr int kTile = 16384;    // 128 rows x 128 bytes (one 128-byte swizzle atom column)
 constexpr int kOpBytes = 2 * kTile;  // 128 x 128 16-bit elements
 constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
+constexpr float kTau = 8.0f;
 
 struct Smem {
   static constexpr int q = 0;
   static constexpr int kv = q + kOpBytes;          // 2 stages x (K, V)
-  static constexpr int p = kv + 2 * 2 * kOpBytes;  // P tile (single buffer)
-  static constexpr int bars = p + kOpBytes;
-  static constexpr int nbars = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+  static constexpr int p = kv + 2 * 2 * kOpBytes;  // 2 P buffers
+  static constexpr int xch = p + 2 * kOpBytes;     // row-max [j & 1][half][row] (row sums reuse it)
+  static constexpr int bars = xch + 2 * 2 * 128 * 4;
+  static constexpr int nbars = 1 + 2 + 2 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int total = misc + 64;
-  static constexpr int alloc = total + 1024;
+  static constexpr int alloc = total;  // no alignment slack: the base is declared 1024-aligned
 };
 
 struct AttnArgs {
@@ -127,25 +138,32 @@ QF2_DEV uint32_t pack2(float a, float b, bool f16) {
 __global__ void __launch_bounds__(kThreads, 1)
     blocksparse_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                             const __grid_constant__ CUtensorMap tmv, AttnArgs A) {
-  extern __shared__ uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  if (smem_u32(smem_raw) & 1023) {  // the 128-byte swizzle needs 1024-byte aligned tiles
+    if (threadIdx.x == 0) atomicExch(A.status, kDevTimeoutProducer);
+    return;
+  }
   const int hk = h / (A.Hq / A.Hkv);
   const int keep = A.keep;
   const int32_t* idx = A.idx + (((int64_t)b * A.Hq + h) * A.nb + qb) * keep;
 
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = smem_raw;
   uint8_t* sQ = base + Smem::q;
   uint8_t* sKV = base + Smem::kv;
   uint8_t* sP = base + Smem::p;
+  float* xmax = reinterpret_cast<float*>(base + Smem::xch);  // [j & 1][half][row]
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + Smem::bars);
   uint64_t* bar_q = bars;
   uint64_t* bar_kv_full = bars + 1;   // [2]
   uint64_t* bar_kv_empty = bars + 3;  // [2]
   uint64_t* bar_s_full = bars + 5;    // [2]
   uint64_t* bar_s_empty = bars + 7;   // [2]
-  uint64_t* bar_p_full = bars + 9;
-  uint64_t* bar_o_done = bars + 10;
-  uint64_t* bar_drain = bars + 11;
+  uint64_t* bar_p_full = bars + 9;    // [P buffer]: P(i) written, i & 1 = buffer
+  uint64_t* bar_o_done = bars + 11;   // [P buffer]: PV(i) completed
+  uint64_t* bar_xm = bars + 13;
+  uint64_t* bar_xl = bars + 14;
+  uint64_t* bar_drain = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + Smem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + Smem::misc + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -156,10 +174,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_kv_full + s, 1);
       mbar_init(bar_kv_empty + s, 1);
       mbar_init(bar_s_full + s, 1);
-      mbar_init(bar_s_empty + s, 4);
+      mbar_init(bar_s_empty + s, 8);
+      mbar_init(bar_o_done + s, 1);
+      mbar_init(bar_p_full + s, 8);
     }
-    mbar_init(bar_p_full, 4);
-    mbar_init(bar_o_done, 1);
+    mbar_init(bar_xm, 8);
+    mbar_init(bar_xl, 8);
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -180,6 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool w = mbar_wait(bar, parity) && (*abort_flag == 0);
     return __all_sync(0xffffffffu, w);
   };
+  // o_done[i & 1] completes once per PV(i) of that P buffer: phase i >> 1
+  auto o_wait = [&](int i) -> bool { return wwait(bar_o_done + (i & 1), (uint32_t)((i >> 1) & 1)); };
 
   if (warp == 0) {
     // ------------------------------------------------------- producer --
@@ -220,12 +242,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ab = A.f16 ? 0u : 1u;
       const uint32_t idesc_qk = make_idesc(1, ab, ab, 0, 0, kBlk, kBlk);   // K-major x K-major -> f32
       const uint32_t idesc_pv = make_idesc(1, ab, ab, 0, 1, kBlk, kD);     // P K-major x V MN-major -> f32
-      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      const uint32_t aQ = smem_u32(sQ);
       bool ok = wwait(bar_q, 0);
       auto issue_pv = [&](int i) -> bool {
-        if (!wwait(bar_p_full, i & 1)) return false;
+        if (!wwait(bar_p_full + (i & 1), (uint32_t)((i >> 1) & 1))) return false;
         tc_fence_after();
         const uint32_t aV = smem_u32(sKV + (i & 1) * 2 * kOpBytes + kOpBytes);
+        const uint32_t aP = smem_u32(sP + (i & 1) * kOpBytes);
         if (lane == 0) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -235,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t db = sdesc_sw128_mnmajor(aV + kk * 16 * 128, kTile, 1024);
             mma_f16(tmem + 256, da, db, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(bar_o_done);
+          tc_commit(bar_o_done + (i & 1));
           tc_commit(bar_kv_empty + (i & 1));
         }
         __syncwarp();
@@ -269,9 +292,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------- softmax --
+    const int sw = warp - 2;
+    const int half = sw >> 2;  // 64-column half of the row (warps 2-5: 0, 6-9: 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tO = tmem + lane_off + 256 + half * 64;
     const bool f16 = A.f16 != 0;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = keep > 0;
@@ -279,79 +305,101 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = j & 1;
       if (!wwait(bar_s_full + s, (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sr[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld32(tmem + lane_off + s * kBlk + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      uint32_t sr[64];
+      tmem_ld32(tmem + lane_off + s * kBlk + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tmem + lane_off + s * kBlk + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_s_empty + s);
 
-      const int64_t valid = A.S - (int64_t)idx[j] * kBlk;  // keys of this block inside the sequence
-      float x[128];
+      const int64_t valid = A.S - (int64_t)idx[j] * kBlk - half * 64;  // keys of this half inside the sequence
+      float x[64];
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
+      for (int i = 0; i < 64; ++i) {
         float v = __uint_as_float(sr[i]) * A.scale_log2;
         if (i >= valid) v = -INFINITY;
         x[i] = v;
         mx = fmaxf(mx, v);
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a fully masked block contributes nothing
-      const float alpha = fast_exp2(m_run - m_use);
+      float* xm = xmax + (j & 1) * 256;
+      xm[half * 128 + row] = mx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_xm);
+      if (!wwait(bar_xm, j & 1)) { ok = false; break; }
+      const float m_tile = fmaxf(mx, xm[(half ^ 1) * 128 + row]);
+      const float m_new = fmaxf(m_run, m_tile);
+      // both warps of a row pair see the same 32 rows, so they agree on the decision
+      const bool rescale = __any_sync(0xffffffffu, m_new > m_run + kTau);
+      float alpha = 1.0f;
+      if (rescale) {
+        alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
+        m_run = m_new;
+        l_run *= alpha;
+      }
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;  // a fully masked row contributes nothing
+      // P(j) goes to buffer j & 1, last read by PV(j - 2)
+      if (j >= 2 && !o_wait(j - 2)) { ok = false; break; }
+      uint8_t* pbuf = sP + (j & 1) * kOpBytes + half * kTile;  // this half's 64-key swizzle atom column
       float rs = 0.f;
-      uint32_t pk[64];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p0 = fast_exp2(x[2 * i] - m_use), p1 = fast_exp2(x[2 * i + 1] - m_use);
-        rs += p0 + p1;
-        pk[i] = pack2(p0, p1, f16);
-      }
-      l_run = l_run * alpha + rs;
-      m_run = m_new;
-      if (j > 0) {
-        // PV(j-1) has read P and finished accumulating O before both are touched
-        if (!wwait(bar_o_done, (j - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_off + 256 + c * 32, o);
-            tmem_wait_ld();
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem + lane_off + 256 + c * 32, o);
-          }
-          tmem_wait_st();
+        for (int q = 0; q < 4; ++q) {
+          const float p0 = fast_exp2(x[8 * c + 2 * q] - m_use), p1 = fast_exp2(x[8 * c + 2 * q + 1] - m_use);
+          rs += p0 + p1;
+          w[q] = pack2(p0, p1, f16);
         }
+        *reinterpret_cast<uint4*>(pbuf + row * 128 + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      // P row: 128 keys = two 64-key swizzle atoms of 8 x 16-byte chunks
+      l_run += rs;
+      if (rescale && j > 0) {
+        // O holds sum_{i<j} P_i V_i against the old max; PV(j) is issued after p_full(j)
+        if (!o_wait(j - 1)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint8_t* dst = sP + (c >> 3) * kTile + row * 128 + (((c & 7) ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+        tmem_wait_st();
       }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p_full);
+      if (lane == 0) mbar_arrive(bar_p_full + (j & 1));
     }
     if (keep > 0 && !ok) fail(kDevTimeoutSoftmax);
     // ------------------------------------------------------- epilogue --
+    float l_tot = l_run;
     if (ok && keep > 0) {
-      if (!wwait(bar_o_done, (keep - 1) & 1)) { fail(kDevTimeoutEpilogue); ok = false; }
+      // row sums of the two halves through the row-max buffer that the last iteration did
+      // not use (both halves are past its last read)
+      float* xs = xmax + (keep & 1) * 256;
+      xs[half * 128 + row] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_xl);
+      if (!wwait(bar_xl, 0) || !o_wait(keep - 1)) {
+        fail(kDevTimeoutEpilogue);
+        ok = false;
+      } else {
+        l_tot = l_run + xs[(half ^ 1) * 128 + row];
+      }
       tc_fence_after();
     }
     const int64_t tok = (int64_t)qb * kBlk + row;
-    const float inv_l = (ok && l_run > 0.f) ? 1.0f / l_run : 0.f;
+    const float inv_l = (ok && l_tot > 0.f) ? 1.0f / l_tot : 0.f;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       uint32_t o[32];
       if (ok && keep > 0) {
-        tmem_ld32(tmem + lane_off + 256 + c * 32, o);
+        tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
@@ -359,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (tok < A.S) {
         uint8_t* dst = reinterpret_cast<uint8_t*>(A.out) +
-                       2 * ((int64_t)b * A.os.b + (int64_t)h * A.os.h + tok * A.os.s + c * 32);
+                       2 * ((int64_t)b * A.os.b + (int64_t)h * A.os.h + tok * A.os.s + half * 64 + c * 32);
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           uint4 w;
