@@ -28,62 +28,130 @@ constexpr int kMaxBlocks = 1024;
 struct S3 { int64_t b, h, s; };
 
 // ------------------------------------------------------------------ pool --
-// grid (nb, Hq + Hkv, B), 128 threads (one per channel)
+// grid (nb, Hq + Hkv, B), 256 threads: thread = (row slot 0..15, 8-channel chunk 0..15);
+// each thread sums 8 rows x 8 channels from 16-byte loads issued together, the 16 row
+// slots are combined through shared memory.
 template <typename T>
-__global__ void __launch_bounds__(128) blocktopk_pool_kernel(const T* __restrict__ q, S3 qs, const T* __restrict__ k,
+__global__ void __launch_bounds__(256) blocktopk_pool_kernel(const T* __restrict__ q, S3 qs, const T* __restrict__ k,
                                                              S3 ks, int64_t S, int Hq, int Hkv, float* __restrict__ pq,
                                                              float* __restrict__ pk) {
-  const int blk = blockIdx.x, job = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+  const int blk = blockIdx.x, job = blockIdx.y, b = blockIdx.z;
+  const int slot = threadIdx.x >> 4, c8 = threadIdx.x & 15;
   const bool is_q = job < Hq;
   const int h = is_q ? job : job - Hq;
-  const T* src = (is_q ? q : k) + (int64_t)b * (is_q ? qs.b : ks.b) + (int64_t)h * (is_q ? qs.h : ks.h) + d;
+  const T* src = (is_q ? q : k) + (int64_t)b * (is_q ? qs.b : ks.b) + (int64_t)h * (is_q ? qs.h : ks.h) + c8 * 8;
   const int64_t ss = is_q ? qs.s : ks.s;
   const int64_t r0 = (int64_t)blk * kBlk;
   const int n = (int)min((int64_t)kBlk, S - r0);
+  uint4 raw[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int r = slot + 16 * u;
+    raw[u] = r < n ? *reinterpret_cast<const uint4*>(src + (r0 + r) * ss) : make_uint4(0, 0, 0, 0);
+  }
   double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int r = 0; r < n; ++r) acc[r & 7] += (double)to_f32(src[(r0 + r) * ss]);
-  // every partial sum is exact for 16-bit inputs, so the combination order is immaterial
-  const double sum = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-  const int nb = (int)((S + kBlk - 1) / kBlk);
-  float* dst = is_q ? pq + (((int64_t)b * Hq + h) * nb + blk) * kD : pk + (((int64_t)b * Hkv + h) * nb + blk) * kD;
-  dst[d] = (float)(sum / (double)n);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] += (double)to_f32(e[j]);
+  }
+  __shared__ double red[16][kD];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[slot][c8 * 8 + j] = acc[j];
+  __syncthreads();
+  if (threadIdx.x < kD) {
+    // every partial sum is exact for 16-bit inputs, so the combination order is immaterial
+    double sum = 0.0;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sum += red[r][threadIdx.x];
+    const int nb = (int)((S + kBlk - 1) / kBlk);
+    float* dst = is_q ? pq + (((int64_t)b * Hq + h) * nb + blk) * kD : pk + (((int64_t)b * Hkv + h) * nb + blk) * kD;
+    dst[threadIdx.x] = (float)(sum / (double)n);
+  }
 }
 
 // ---------------------------------------------------------------- select --
-// grid (nqb, Hq, B), 128 threads
-__global__ void __launch_bounds__(128) blocktopk_select_kernel(const float* __restrict__ pq, const float* __restrict__ pk,
+// grid (ceil(nb / kSelQ), Hq, B), 256 threads.  A CTA scores kSelQ query blocks against
+// every key block: the pooled queries (as fp64) stay in shared memory, the pooled keys go
+// through shared memory 64 blocks at a time (rows padded to 129 floats so the lanes of a
+// warp, one key block each, hit distinct banks); each thread runs 4 independent dot
+// products, each in the fixed order d = 0..127 with separately rounded fp64 products and
+// sums, rounded once to fp32.  Ranks and ascending positions follow per query block.
+constexpr int kSelQ = 16, kSelK = 64, kSelPad = kD + 1;
+
+struct SelSmem {
+  static constexpr int sq = 0;                                         // [kSelQ][kD] double
+  static constexpr int skc = sq + kSelQ * kD * 8;                       // [kSelK][kSelPad] float
+  static constexpr int sc = skc + kSelK * kSelPad * 4;                  // [kSelQ][nb] float
+  static int bytes(int nb) { return sc + kSelQ * nb * 4 + kSelQ * nb; }  // + sel [kSelQ][nb]
+};
+
+__global__ void __launch_bounds__(256) blocktopk_select_kernel(const float* __restrict__ pq, const float* __restrict__ pk,
                                                                int nb, int Hq, int Hkv, int keep, int32_t* __restrict__ idx) {
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  extern __shared__ __align__(16) uint8_t sm[];
+  double* sq = reinterpret_cast<double*>(sm + SelSmem::sq);
+  float* skc = reinterpret_cast<float*>(sm + SelSmem::skc);
+  float* sc = reinterpret_cast<float*>(sm + SelSmem::sc);
+  unsigned char* sel = sm + SelSmem::sc + kSelQ * nb * 4;
+  const int q0 = blockIdx.x * kSelQ, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   const int hk = h / (Hq / Hkv);
-  __shared__ double sq[kD];
-  __shared__ float sc[kMaxBlocks];
-  __shared__ unsigned char sel[kMaxBlocks];
-  sq[tid] = (double)pq[(((int64_t)b * Hq + h) * nb + qb) * kD + tid];
-  __syncthreads();
-  const float* kb = pk + ((int64_t)b * Hkv + hk) * nb * kD;
-  for (int j = tid; j < nb; j += blockDim.x) {
-    const float* row = kb + (int64_t)j * kD;
-    double acc = 0.0;
-    for (int d = 0; d < kD; ++d) acc = __dadd_rn(acc, __dmul_rn(sq[d], (double)row[d]));
-    sc[j] = (float)acc;
-  }
-  __syncthreads();
-  for (int j = tid; j < nb; j += blockDim.x) {
-    const float v = sc[j];
-    int rank = 0;
-    for (int i = 0; i < nb; ++i) {
-      const float u = sc[i];
-      rank += (u > v) || (u == v && i < j);
+  const int nq = min(kSelQ, nb - q0);
+  const float* qsrc = pq + (((int64_t)b * Hq + h) * nb + q0) * kD;
+  for (int i = tid; i < kSelQ * kD; i += 256) sq[i] = i < nq * kD ? (double)qsrc[i] : 0.0;
+  const float* ksrc = pk + ((int64_t)b * Hkv + hk) * nb * kD;
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int k0 = 0; k0 < nb; k0 += kSelK) {
+    __syncthreads();  // sq written / the previous chunk's reads done
+    const int nk = min(kSelK, nb - k0);
+    for (int i = tid; i < kSelK * kD; i += 256) {
+      const int r = i / kD, d = i % kD;
+      skc[r * kSelPad + d] = r < nk ? ksrc[(int64_t)(k0 + r) * kD + d] : 0.f;
     }
-    sel[j] = rank < keep;
+    __syncthreads();
+    // warp w: query blocks w, w + 8; lane: key blocks lane, lane + 32 of the chunk
+    double acc[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+    const double* qa = sq + warp * kD;
+    const double* qb2 = sq + (warp + 8) * kD;
+    const float* ka = skc + lane * kSelPad;
+    const float* kb2 = skc + (lane + 32) * kSelPad;
+#pragma unroll 4
+    for (int d = 0; d < kD; ++d) {
+      const double x0 = qa[d], x1 = qb2[d];
+      const double y0 = (double)ka[d], y1 = (double)kb2[d];
+      acc[0][0] = __dadd_rn(acc[0][0], __dmul_rn(x0, y0));
+      acc[0][1] = __dadd_rn(acc[0][1], __dmul_rn(x0, y1));
+      acc[1][0] = __dadd_rn(acc[1][0], __dmul_rn(x1, y0));
+      acc[1][1] = __dadd_rn(acc[1][1], __dmul_rn(x1, y1));
+    }
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int ql = warp + 8 * a, kl = lane + 32 * c;
+        if (kl < nk) sc[ql * nb + k0 + kl] = (float)acc[a][c];
+      }
   }
   __syncthreads();
-  int32_t* out = idx + (((int64_t)b * Hq + h) * nb + qb) * keep;
-  for (int j = tid; j < nb; j += blockDim.x) {
-    if (sel[j]) {
+  // rank of every (query block, key block): the lower index wins ties
+  for (int i = tid; i < nq * nb; i += 256) {
+    const int ql = i / nb, j = i % nb;
+    const float* row = sc + ql * nb;
+    const float v = row[j];
+    int rank = 0;
+    for (int t = 0; t < nb; ++t) {
+      const float u = row[t];
+      rank += (u > v) || (u == v && t < j);
+    }
+    sel[ql * nb + j] = rank < keep;
+  }
+  __syncthreads();
+  for (int i = tid; i < nq * nb; i += 256) {
+    const int ql = i / nb, j = i % nb;
+    if (sel[ql * nb + j]) {
       int pos = 0;
-      for (int i = 0; i < j; ++i) pos += sel[i];
-      out[pos] = j;
+      for (int t = 0; t < j; ++t) pos += sel[ql * nb + t];
+      idx[(((int64_t)b * Hq + h) * nb + q0 + ql) * keep + pos] = j;
     }
   }
 }
@@ -479,16 +547,19 @@ extern "C" int qf2_blocktopk_select(const void* q, const int64_t* q_strides, con
   const S3 qs{q_strides[0], q_strides[1], q_strides[2]}, ks{k_strides[0], k_strides[1], k_strides[2]};
   const dim3 gp((unsigned)nb, (unsigned)(Hq + Hkv), (unsigned)B);
   if (dtype == QF2_BF16)
-    blocktopk_pool_kernel<__nv_bfloat16><<<gp, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(q), qs,
+    blocktopk_pool_kernel<__nv_bfloat16><<<gp, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(q), qs,
                                                              reinterpret_cast<const __nv_bfloat16*>(k), ks, S,
                                                              (int)Hq, (int)Hkv, pq, pk);
   else
-    blocktopk_pool_kernel<__half><<<gp, 128, 0, s>>>(reinterpret_cast<const __half*>(q), qs,
+    blocktopk_pool_kernel<__half><<<gp, 256, 0, s>>>(reinterpret_cast<const __half*>(q), qs,
                                                       reinterpret_cast<const __half*>(k), ks, S, (int)Hq, (int)Hkv,
                                                       pq, pk);
   QF2_LAUNCH_CHECK();
-  blocktopk_select_kernel<<<dim3((unsigned)nb, (unsigned)Hq, (unsigned)B), 128, 0, s>>>(pq, pk, (int)nb, (int)Hq,
-                                                                                     (int)Hkv, (int)keep, idx_out);
+  const int sel_bytes = SelSmem::bytes((int)nb);
+  static std::atomic<uint64_t> sel_attr{0};
+  QF2_CUDA_CHECK(qf2_set_smem_once(blocktopk_select_kernel, SelSmem::bytes(kMaxBlocks), &sel_attr));
+  blocktopk_select_kernel<<<dim3((unsigned)((nb + kSelQ - 1) / kSelQ), (unsigned)Hq, (unsigned)B), 256, sel_bytes, s>>>(
+      pq, pk, (int)nb, (int)Hq, (int)Hkv, (int)keep, idx_out);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }
