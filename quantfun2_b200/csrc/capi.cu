@@ -45,6 +45,14 @@ bool qf2_make_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* b
   return make_tmap(map, dtype, 4, base, gdim, gstr, bdim);
 }
 
+bool qf2_make_tmap_4d_noswizzle(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[4],
+                                const uint64_t strides_bytes[3], const uint32_t box[4]) {
+  const cuuint64_t gdim[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t gstr[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  const cuuint32_t bdim[4] = {box[0], box[1], box[2], box[3]};
+  return make_tmap(map, dtype, 4, base, gdim, gstr, bdim, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
                       uint64_t stride_bytes, const uint32_t box[2]) {
   const cuuint64_t gdim[2] = {dims[0], dims[1]};

@@ -128,6 +128,23 @@ QF2_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The two halves of cluster_sync, for threads that have work to do in between (every
+// thread of every CTA of the cluster arrives once per phase, warp-convergent).
+QF2_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+QF2_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// Loads from another CTA's shared memory (shared::cluster address from mapa_shared).
+QF2_DEV double ld_dsmem_f64(uint32_t cluster_addr) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+QF2_DEV float ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
 // 2-D tiled TMA load into this CTA's shared memory whose completion is counted on an
 // mbarrier of either CTA of the pair (shared::cluster address).  No multicast.
 QF2_DEV void tma_load_2d_pair(void* smem_dst, const void* tmap, int32_t x, int32_t y, uint32_t bar_cluster_addr) {
@@ -214,11 +231,41 @@ QF2_DEV void tma_load_4d(void* smem_dst, const void* tmap, int32_t x, int32_t y,
       : "memory");
 }
 
+// L2 eviction-priority policies for the cache-hinted loads below (the whole access
+// range gets the priority).
+QF2_DEV uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+QF2_DEV uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// 4-D tiled TMA load (no multicast) with an L2 eviction-priority hint.
+QF2_DEV void tma_load_4d_hint(void* smem_dst, const void* tmap, int32_t x, int32_t y, int32_t z, int32_t w,
+                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // 2-D tiled TMA store shared -> global (bulk group completion); out-of-bounds parts of
 // the box are not written.
 QF2_DEV void tma_store_2d(const void* tmap, const void* smem_src, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
                "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+// 1-D bulk copy shared -> global (bulk group completion); both addresses 16-byte
+// aligned, size a multiple of 16.
+QF2_DEV void bulk_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst), "r"(smem_u32(smem_src)),
+               "r"(bytes)
                : "memory");
 }
 QF2_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -446,6 +493,9 @@ inline cudaError_t qf2_sm_count(int* out) {
 // the driver entry point is unavailable or the encoder rejects the layout.
 bool qf2_make_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[4],
                       const uint64_t strides_bytes[3], const uint32_t box[4]);
+// Same without swizzle (rows land in shared memory as they are in global memory).
+bool qf2_make_tmap_4d_noswizzle(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[4],
+                                const uint64_t strides_bytes[3], const uint32_t box[4]);
 // Same, 2-D (dims innermost first, byte stride of dim 1).
 bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
                       uint64_t stride_bytes, const uint32_t box[2]);

@@ -4,17 +4,19 @@
 //   sageattn(q, k, v)                      src/models/flux/attn.py:39-41   (HND)
 //   sageattn_varlen(q, k, v, cu_seqlens..) src/models/common/attn.py:109-120
 //
-// Pipeline (4 launches, all on the caller's stream):
-//   1. sage_stats_kernel      per (seq, kv head, 512-token chunk): fp64 channel sums
-//                             of K and channel amax of V -> partials
-//   2. sage_finalize_kernel   per (seq, kv head): K token mean, V per-channel scale
-//   3. sage_quant_kernel      per (128-token tile, head): Q and smoothed K to INT8 per
-//                             64-token block, V^T to FP8 e4m3; codes written in the
-//                             128-byte-swizzled K-major tile layout tcgen05 reads
-//                             directly from shared memory (one 16 KB bulk copy per tile)
-//   4. sage_attn_kernel       warp-specialised tcgen05 attention: 1 producer warp
+// Pipeline (2 launches and a 4-byte memset, all on the caller's stream):
+//   1. sage_prep_kernel       persistent, TMA-fed, in thread-block clusters: one cluster
+//                             per (seq, kv head) computes the K token mean and the V
+//                             per-channel scale (partials exchanged through distributed
+//                             shared memory) and then writes smoothed-K INT8 and V e4m3
+//                             codes from a second, L2-resident pass over its tiles;
+//                             the remaining CTAs write Q INT8 codes.  Codes land in the
+//                             128-byte-swizzled tile layout tcgen05 reads directly from
+//                             shared memory (one 16 KB bulk copy per tile; Q/K K-major,
+//                             V token-major)
+//   2. sage_attn_kernel       warp-specialised tcgen05 attention: 1 producer warp
 //                             (bulk copies), 1 MMA warp (kind::i8 QK^T and kind::f8f6f4
-//                             PV into TMEM), 4 softmax warps (TMEM -> registers, online
+//                             PV into TMEM), 8 softmax warps (TMEM -> registers, online
 //                             base-2 softmax, P -> e4m3 into swizzled smem, O rescale,
 //                             epilogue).
 #include "qf2_common.cuh"
@@ -30,7 +32,7 @@ constexpr int kTile = 128;          // tokens per tile (MMA M and N)
 constexpr int kHeadDim = 128;       // D
 constexpr int kTileBytes = 16384;   // 128 rows x 128 bytes of 8-bit codes
 constexpr int kQuantBlock = 64;     // tokens per INT8 scale block
-constexpr int kStatChunk = 512;     // tokens per stats partial (one CTA, 32 tokens per thread)
+static_assert(kTile == 2 * kQuantBlock, "a Q/K tile holds two INT8 scale blocks");
 constexpr int kStages = 4;          // K/V smem ring depth
 constexpr int kMaxKvTiles = 512;    // k-scale smem capacity (65536 tokens)
 constexpr float kLog2_448 = 8.807354922057604f;
@@ -83,155 +85,453 @@ struct Workspace {
   int64_t nch;      // stats chunks per sequence
 };
 
-// ----------------------------------------------------------------- stats --
-// grid (nch, Hkv, batch), 256 threads: thread = (row slot 0..15, 8-channel chunk 0..15)
+// --------------------------------------------------------- packed fp32 math --
+// Two-lane fp32 arithmetic (sm_100 f32x2 instructions); each lane rounds like the
+// scalar .rn instruction.
+QF2_DEV float2 fmul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+QF2_DEV float2 fadd2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+QF2_DEV float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// The two 16-bit floats of a 32-bit word as fp32 (exact).
 template <typename T>
-__global__ void __launch_bounds__(256, 3) sage_stats_kernel(const T* __restrict__ k, Strides3 ks_, const T* __restrict__ v,
-                                                         Strides3 vs_, SeqGeom g, int Hkv, Workspace ws) {
-  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const SeqInfo si = seq_k(g, b);
-  const int64_t t_begin = (int64_t)chunk * kStatChunk;
-  const int slot = threadIdx.x >> 4, c8 = threadIdx.x & 15;
-  double sum[8];
-  float amax[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) { sum[j] = 0.0; amax[j] = 0.f; }
-  if (t_begin < si.len) {
-    const int64_t t_end = si.len < t_begin + kStatChunk ? si.len : t_begin + kStatChunk;
-    const T* kb = k + (int64_t)b * ks_.b + (int64_t)h * ks_.h + c8 * 8;
-    const T* vb = v + (int64_t)b * vs_.b + (int64_t)h * vs_.h + c8 * 8;
-    // 4 tokens per batch, the next batch's 8 loads issued before this batch's arithmetic
-    constexpr int kBatch = 4, kBatches = kStatChunk / (16 * kBatch);
-    uint4 kc[kBatch], vc[kBatch], kn[kBatch], vn[kBatch];
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int64_t t = t_begin + slot + u * 16;
-      const bool in = t < t_end;
-      kc[u] = in ? *reinterpret_cast<const uint4*>(kb + (si.tok0 + t) * ks_.s) : make_uint4(0, 0, 0, 0);
-      vc[u] = in ? *reinterpret_cast<const uint4*>(vb + (si.tok0 + t) * vs_.s) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll 1
-    for (int bt = 0; bt < kBatches; ++bt) {
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int64_t t = t_begin + slot + ((bt + 1) * kBatch + u) * 16;
-        const bool in = bt + 1 < kBatches && t < t_end;
-        kn[u] = in ? *reinterpret_cast<const uint4*>(kb + (si.tok0 + t) * ks_.s) : make_uint4(0, 0, 0, 0);
-        vn[u] = in ? *reinterpret_cast<const uint4*>(vb + (si.tok0 + t) * vs_.s) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const T* ke = reinterpret_cast<const T*>(&kc[u]);
-        const T* ve = reinterpret_cast<const T*>(&vc[u]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          sum[j] += (double)to_f32(ke[j]);
-          amax[j] = fmaxf(amax[j], fabsf(to_f32(ve[j])));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        kc[u] = kn[u];
-        vc[u] = vn[u];
-      }
-    }
-  }
-  __shared__ double s_sum[16][kHeadDim];
-  __shared__ float s_amax[16][kHeadDim];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) { s_sum[slot][c8 * 8 + j] = sum[j]; s_amax[slot][c8 * 8 + j] = amax[j]; }
-  __syncthreads();
-  if (threadIdx.x < kHeadDim) {
-    const int c = threadIdx.x;
-    double acc = 0.0;
-    float am = 0.f;
-#pragma unroll
-    for (int r = 0; r < 16; ++r) { acc += s_sum[r][c]; am = fmaxf(am, s_amax[r][c]); }
-    const int64_t o = (((int64_t)b * Hkv + h) * ws.nch + chunk) * kHeadDim + c;
-    ws.ksum_part[o] = acc;
-    ws.vamax_part[o] = am;
-  }
+QF2_DEV float2 unpack2(uint32_t w);
+template <>
+QF2_DEV float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+QF2_DEV float2 unpack2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
 }
 
-// -------------------------------------------------------------- finalize --
-// grid (Hkv, batch), 128 threads (one per channel)
-__global__ void __launch_bounds__(128) sage_finalize_kernel(SeqGeom g, int Hkv, Workspace ws) {
-  const int h = blockIdx.x, b = blockIdx.y, c = threadIdx.x;
-  const SeqInfo si = seq_k(g, b);
-  const int64_t nchunks = (si.len + kStatChunk - 1) / kStatChunk;
-  const int64_t base = ((int64_t)b * Hkv + h) * ws.nch * kHeadDim + c;
-  double acc = 0.0;
-  float am = 0.f;
-  for (int64_t i = 0; i < nchunks; ++i) {
-    acc += ws.ksum_part[base + i * kHeadDim];
-    am = fmaxf(am, ws.vamax_part[base + i * kHeadDim]);
-  }
-  const int64_t o = ((int64_t)b * Hkv + h) * kHeadDim + c;
-  ws.kmean[o] = si.len > 0 ? (float)(acc / (double)si.len) : 0.f;
-  ws.vs[o] = am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f;
-  ws.vinv[o] = am > 0.f ? __fdiv_rn(448.0f, am) : 1.0f;
+// max(|a|, |b|) of the four 16-bit floats of two words, as fp32 (NaN lanes ignored like fmaxf)
+template <typename T>
+QF2_DEV uint32_t absmax2(uint32_t acc, uint32_t w);
+template <>
+QF2_DEV uint32_t absmax2<__nv_bfloat16>(uint32_t acc, uint32_t w) {
+  __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&acc),
+                             __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w)));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+template <>
+QF2_DEV uint32_t absmax2<__half>(uint32_t acc, uint32_t w) {
+  __half2 r = __hmax2(*reinterpret_cast<const __half2*>(&acc), __habs2(*reinterpret_cast<const __half2*>(&w)));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// ----------------------------------------------------------------- quant --
+// rint(x) for |x| < 2^22 as the low byte of the fp32 x + 1.5 * 2^23 (round to nearest
+// even, like cvt.rni); NaN gives 0.  The add must see the already rounded product: ptxas
+// contracts a packed mul.rn.f32x2 followed by add.rn.f32x2 into one fma, so this pair
+// uses the scalar __fmul_rn / __fadd_rn, which are never contracted.
+constexpr float kRintMagic = 12582912.0f;
+
+// ------------------------------------------------------------ preparation --
+// One persistent, TMA-fed, warp-specialised kernel launched in clusters of C CTAs
+// (C <= 8).  Warp 8 produces: it picks the tiles, writes each tile's descriptor next to
+// its 32 KB ring slot (128 tokens x 128 channels of 16-bit values, 3-stage ring) and
+// starts the TMA load; warps 0-7 consume the slots in order.  thread = (row slot rg
+// 0..15, 8-channel chunk c8 0..15); it reads rows rg + 16 i (i < 4: first 64-token block).
+//   KV role (the first batch * Hkv clusters, one per (seq, kv head)): CTA r owns a
+//     contiguous range of the sequence's tiles.  Phase 1 streams its K and V tiles: fp64
+//     channel sums of K and channel amax of V.  The CTAs exchange these partials through
+//     distributed shared memory (cluster barrier); each derives the K token mean and the
+//     V channel scale (fp64 sums of 16-bit floats are exact, so the order of the partials
+//     does not matter), and phase 2 streams the same tiles again -- from L2, where phase 1
+//     left them with evict-last priority -- to write the codes: smoothed K -> INT8 per
+//     64-token block, V -> e4m3 per channel.
+//   Q tiles -> INT8 per 64-token block (x = q * sm_scale * log2 e): every CTA takes them
+//     from a global counter once it has no K/V work left, so the grid finishes together.
+// Codes go straight into the 128-byte-swizzled tile layout tcgen05 reads from shared
+// memory (Q and K K-major, V token-major = MN-major B operand of the PV product).
+constexpr int kPrepThreads = 288;      // warps 0-7 consumers, warp 8 TMA producer
+constexpr int kPrepStages = 3;
+constexpr int kPrepTile = 32768;       // 128 tokens x 128 channels x 16 bit
+constexpr int kPrepCtasPerSm = 2;
+constexpr int kMaxCluster = 8;
+
+struct PrepSmem {
+  static constexpr int ring = 0;
+  static constexpr int red = ring + kPrepStages * kPrepTile;  // 8 warps x 128 doubles
+  static constexpr int part_sum = red + 8 * kHeadDim * 8;      // this CTA's K channel sums
+  static constexpr int part_amax = part_sum + kHeadDim * 8;    // this CTA's V channel amax
+  static constexpr int stats = part_amax + kHeadDim * 4;       // K mean, V 448 / amax
+  static constexpr int blk = stats + 2 * kHeadDim * 4;         // per-tile block amax [2][16]
+  static constexpr int items = blk + 2 * 16 * 4;               // slot descriptors (int4)
+  static constexpr int bars = items + kPrepStages * 16;
+  static constexpr int nbars = 2 * kPrepStages + 2;            // full, empty, block-amax [2]
+  static constexpr int total = bars + nbars * 8;
+};
+static_assert(kPrepCtasPerSm * (PrepSmem::total + 1024) <= 228 * 1024, "two CTAs per SM");
+
 // Byte offset of (row, 16-byte chunk) in a 128x128-byte tile stored in the
-// 128B-swizzle K-major layout: row r at r*128, chunk c at slot c ^ (r & 7).
+// 128B-swizzle layout: row r at r*128, chunk c at slot c ^ (r & 7).
 QF2_DEV int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-template <typename T>
-QF2_DEV void unpack8(const uint4& raw, float* f) {
-  const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) f[j] = to_f32(e[j]);
+struct PrepArgs {
+  SeqGeom g;
+  Workspace ws;
+  int batch, Hq, Hkv;
+  int64_t mtq;           // tiles of the longest q sequence
+  float qmul;            // sm_scale * log2(e)
+  int varlen;
+  int csize;             // CTAs per cluster
+  uint32_t n_kv_ctas;    // batch * Hkv * csize
+  uint32_t* q_next;      // Q tile counter (zeroed with the status word)
+};
+
+// Slot descriptor: x = tensor (0 Q, 1 K, 2 V; -1 end of work) | phase << 4, y = b,
+// z = h, w = tile.
+QF2_DEV int4 make_desc(int tensor, int phase, int b, int h, int64_t tile) {
+  return make_int4(tensor < 0 ? -1 : (tensor | (phase << 4)), b, h, (int)tile);
 }
 
-// grid (max tiles, Hq + 2*Hkv, batch), 256 threads.
-// Q/K tile: thread = (row slot 0..15, 8-channel chunk 0..15), rows slot + 16*i.
-//   code = rint(x * (127 / amax_block)) with x = q * qmul or k - kmean (fp32).
-// V tile: thread = (channel pair 0..63, 32-token group 0..3); writes rows of V^T.
-//   code = e4m3(v * (448 / amax_channel)).
-template <typename T>
-__global__ void __launch_bounds__(256, 4) sage_quant_kernel(const T* __restrict__ q, Strides3 qs_, const T* __restrict__ k,
-                                                         Strides3 ks_, const T* __restrict__ v, Strides3 vs_, SeqGeom g,
-                                                         int Hq, int Hkv, float qmul, Workspace ws) {
-  const int tile = blockIdx.x, job = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x;
-  __shared__ float s_red[2][8];
+QF2_DEV float2 ffma2_rn(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
 
-  if (job < Hq + Hkv) {
-    const bool is_q = job < Hq;
-    const int h = is_q ? job : job - Hq;
-    const SeqInfo si = is_q ? seq_q(g, b) : seq_k(g, b);
-    const int64_t ntiles = (si.len + kTile - 1) / kTile;
-    if (tile >= ntiles) return;
-    const T* src = is_q ? q : k;
-    const Strides3 st = is_q ? qs_ : ks_;
-    const int rg = tid >> 4, c8 = tid & 15;
-    float sub[8];
-    if (is_q) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sub[j] = 0.f;
-    } else {
-      const float4* km = reinterpret_cast<const float4*>(ws.kmean + ((int64_t)b * Hkv + h) * kHeadDim + c8 * 8);
-      const float4 a = km[0], c = km[1];
-      sub[0] = a.x; sub[1] = a.y; sub[2] = a.z; sub[3] = a.w; sub[4] = c.x; sub[5] = c.y; sub[6] = c.z; sub[7] = c.w;
+QF2_DEV void bar_consumers() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+template <typename T>
+__global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
+    sage_prep_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, PrepArgs A) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem + PrepSmem::ring;
+  double* red = reinterpret_cast<double*>(smem + PrepSmem::red);
+  double* part_sum = reinterpret_cast<double*>(smem + PrepSmem::part_sum);
+  float* part_amax = reinterpret_cast<float*>(smem + PrepSmem::part_amax);
+  float* s_kmean = reinterpret_cast<float*>(smem + PrepSmem::stats);
+  float* s_vinv = s_kmean + kHeadDim;
+  float* s_blk = reinterpret_cast<float*>(smem + PrepSmem::blk);
+  int4* s_item = reinterpret_cast<int4*>(smem + PrepSmem::items);  // ordered by the full/empty mbarriers
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PrepSmem::bars);
+  uint64_t* empty = full + kPrepStages;
+  uint64_t* bar_blk = empty + kPrepStages;  // [2]: the 8 warps' block amax of a Q/K tile
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const Workspace& ws = A.ws;
+  if (tid == 0) {
+    for (int s = 0; s < kPrepStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 8);
     }
-    const T* base = src + (int64_t)b * st.b + (int64_t)h * st.h + (si.tok0 + (int64_t)tile * kTile) * st.s + c8 * 8;
-    const int valid = (int)min((int64_t)kTile, si.len - (int64_t)tile * kTile);
+    mbar_init(bar_blk, 8);
+    mbar_init(bar_blk + 1, 8);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // KV role of this CTA: tiles [t0, t0 + nt) of (b_kv, h_kv)
+  const bool kv = blockIdx.x < A.n_kv_ctas;
+  int b_kv = 0, h_kv = 0;
+  int64_t t0 = 0, nt = 0;
+  if (kv) {
+    const uint32_t head = blockIdx.x / (uint32_t)A.csize, rank = blockIdx.x - head * (uint32_t)A.csize;
+    b_kv = (int)(head / (uint32_t)A.Hkv);
+    h_kv = (int)(head - (uint32_t)b_kv * (uint32_t)A.Hkv);
+    const int64_t ntiles = (seq_k(A.g, b_kv).len + kTile - 1) / kTile;
+    const int64_t per = (ntiles + A.csize - 1) / A.csize;
+    t0 = min(ntiles, (int64_t)rank * per);
+    nt = min(ntiles, t0 + per) - t0;
+  }
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer --
+    uint32_t n = 0;  // slots filled
+    bool dead = false;
+    const uint64_t keep = l2_policy_evict_last(), drop = l2_policy_evict_first();
+    // lane 0: wait for a free slot, publish the descriptor, start the load (none for the
+    // end marker; its slot completes on the arrive alone)
+    auto push = [&](int tensor, int phase, int b, int h, int64_t tile) {
+      if (dead) return;
+      const int s = (int)(n % kPrepStages);
+      if (!mbar_wait(empty + s, ((n / kPrepStages) & 1u) ^ 1u)) {
+        atomicExch(ws.status, kDevTimeoutProducer);
+        dead = true;
+        return;
+      }
+      s_item[s] = make_desc(tensor, phase, b, h, tile);
+      ++n;
+      if (tensor < 0) {
+        mbar_arrive(full + s);
+        return;
+      }
+      mbar_arrive_expect_tx(full + s, kPrepTile);
+      const SeqInfo si = tensor == 0 ? seq_q(A.g, b) : seq_k(A.g, b);
+      const CUtensorMap* tm = tensor == 0 ? &tm_q : tensor == 1 ? &tm_k : &tm_v;
+      // K/V tiles stay in L2 between their two reads; Q tiles and second reads go first
+      tma_load_4d_hint(ring + s * kPrepTile, tm, 0, (int32_t)(si.tok0 + tile * kTile), h, A.varlen ? 0 : b, full + s,
+                       phase == 1 ? keep : drop);
+    };
+    if (lane == 0) {
+      if (nt > 0) {
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+      }
+      if (A.mtq > 0) prefetch_tmap(&tm_q);
+      for (int64_t t = t0; t < t0 + nt; ++t) {
+        push(1, 1, b_kv, h_kv, t);
+        push(2, 1, b_kv, h_kv, t);
+      }
+    }
+    __syncwarp();
+    if (kv) cluster_arrive();  // phase-1 partials barrier (this warp publishes nothing)
+    if (lane == 0) {
+      for (int64_t t = t0; t < t0 + nt; ++t) {
+        push(1, 2, b_kv, h_kv, t);
+        push(2, 2, b_kv, h_kv, t);
+      }
+      const uint32_t mtq = (uint32_t)A.mtq;
+      const uint32_t nq = (uint32_t)A.batch * (uint32_t)A.Hq * mtq;
+      while (!dead) {
+        const uint32_t gq = atomicAdd(A.q_next, 1u);
+        if (gq >= nq) break;
+        const uint32_t bh = gq / mtq;
+        const int64_t tile = (int64_t)(gq - bh * mtq);
+        const int b = (int)(bh / (uint32_t)A.Hq);
+        const int h = (int)(bh - (uint32_t)b * (uint32_t)A.Hq);
+        if (tile * kTile < seq_q(A.g, b).len) push(0, 2, b, h, tile);
+      }
+      push(-1, 0, 0, 0, 0);
+    }
+    __syncwarp();
+    if (kv) cluster_wait();
+    // the last loads have landed before this CTA's shared memory goes away (their phases
+    // completed already when the consumers took them; bounded if the consumers gave up)
+    if (lane == 0)
+      for (uint32_t i = n > kPrepStages ? n - kPrepStages : 0; i < n; ++i)
+        mbar_wait(full + (int)(i % kPrepStages), (i / kPrepStages) & 1u);
+    __syncwarp();
+    if (kv) {
+      cluster_arrive();  // no CTA leaves while another may still read its partials
+      cluster_wait();
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers --
+  // Bounded waits only inside the tile loop: a warp that gives up records the error and
+  // leaves the loop; the others then give up at their next wait.  The code after the
+  // loop is taken by every warp exactly once.
+  const int rg = tid >> 4, c8 = tid & 15;
+  bool dead = false, stats_done = !kv;
+  uint32_t n = 0;     // slots consumed
+  uint32_t nbar = 0;  // Q/K tiles (block-amax exchanges)
+  double ksum[8];
+  uint32_t vmax[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ksum[j] = 0.0;
+
+  // CTA partials -> cluster exchange -> K mean and V scale of (b_kv, h_kv) in smem
+  auto finish_stats = [&]() {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ksum[j] += __shfl_xor_sync(0xffffffffu, ksum[j], 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) vmax[j] = absmax2<T>(vmax[j], __shfl_xor_sync(0xffffffffu, vmax[j], 16));
+    if (lane < 16) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[warp * kHeadDim + c8 * 8 + j] = ksum[j];
+    }
+    bar_consumers();
+    if (tid < kHeadDim) {
+      double acc = 0.0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc += red[q * kHeadDim + tid];
+      part_sum[tid] = acc;
+    }
+    bar_consumers();
+    float* redf = reinterpret_cast<float*>(red);
+    if (lane < 16) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack2<T>(vmax[j]);
+        redf[warp * kHeadDim + c8 * 8 + 2 * j] = f.x;
+        redf[warp * kHeadDim + c8 * 8 + 2 * j + 1] = f.y;
+      }
+    }
+    bar_consumers();
+    if (tid < kHeadDim) {
+      float am = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) am = fmaxf(am, redf[q * kHeadDim + tid]);
+      part_amax[tid] = am;
+    }
+    cluster_arrive();
+    cluster_wait();
+    if (tid < kHeadDim) {
+      double acc = 0.0;
+      float am = 0.f;
+      const uint32_t a_sum = smem_u32(part_sum + tid), a_amax = smem_u32(part_amax + tid);
+      for (int r = 0; r < A.csize; ++r) {
+        acc += ld_dsmem_f64(mapa_shared(a_sum, (uint32_t)r));
+        am = fmaxf(am, ld_dsmem_f32(mapa_shared(a_amax, (uint32_t)r)));
+      }
+      const int64_t len = seq_k(A.g, b_kv).len;
+      const float km = len > 0 ? (float)(acc / (double)len) : 0.f;
+      const float vinv = am > 0.f ? __fdiv_rn(448.0f, am) : 1.0f;
+      s_kmean[tid] = km;
+      s_vinv[tid] = vinv;
+      if (cluster_rank() == 0) {
+        const int64_t o = ((int64_t)b_kv * A.Hkv + h_kv) * kHeadDim + tid;
+        ws.kmean[o] = km;
+        ws.vs[o] = am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f;
+        ws.vinv[o] = vinv;
+      }
+    }
+    bar_consumers();  // K mean and V scale in shared memory from here on (read per tile)
+    stats_done = true;
+  };
+  // this thread's 8 channels of the K mean (negated) / V 448 / amax
+  auto load_pairs = [&](const float* src, float sign, float2 (&out)[4]) {
+    const float4 a = *reinterpret_cast<const float4*>(src + c8 * 8);
+    const float4 c = *reinterpret_cast<const float4*>(src + c8 * 8 + 4);
+    out[0] = make_float2(sign * a.x, sign * a.y); out[1] = make_float2(sign * a.z, sign * a.w);
+    out[2] = make_float2(sign * c.x, sign * c.y); out[3] = make_float2(sign * c.z, sign * c.w);
+  };
+
+  // next slot: wait (bounded) for its descriptor; false once a wait gave up
+  int slot = 0;
+  auto next = [&](int4& d) -> bool {
+    slot = (int)(n % kPrepStages);
+    const bool ok = mbar_wait(full + slot, (n / kPrepStages) & 1u);
+    ++n;
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) atomicExch(ws.status, kDevTimeoutSoftmax);
+      dead = true;
+      return false;
+    }
+    d = s_item[slot];
+    return true;
+  };
+  // the tile of the current slot into registers, then the slot back to the producer
+  auto read_tile = [&](uint4 (&raw)[8]) {
+    const uint8_t* src = ring + slot * kPrepTile + rg * 256 + c8 * 16;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = *reinterpret_cast<const uint4*>(src + i * 16 * 256);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);
+  };
+
+  // ---- phase 1 (K/V role): channel statistics of this CTA's K and V tiles ----
+  int4 d = make_int4(-1, 0, 0, 0);
+  while (next(d) && d.x >= 0 && (d.x >> 4) == 1) {
+    const int tensor = d.x & 15;
+    const int64_t tile = d.w;
     uint4 raw[8];
+    read_tile(raw);
+    const int valid = (int)min((int64_t)kTile, seq_k(A.g, d.y).len - tile * kTile);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = rg + 16 * i;
-      raw[i] = r < valid ? *reinterpret_cast<const uint4*>(base + (int64_t)r * st.s) : make_uint4(0, 0, 0, 0);
+    for (int r = 0; r < 8; ++r) {
+      if (rg + 16 * r < valid) {
+        const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r]);
+        if (tensor == 1) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack2<T>(wd[j]);
+            ksum[2 * j] += (double)f.x;
+            ksum[2 * j + 1] += (double)f.y;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) vmax[j] = absmax2<T>(vmax[j], wd[j]);
+        }
+      }
     }
-    auto xform = [&](float f, int j) { return is_q ? __fmul_rn(f, qmul) : __fsub_rn(f, sub[j]); };
+  }
+  if (!stats_done) finish_stats();  // every warp exactly once, also after a wait gave up
+
+  // ---- phase 2: codes (d holds the first descriptor not yet processed) ----
+  const float2 mul = make_float2(A.qmul, A.qmul);
+  const float2 zero2 = make_float2(0.f, 0.f), magic2 = make_float2(kRintMagic, kRintMagic);
+  for (bool have = !dead; have && d.x >= 0; have = next(d)) {
+    const int tensor = d.x & 15, b = d.y, h = d.z;
+    const int64_t tile = d.w;
+    uint4 raw[8];
+    read_tile(raw);
+    const SeqInfo si = tensor == 0 ? seq_q(A.g, b) : seq_k(A.g, b);
+    const int valid = (int)min((int64_t)kTile, si.len - tile * kTile);
+    if (tensor == 2) {
+      // V: e4m3(v * (448 / amax_channel)), token-major
+      float2 vinv2[4];
+      load_pairs(s_vinv, 1.0f, vinv2);
+      uint8_t* dst = ws.vc + ((int64_t)h * ws.tk + si.tile0 + tile) * kTileBytes;
+#pragma unroll
+      for (int r8 = 0; r8 < 8; ++r8) {
+        const int r = rg + 16 * r8;
+        const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r8]);
+        uint32_t e[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 x = fmul2(unpack2<T>(wd[j]), vinv2[j]);
+          e[j] = f32x2_to_e4m3x2(x.x, x.y);
+        }
+        const bool in = r < valid;  // rows past the sequence end get code 0
+        *reinterpret_cast<uint2*>(dst + swz(r, c8 >> 1) + (c8 & 1) * 8) =
+            make_uint2(in ? (e[0] | (e[1] << 16)) : 0u, in ? (e[2] | (e[3] << 16)) : 0u);
+      }
+      continue;
+    }
+    // Q / K: x = q * qmul or k - mean; INT8 per 64-token block
+    const bool is_q = tensor == 0;
+    float2 neg[4];
+    if (!is_q) load_pairs(s_kmean, -1.0f, neg);
     float am[2] = {0.f, 0.f};
+    if (is_q) {
+      // |round(q * qmul)| = round(|q| * |qmul|) and rounding is monotone: the block amax
+      // of x is the rounded product of the 16-bit amax.  Rows past the sequence end (the
+      // next sequence's tokens in a varlen batch) are left out.
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (rg + 16 * i < valid) {
-        float f[8];
-        unpack8<T>(raw[i], f);
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t m = 0u;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) am[i >> 2] = fmaxf(am[i >> 2], fabsf(xform(f[j], j)));
+        for (int r8 = 4 * hb; r8 < 4 * hb + 4; ++r8) {
+          if (rg + 16 * r8 < valid) {
+            const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r8]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) m = absmax2<T>(m, wd[j]);
+          }
+        }
+        const float2 f = unpack2<T>(m);
+        am[hb] = __fmul_rn(fmaxf(f.x, f.y), fabsf(A.qmul));
+      }
+    } else {
+#pragma unroll
+      for (int r8 = 0; r8 < 8; ++r8) {
+        if (rg + 16 * r8 < valid) {
+          const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r8]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 x = fadd2(unpack2<T>(wd[j]), neg[j]);
+            am[r8 >> 2] = fmax3(am[r8 >> 2], fabsf(x.x), fabsf(x.y));
+          }
+        }
       }
     }
 #pragma unroll
@@ -239,73 +539,60 @@ __global__ void __launch_bounds__(256, 4) sage_quant_kernel(const T* __restrict_
       am[0] = fmaxf(am[0], __shfl_xor_sync(0xffffffffu, am[0], o));
       am[1] = fmaxf(am[1], __shfl_xor_sync(0xffffffffu, am[1], o));
     }
-    if ((tid & 31) == 0) { s_red[0][tid >> 5] = am[0]; s_red[1][tid >> 5] = am[1]; }
-    __syncthreads();
+    // block amax across the 8 warps: double-buffered, exchange k completes phase k >> 1
+    // of bar_blk[k & 1]; buffer k & 1 is rewritten only after every warp passed exchange
+    // k + 1, i.e. after it read buffer k
+    const uint32_t kb2 = nbar & 1u;
+    float* r2 = s_blk + kb2 * 16;
+    if (lane == 0) {
+      r2[warp] = am[0];
+      r2[8 + warp] = am[1];
+      mbar_arrive(bar_blk + kb2);
+    }
+    const bool got = mbar_wait(bar_blk + kb2, (nbar >> 1) & 1u);
+    ++nbar;
+    if (!__all_sync(0xffffffffu, got)) {
+      if (lane == 0) atomicExch(ws.status, kDevTimeoutSoftmax);
+      dead = true;
+      break;
+    }
     float bm[2] = {0.f, 0.f};
 #pragma unroll
-    for (int w = 0; w < 8; ++w) { bm[0] = fmaxf(bm[0], s_red[0][w]); bm[1] = fmaxf(bm[1], s_red[1][w]); }
+    for (int q = 0; q < 8; ++q) { bm[0] = fmaxf(bm[0], r2[q]); bm[1] = fmaxf(bm[1], r2[8 + q]); }
     const float inv[2] = {bm[0] > 0.f ? __fdiv_rn(127.0f, bm[0]) : 1.0f, bm[1] > 0.f ? __fdiv_rn(127.0f, bm[1]) : 1.0f};
-    const int64_t slot = (int64_t)h * (is_q ? ws.tq : ws.tk) + si.tile0 + tile;
-    int8_t* dst = (is_q ? ws.qc : ws.kc) + slot * kTileBytes;
+    const int64_t tslot = (int64_t)h * (is_q ? ws.tq : ws.tk) + si.tile0 + tile;
+    int8_t* dst = (is_q ? ws.qc : ws.kc) + tslot * kTileBytes;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = rg + 16 * i;
-      uint32_t w[2] = {0u, 0u};
-      if (r < valid) {
-        float f[8];
-        unpack8<T>(raw[i], f);
+    for (int r8 = 0; r8 < 8; ++r8) {
+      const int r = rg + 16 * r8;
+      const float2 iv = make_float2(inv[r8 >> 2], inv[r8 >> 2]);
+      const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r8]);
+      uint32_t y[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          int c = __float2int_rn(__fmul_rn(xform(f[j], j), inv[i >> 2]));
-          c = max(-127, min(127, c));
-          w[j >> 2] |= (uint32_t)(c & 0xff) << ((j & 3) * 8);
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack2<T>(wd[j]);
+        const float2 x = is_q ? fmul2(f, mul) : fadd2(f, neg[j]);
+        // the product is rounded on its own (fma with a +0 addend: not a multiply that a
+        // following add could be contracted with), then the rounding add gives rint
+        const float2 z = fadd2(ffma2_rn(x, iv, zero2), magic2);
+        y[2 * j] = __float_as_uint(z.x);
+        y[2 * j + 1] = __float_as_uint(z.y);
       }
-      *reinterpret_cast<uint2*>(dst + swz(r, c8 >> 1) + (c8 & 1) * 8) = make_uint2(w[0], w[1]);
+      const uint32_t lo = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
+      const uint32_t hi = __byte_perm(__byte_perm(y[4], y[5], 0x0040), __byte_perm(y[6], y[7], 0x0040), 0x5410);
+      const bool in = r < valid;  // rows past the sequence end get code 0
+      *reinterpret_cast<uint2*>(dst + swz(r, c8 >> 1) + (c8 & 1) * 8) = make_uint2(in ? lo : 0u, in ? hi : 0u);
     }
     if (tid == 0) {
-      float* sc = (is_q ? ws.qs : ws.ks) + slot * 4;
+      float* sc = (is_q ? ws.qs : ws.ks) + tslot * 4;
       const float s0 = bm[0] > 0.f ? __fdiv_rn(bm[0], 127.0f) : 1.0f;
       const float s1 = bm[1] > 0.f ? __fdiv_rn(bm[1], 127.0f) : 1.0f;
       *reinterpret_cast<float4*>(sc) = make_float4(s0, s1, 0.f, 0.f);
     }
-  } else {
-    // ---- V: transpose to [d][token] and quantize to e4m3 per channel ----
-    const int h = job - Hq - Hkv;
-    const SeqInfo si = seq_k(g, b);
-    const int64_t ntiles = (si.len + kTile - 1) / kTile;
-    if (tile >= ntiles) return;
-    const int dp = tid & 63, tg = tid >> 6;  // channel pair, 32-token group
-    const float2 inv = *reinterpret_cast<const float2*>(ws.vinv + ((int64_t)b * Hkv + h) * kHeadDim + 2 * dp);
-    const int valid = (int)min((int64_t)kTile, si.len - (int64_t)tile * kTile);
-    const T* base = v + (int64_t)b * vs_.b + (int64_t)h * vs_.h + (si.tok0 + (int64_t)tile * kTile + tg * 32) * vs_.s +
-                    2 * dp;
-    uint32_t raw[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      raw[i] = (tg * 32 + i < valid) ? *reinterpret_cast<const uint32_t*>(base + (int64_t)i * vs_.s) : 0u;
-    uint32_t out0[8], out1[8];  // 32 bytes of V^T row per channel
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      const T* e0 = reinterpret_cast<const T*>(&raw[i]);
-      const T* e1 = reinterpret_cast<const T*>(&raw[i + 1]);
-      const uint16_t p0 = f32x2_to_e4m3x2(__fmul_rn(to_f32(e0[0]), inv.x), __fmul_rn(to_f32(e1[0]), inv.x));
-      const uint16_t p1 = f32x2_to_e4m3x2(__fmul_rn(to_f32(e0[1]), inv.y), __fmul_rn(to_f32(e1[1]), inv.y));
-      if ((i & 2) == 0) {
-        out0[i >> 2] = p0;
-        out1[i >> 2] = p1;
-      } else {
-        out0[i >> 2] |= (uint32_t)p0 << 16;
-        out1[i >> 2] |= (uint32_t)p1 << 16;
-      }
-    }
-    const int64_t slot = (int64_t)h * ws.tk + si.tile0 + tile;
-    uint8_t* dst = ws.vc + slot * kTileBytes;
-    const int d0 = 2 * dp, d1 = 2 * dp + 1;
-    *reinterpret_cast<uint4*>(dst + swz(d0, tg * 2)) = make_uint4(out0[0], out0[1], out0[2], out0[3]);
-    *reinterpret_cast<uint4*>(dst + swz(d0, tg * 2 + 1)) = make_uint4(out0[4], out0[5], out0[6], out0[7]);
-    *reinterpret_cast<uint4*>(dst + swz(d1, tg * 2)) = make_uint4(out1[0], out1[1], out1[2], out1[3]);
-    *reinterpret_cast<uint4*>(dst + swz(d1, tg * 2 + 1)) = make_uint4(out1[4], out1[5], out1[6], out1[7]);
+  }
+  if (kv) {
+    cluster_arrive();  // no CTA leaves while another may still read its partials
+    cluster_wait();
   }
 }
 
@@ -380,7 +667,7 @@ QF2_DEV void store_row_out(void* out, const Strides3& os, int b, int h, int64_t 
   }
 }
 
-// fma / add on two packed fp32 lanes (sm_100 f32x2 instructions)
+// fma on two packed fp32 lanes (sm_100 f32x2 instruction)
 QF2_DEV float2 ffma2(float2 a, float2 b, float2 c) {
   float2 r;
   asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
@@ -391,21 +678,7 @@ QF2_DEV float2 ffma2(float2 a, float2 b, float2 c) {
   return r;
 }
 
-QF2_DEV float2 fadd2(float2 a, float2 b) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
-}
 
-QF2_DEV float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
 
 
 // grid (ceil(max q tiles / 2), Hq, batch)
@@ -511,7 +784,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       // ------------------------------------------------------------ MMA --
       // converged warp: descriptors are warp-uniform, lane 0 issues and commits
       constexpr uint32_t idesc_qk = make_idesc(2, 1, 1, 0, 0, kTile, kTile);     // s8 x s8 -> s32
-      constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 0, 0, kTile, kHeadDim);  // e4m3 x e4m3 -> f32
+      // e4m3 x e4m3 -> f32; V tiles are token-major (MN-major B: 128-byte rows of channels,
+      // 8-token swizzle atoms 1024 B apart, one 32-token K step = 4096 B)
+      constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 0, 1, kTile, kHeadDim);
       bool ok = wwait(bar_q, 0);
       // Descriptors are built once; per stage / k-step only the 14-bit start-address
       // field moves (16-byte units: a stage is 2048, a 32-byte k-step is 2).
@@ -520,7 +795,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       const uint64_t dK0 = sdesc_sw128_kmajor(smem_u32(sKV));
       constexpr uint64_t kTileStep = kTileBytes >> 4, kStageStep = 2 * kTileBytes >> 4;
       auto issue_pv = [&](int i) -> bool {
-        const uint64_t dV = dK0 + (uint64_t)(i % kStages) * kStageStep + kTileStep;
+        const uint32_t aV = smem_u32(sKV) + (uint32_t)(i % kStages) * 2 * kTileBytes + kTileBytes;
         for (int t = 0; t < ntile; ++t) {
           if (!wwait(bar_p_full + t, i & 1)) return false;
           tc_fence_after();
@@ -528,7 +803,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
           if (lane == 0) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_f8f6f4(tmem + 256 + t * 128, dP + 2 * kk, dV + 2 * kk, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+              mma_f8f6f4(tmem + 256 + t * 128, dP + 2 * kk, sdesc_sw128_mnmajor(aV + kk * 4096, kTileBytes, 1024),
+                         idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
             tc_commit(bar_o_done + t);
           }
           __syncwarp();
@@ -740,10 +1016,10 @@ static Layout make_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_
     L.tq = batch * ((max_q + kTile - 1) / kTile);
     L.tk = batch * ((max_k + kTile - 1) / kTile);
   }
-  L.nch = std::max<int64_t>(1, (max_k + kStatChunk - 1) / kStatChunk);
+  L.nch = std::max<int64_t>(1, (max_k + kTile - 1) / kTile);
   int64_t o = 0;
   auto put = [&](int i, int64_t bytes) { L.off[i] = o; o = align_up(o + bytes, 1024); };
-  put(0, 256);                                       // status
+  put(0, 256);                                       // status word, Q tile counter at byte 16
   put(1, Hq * L.tq * kTileBytes);                    // q codes
   put(2, Hq * L.tq * 16);                            // q scales
   put(3, Hkv * L.tk * kTileBytes);                   // k codes
@@ -798,6 +1074,10 @@ static int validate(const Args& a, bool need_out) {
   if (a.Hq <= 0 || a.Hkv <= 0 || a.Hq % a.Hkv != 0 || a.batch <= 0) return QF2_ERR_SHAPE;
   if (a.max_q < 0 || a.max_k < 0 || a.max_k > (int64_t)kMaxKvTiles * kTile) return QF2_ERR_SHAPE;
   if (a.Hq > 65535 || a.Hq + 2 * a.Hkv > 65535 || a.batch > 65535) return QF2_ERR_SHAPE;
+  // the quantization grid is one-dimensional: batch * (Hq * q tiles + 2 * Hkv * kv tiles) CTAs
+  if ((double)a.batch * ((double)a.Hq * (double)((a.max_q + kTile - 1) / kTile) +
+                         2.0 * (double)a.Hkv * (double)((a.max_k + kTile - 1) / kTile)) > 2147483647.0)
+    return QF2_ERR_SHAPE;
   if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || (need_out && !aligned16(a.out))) return QF2_ERR_ALIGN;
   const Strides3* ss[4] = {&a.qs, &a.ks, &a.vs, &a.os};
   for (int i = 0; i < (need_out ? 4 : 3); ++i) {
@@ -810,32 +1090,73 @@ static int validate(const Args& a, bool need_out) {
   return QF2_OK;
 }
 
+// Tensor map over q, k or v as {channels, tokens, heads, batch} with a 128 x 128 box and
+// no swizzle (the consumers read whole 256-byte rows).  Varlen inputs have one batch
+// entry whose stride is only a placeholder.
+static bool make_prep_map(CUtensorMap* m, const void* base, const Strides3& st, int64_t tokens, int64_t H,
+                          int64_t batch_ext, int dtype) {
+  const uint64_t esz = 2;
+  const uint64_t dims[4] = {(uint64_t)kHeadDim, (uint64_t)tokens, (uint64_t)H, (uint64_t)batch_ext};
+  const uint64_t sb = st.b != 0 ? (uint64_t)st.b * esz : (uint64_t)st.s * esz * (uint64_t)tokens;
+  const uint64_t strides[3] = {(uint64_t)st.s * esz, (uint64_t)st.h * esz, sb};
+  const uint32_t box[4] = {(uint32_t)kHeadDim, (uint32_t)kTile, 1, 1};
+  return qf2_make_tmap_4d_noswizzle(m, dtype == QF2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                    base, dims, strides, box);
+}
+
 template <typename T>
 static int launch_quant(const Args& a) {
   const bool varlen = a.cu_q != nullptr;
   const Layout L = make_layout(a.batch, a.Hq, a.Hkv, a.total_q, a.total_k, a.max_q, a.max_k, varlen);
-  Workspace ws = bind_ws(a.workspace, L);
-  SeqGeom g;
-  g.cu_q = a.cu_q; g.cu_k = a.cu_k; g.Sq = a.Sq; g.Skv = a.Skv;
-  g.tiles_q_dense = (a.Sq + kTile - 1) / kTile;
-  g.tiles_k_dense = (a.Skv + kTile - 1) / kTile;
-  const float qmul = (float)((double)a.sm_scale * 1.4426950408889634);
-  const T* q = reinterpret_cast<const T*>(a.q);
-  const T* k = reinterpret_cast<const T*>(a.k);
-  const T* v = reinterpret_cast<const T*>(a.v);
-  if (a.max_k > 0) {
-    sage_stats_kernel<T><<<dim3((unsigned)L.nch, (unsigned)a.Hkv, (unsigned)a.batch), 256, 0, a.stream>>>(
-        k, a.ks, v, a.vs, g, (int)a.Hkv, ws);
-    QF2_LAUNCH_CHECK();
-  }
-  sage_finalize_kernel<<<dim3((unsigned)a.Hkv, (unsigned)a.batch), 128, 0, a.stream>>>(g, (int)a.Hkv, ws);
-  QF2_LAUNCH_CHECK();
-  const int64_t mt = std::max((a.max_q + kTile - 1) / kTile, (a.max_k + kTile - 1) / kTile);
-  if (mt > 0) {
-    sage_quant_kernel<T><<<dim3((unsigned)mt, (unsigned)(a.Hq + 2 * a.Hkv), (unsigned)a.batch), 256, 0, a.stream>>>(
-        q, a.qs, k, a.ks, v, a.vs, g, (int)a.Hq, (int)a.Hkv, qmul, ws);
-    QF2_LAUNCH_CHECK();
-  }
+  PrepArgs A;
+  A.ws = bind_ws(a.workspace, L);
+  A.g.cu_q = a.cu_q; A.g.cu_k = a.cu_k; A.g.Sq = a.Sq; A.g.Skv = a.Skv;
+  A.g.tiles_q_dense = (a.Sq + kTile - 1) / kTile;
+  A.g.tiles_k_dense = (a.Skv + kTile - 1) / kTile;
+  A.batch = (int)a.batch; A.Hq = (int)a.Hq; A.Hkv = (int)a.Hkv;
+  A.mtq = (a.max_q + kTile - 1) / kTile;
+  const int64_t mtk = (a.max_k + kTile - 1) / kTile;
+  A.qmul = (float)((double)a.sm_scale * 1.4426950408889634);
+  A.varlen = varlen ? 1 : 0;
+  const int64_t tok_q = varlen ? a.total_q : a.Sq, tok_k = varlen ? a.total_k : a.Skv;
+  const int64_t bext = varlen ? 1 : a.batch;
+  CUtensorMap mq, mk, mv;
+  memset(&mq, 0, sizeof(mq));
+  memset(&mk, 0, sizeof(mk));
+  memset(&mv, 0, sizeof(mv));
+  if (A.mtq > 0 && !make_prep_map(&mq, a.q, a.qs, tok_q, a.Hq, bext, a.dtype)) return QF2_ERR_ALIGN;
+  if (mtk > 0 && (!make_prep_map(&mk, a.k, a.ks, tok_k, a.Hkv, bext, a.dtype) ||
+                  !make_prep_map(&mv, a.v, a.vs, tok_k, a.Hkv, bext, a.dtype)))
+    return QF2_ERR_ALIGN;
+  int sms = 0;
+  QF2_CUDA_CHECK(qf2_sm_count(&sms));
+  static std::atomic<uint64_t> attr_done{0};
+  QF2_CUDA_CHECK(qf2_set_smem_once(sage_prep_kernel<T>, PrepSmem::total, &attr_done));
+  // One wave of CTAs, about two thirds of it with a K/V role (per element K/V read two
+  // tensors and write two codes, Q one and one); cluster size <= 8 and <= the tiles of a
+  // sequence.  The remaining CTAs start on Q tiles, which the K/V CTAs join when done.
+  const int64_t slots = (int64_t)sms * kPrepCtasPerSm;
+  const int64_t heads = a.batch * a.Hkv;
+  int C = (int)std::min<int64_t>(kMaxCluster, std::max<int64_t>(1, std::llround((double)slots * 2.0 / 3.0 / heads)));
+  C = std::max(1, std::min(C, (int)std::max<int64_t>(1, mtk)));
+  const int64_t n_kv = heads * C;
+  const int64_t grid = std::max(n_kv, slots / C * C);
+  A.csize = C;
+  A.n_kv_ctas = (uint32_t)n_kv;
+  A.q_next = reinterpret_cast<uint32_t*>(A.ws.status) + 4;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.dynamicSmemBytes = PrepSmem::total;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QF2_CUDA_CHECK(cudaLaunchKernelEx(&cfg, sage_prep_kernel<T>, mq, mk, mv, A));
   return QF2_OK;
 }
 
@@ -870,8 +1191,9 @@ static int run_attn_only(const Args& a) {
 static int run(const Args& a, bool quant_only) {
   int st = validate(a, !quant_only);
   if (st != QF2_OK) return st;
-  // the status word starts every call at zero (stream-ordered, no allocation)
-  QF2_CUDA_CHECK(cudaMemsetAsync(a.workspace, 0, sizeof(int), a.stream));
+  // the status word and the Q tile counter start every call at zero (stream-ordered,
+  // no allocation)
+  QF2_CUDA_CHECK(cudaMemsetAsync(a.workspace, 0, 32, a.stream));
   st = (a.dtype == QF2_BF16) ? launch_quant<__nv_bfloat16>(a) : launch_quant<__half>(a);
   if (st != QF2_OK || quant_only) return st;
   return launch_attn(a);

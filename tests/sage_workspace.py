@@ -32,7 +32,7 @@ def decode(ws_np, offs, batch, Hq, Hkv, lens_q, lens_k, tile0_q, tile0_k):
             rows = [unswizzle_tile(kc[h, tile0_k[b] + t].view(np.uint8)).view(np.int8) for t in range(nk)]
             codes = np.concatenate(rows, 0)[: lens_k[b]] if rows else np.zeros((0, 128), np.int8)
             scales = ks[h, tile0_k[b]:tile0_k[b] + nk, :2].reshape(-1)[: (lens_k[b] + 63) // 64]
-            vt = [unswizzle_tile(vc[h, tile0_k[b] + t]) for t in range(nk)]   # [d, token] tiles
-            v8 = np.concatenate([t.T for t in vt], 0)[: lens_k[b]] if vt else np.zeros((0, 128), np.uint8)
+            vt = [unswizzle_tile(vc[h, tile0_k[b] + t]) for t in range(nk)]   # [token, d] tiles
+            v8 = np.concatenate(vt, 0)[: lens_k[b]] if vt else np.zeros((0, 128), np.uint8)
             out[("k", b, h)] = dict(codes=codes, scales=scales, v8=v8, vscale=vs[b, h], kmean=km[b, h])
     return out
