@@ -153,14 +153,15 @@ constexpr float kRintMagic = 12582912.0f;
 // its 32 KB ring slot (128 tokens x 128 channels of 16-bit values, 3-stage ring) and
 // starts the TMA load; warps 0-7 consume the slots in order.  thread = (row slot rg
 // 0..15, 8-channel chunk c8 0..15); it reads rows rg + 16 i (i < 4: first 64-token block).
-//   KV role (the first batch * Hkv clusters, one per (seq, kv head)): CTA r owns a
-//     contiguous range of the sequence's tiles.  Phase 1 streams its K and V tiles: fp64
-//     channel sums of K and channel amax of V.  The CTAs exchange these partials through
-//     distributed shared memory (cluster barrier); each derives the K token mean and the
-//     V channel scale (fp64 sums of 16-bit floats are exact, so the order of the partials
-//     does not matter), and phase 2 streams the same tiles again -- from L2, where phase 1
-//     left them with evict-last priority -- to write the codes: smoothed K -> INT8 per
-//     64-token block, V -> e4m3 per channel.
+//   K/V role (the first clusters): a cluster walks (seq, kv head) pairs one after the
+//     other; CTA r owns a contiguous range of the sequence's tiles.  Phase 1 streams its
+//     K and V tiles: fp64 channel sums of K and channel amax of V.  An exchange marker in
+//     the ring then makes the CTAs swap these partials through distributed shared memory
+//     (cluster barrier); each derives the K token mean and the V channel scale (fp64 sums
+//     of 16-bit floats are exact, so the order of the partials does not matter), and
+//     phase 2 streams the same tiles again -- from L2, where phase 1 left them with
+//     evict-last priority and where only a few heads are in flight -- to write the codes:
+//     smoothed K -> INT8 per 64-token block, V -> e4m3 per channel.
 //   Q tiles -> INT8 per 64-token block (x = q * sm_scale * log2 e): every CTA takes them
 //     from a global counter once it has no K/V work left, so the grid finishes together.
 // Codes go straight into the 128-byte-swizzled tile layout tcgen05 reads from shared
@@ -174,9 +175,9 @@ constexpr int kMaxCluster = 8;
 struct PrepSmem {
   static constexpr int ring = 0;
   static constexpr int red = ring + kPrepStages * kPrepTile;  // 8 warps x 128 doubles
-  static constexpr int part_sum = red + 8 * kHeadDim * 8;      // this CTA's K channel sums
-  static constexpr int part_amax = part_sum + kHeadDim * 8;    // this CTA's V channel amax
-  static constexpr int stats = part_amax + kHeadDim * 4;       // K mean, V 448 / amax
+  static constexpr int part_sum = red + 8 * kHeadDim * 8;      // [2 heads] this CTA's K channel sums
+  static constexpr int part_amax = part_sum + 2 * kHeadDim * 8;  // [2 heads] this CTA's V channel amax
+  static constexpr int stats = part_amax + 2 * kHeadDim * 4;   // K mean, V 448 / amax
   static constexpr int blk = stats + 2 * kHeadDim * 4;         // per-tile block amax [2][16]
   static constexpr int items = blk + 2 * 16 * 4;               // slot descriptors (int4)
   static constexpr int bars = items + kPrepStages * 16;
@@ -197,12 +198,12 @@ struct PrepArgs {
   float qmul;            // sm_scale * log2(e)
   int varlen;
   int csize;             // CTAs per cluster
-  uint32_t n_kv_ctas;    // batch * Hkv * csize
+  uint32_t n_kv_ctas;    // CTAs with the K/V role (whole clusters)
   uint32_t* q_next;      // Q tile counter (zeroed with the status word)
 };
 
-// Slot descriptor: x = tensor (0 Q, 1 K, 2 V; -1 end of work) | phase << 4, y = b,
-// z = h, w = tile.
+// Slot descriptor: x = kind (0 Q, 1 K, 2 V, 3 statistics exchange; -1 end of work) |
+// phase << 4, y = b, z = h, w = tile.  Kinds -1 and 3 carry no tile.
 QF2_DEV int4 make_desc(int tensor, int phase, int b, int h, int64_t tile) {
   return make_int4(tensor < 0 ? -1 : (tensor | (phase << 4)), b, h, (int)tile);
 }
@@ -218,6 +219,23 @@ QF2_DEV float2 ffma2_rn(float2 a, float2 b, float2 c) {
 }
 
 QF2_DEV void bar_consumers() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// K/V range of CTA `rank` for kv head `hd` (= b * Hkv + h): tiles [t0, t0 + nt)
+struct KvRange {
+  int b, h;
+  int64_t t0, nt;
+};
+
+QF2_DEV KvRange kv_range(const PrepArgs& A, uint32_t hd, uint32_t rank) {
+  KvRange r;
+  r.b = (int)(hd / (uint32_t)A.Hkv);
+  r.h = (int)(hd - (uint32_t)r.b * (uint32_t)A.Hkv);
+  const int64_t ntiles = (seq_k(A.g, r.b).len + kTile - 1) / kTile;
+  const int64_t per = (ntiles + A.csize - 1) / A.csize;
+  r.t0 = min(ntiles, (int64_t)rank * per);
+  r.nt = min(ntiles, r.t0 + per) - r.t0;
+  return r;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
@@ -248,19 +266,13 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
   }
   __syncthreads();
 
-  // KV role of this CTA: tiles [t0, t0 + nt) of (b_kv, h_kv)
+  // K/V role: this cluster walks kv heads cl, cl + ncl, ... (b * Hkv + h order)
   const bool kv = blockIdx.x < A.n_kv_ctas;
-  int b_kv = 0, h_kv = 0;
-  int64_t t0 = 0, nt = 0;
-  if (kv) {
-    const uint32_t head = blockIdx.x / (uint32_t)A.csize, rank = blockIdx.x - head * (uint32_t)A.csize;
-    b_kv = (int)(head / (uint32_t)A.Hkv);
-    h_kv = (int)(head - (uint32_t)b_kv * (uint32_t)A.Hkv);
-    const int64_t ntiles = (seq_k(A.g, b_kv).len + kTile - 1) / kTile;
-    const int64_t per = (ntiles + A.csize - 1) / A.csize;
-    t0 = min(ntiles, (int64_t)rank * per);
-    nt = min(ntiles, t0 + per) - t0;
-  }
+  const uint32_t heads = (uint32_t)A.batch * (uint32_t)A.Hkv;
+  const uint32_t ncl = A.n_kv_ctas / (uint32_t)A.csize;
+  const uint32_t cl = kv ? blockIdx.x / (uint32_t)A.csize : 0u;
+  const uint32_t rank = kv ? blockIdx.x - cl * (uint32_t)A.csize : 0u;
+  const uint32_t my_heads = kv && cl < heads ? (heads - cl + ncl - 1) / ncl : 0u;
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer --
@@ -268,8 +280,8 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
     bool dead = false;
     const uint64_t keep = l2_policy_evict_last(), drop = l2_policy_evict_first();
     // lane 0: wait for a free slot, publish the descriptor, start the load (none for the
-    // end marker; its slot completes on the arrive alone)
-    auto push = [&](int tensor, int phase, int b, int h, int64_t tile) {
+    // markers; their slot completes on the arrive alone)
+    auto push = [&](int kind, int phase, int b, int h, int64_t tile) {
       if (dead) return;
       const int s = (int)(n % kPrepStages);
       if (!mbar_wait(empty + s, ((n / kPrepStages) & 1u) ^ 1u)) {
@@ -277,37 +289,47 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
         dead = true;
         return;
       }
-      s_item[s] = make_desc(tensor, phase, b, h, tile);
+      s_item[s] = make_desc(kind, phase, b, h, tile);
       ++n;
-      if (tensor < 0) {
+      if (kind < 0 || kind == 3) {
         mbar_arrive(full + s);
         return;
       }
       mbar_arrive_expect_tx(full + s, kPrepTile);
-      const SeqInfo si = tensor == 0 ? seq_q(A.g, b) : seq_k(A.g, b);
-      const CUtensorMap* tm = tensor == 0 ? &tm_q : tensor == 1 ? &tm_k : &tm_v;
+      const SeqInfo si = kind == 0 ? seq_q(A.g, b) : seq_k(A.g, b);
+      const CUtensorMap* tm = kind == 0 ? &tm_q : kind == 1 ? &tm_k : &tm_v;
       // K/V tiles stay in L2 between their two reads; Q tiles and second reads go first
       tma_load_4d_hint(ring + s * kPrepTile, tm, 0, (int32_t)(si.tok0 + tile * kTile), h, A.varlen ? 0 : b, full + s,
                        phase == 1 ? keep : drop);
     };
     if (lane == 0) {
-      if (nt > 0) {
+      if (my_heads > 0) {
         prefetch_tmap(&tm_k);
         prefetch_tmap(&tm_v);
       }
       if (A.mtq > 0) prefetch_tmap(&tm_q);
-      for (int64_t t = t0; t < t0 + nt; ++t) {
-        push(1, 1, b_kv, h_kv, t);
-        push(2, 1, b_kv, h_kv, t);
-      }
     }
-    __syncwarp();
-    if (kv) cluster_arrive();  // phase-1 partials barrier (this warp publishes nothing)
-    if (lane == 0) {
-      for (int64_t t = t0; t < t0 + nt; ++t) {
-        push(1, 2, b_kv, h_kv, t);
-        push(2, 2, b_kv, h_kv, t);
+    for (uint32_t i = 0; i < my_heads; ++i) {
+      const KvRange r = kv_range(A, cl + i * ncl, rank);
+      if (lane == 0) {
+        for (int64_t t = r.t0; t < r.t0 + r.nt; ++t) {
+          push(1, 1, r.b, r.h, t);
+          push(2, 1, r.b, r.h, t);
+        }
+        push(3, 1, r.b, r.h, 0);
       }
+      __syncwarp();
+      cluster_arrive();  // this head's partials exchange (this warp publishes nothing)
+      if (lane == 0) {
+        for (int64_t t = r.t0; t < r.t0 + r.nt; ++t) {
+          push(1, 2, r.b, r.h, t);
+          push(2, 2, r.b, r.h, t);
+        }
+      }
+      __syncwarp();
+      cluster_wait();
+    }
+    if (lane == 0) {
       const uint32_t mtq = (uint32_t)A.mtq;
       const uint32_t nq = (uint32_t)A.batch * (uint32_t)A.Hq * mtq;
       while (!dead) {
@@ -320,14 +342,11 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
         if (tile * kTile < seq_q(A.g, b).len) push(0, 2, b, h, tile);
       }
       push(-1, 0, 0, 0, 0);
-    }
-    __syncwarp();
-    if (kv) cluster_wait();
-    // the last loads have landed before this CTA's shared memory goes away (their phases
-    // completed already when the consumers took them; bounded if the consumers gave up)
-    if (lane == 0)
+      // the last loads have landed before this CTA's shared memory goes away (their
+      // phases completed already when the consumers took them; bounded if they gave up)
       for (uint32_t i = n > kPrepStages ? n - kPrepStages : 0; i < n; ++i)
         mbar_wait(full + (int)(i % kPrepStages), (i / kPrepStages) & 1u);
+    }
     __syncwarp();
     if (kv) {
       cluster_arrive();  // no CTA leaves while another may still read its partials
@@ -338,23 +357,50 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
 
   // -------------------------------------------------------------- consumers --
   // Bounded waits only inside the tile loop: a warp that gives up records the error and
-  // leaves the loop; the others then give up at their next wait.  The code after the
-  // loop is taken by every warp exactly once.
+  // leaves the loop; the others then give up at their next wait.  Every warp takes each
+  // head's exchange exactly once (after the loop for the heads it did not reach).
   const int rg = tid >> 4, c8 = tid & 15;
-  bool dead = false, stats_done = !kv;
-  uint32_t n = 0;     // slots consumed
-  uint32_t nbar = 0;  // Q/K tiles (block-amax exchanges)
-  double ksum[8];
-  uint32_t vmax[4] = {0u, 0u, 0u, 0u};
+  bool dead = false;
+  uint32_t n = 0;          // slots consumed
+  uint32_t nbar = 0;       // Q/K tiles (block-amax exchanges)
+  uint32_t heads_done = 0;
+  int slot = 0;
+  auto next = [&](int4& d) -> bool {
+    if (dead) return false;
+    slot = (int)(n % kPrepStages);
+    const bool ok = mbar_wait(full + slot, (n / kPrepStages) & 1u);
+    ++n;
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) atomicExch(ws.status, kDevTimeoutSoftmax);
+      dead = true;
+      return false;
+    }
+    d = s_item[slot];
+    return true;
+  };
+  auto release = [&]() {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);
+  };
+  // the tile of the current slot into registers, then the slot back to the producer
+  auto read_tile = [&](uint4 (&raw)[8]) {
+    const uint8_t* src = ring + slot * kPrepTile + rg * 256 + c8 * 16;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) ksum[j] = 0.0;
-
-  // CTA partials -> cluster exchange -> K mean and V scale of (b_kv, h_kv) in smem
-  auto finish_stats = [&]() {
+    for (int i = 0; i < 8; ++i) raw[i] = *reinterpret_cast<const uint4*>(src + i * 16 * 256);
+    release();
+  };
+  // CTA partials of head i of this cluster -> cluster exchange -> its K mean and V scale
+  // in shared memory (rank 0 also writes them to the workspace)
+  auto exchange = [&](const double (&ksum_in)[8], const uint32_t (&vmax_in)[4]) {
+    double ksum[8];
+    uint32_t vmax[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ksum[j] += __shfl_xor_sync(0xffffffffu, ksum[j], 16);
+    for (int j = 0; j < 8; ++j) ksum[j] = ksum_in[j] + __shfl_xor_sync(0xffffffffu, ksum_in[j], 16);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) vmax[j] = absmax2<T>(vmax[j], __shfl_xor_sync(0xffffffffu, vmax[j], 16));
+    for (int j = 0; j < 4; ++j) vmax[j] = absmax2<T>(vmax_in[j], __shfl_xor_sync(0xffffffffu, vmax_in[j], 16));
+    const uint32_t par = heads_done & 1u;
+    double* psum = part_sum + par * kHeadDim;
+    float* pamax = part_amax + par * kHeadDim;
     if (lane < 16) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) red[warp * kHeadDim + c8 * 8 + j] = ksum[j];
@@ -364,7 +410,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
       double acc = 0.0;
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc += red[q * kHeadDim + tid];
-      part_sum[tid] = acc;
+      psum[tid] = acc;
     }
     bar_consumers();
     float* redf = reinterpret_cast<float*>(red);
@@ -381,32 +427,37 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
       float am = 0.f;
 #pragma unroll
       for (int q = 0; q < 8; ++q) am = fmaxf(am, redf[q * kHeadDim + tid]);
-      part_amax[tid] = am;
+      pamax[tid] = am;
     }
+    // partials of head i live in buffer i & 1: a CTA rewrites it for head i + 2 only
+    // after the exchange of head i + 1, which every CTA joins after reading head i's
     cluster_arrive();
     cluster_wait();
     if (tid < kHeadDim) {
       double acc = 0.0;
       float am = 0.f;
-      const uint32_t a_sum = smem_u32(part_sum + tid), a_amax = smem_u32(part_amax + tid);
+      const uint32_t a_sum = smem_u32(psum + tid), a_amax = smem_u32(pamax + tid);
       for (int r = 0; r < A.csize; ++r) {
         acc += ld_dsmem_f64(mapa_shared(a_sum, (uint32_t)r));
         am = fmaxf(am, ld_dsmem_f32(mapa_shared(a_amax, (uint32_t)r)));
       }
-      const int64_t len = seq_k(A.g, b_kv).len;
+      const uint32_t hd = cl + heads_done * ncl;
+      const int b = (int)(hd / (uint32_t)A.Hkv);
+      const int h = (int)(hd - (uint32_t)b * (uint32_t)A.Hkv);
+      const int64_t len = seq_k(A.g, b).len;
       const float km = len > 0 ? (float)(acc / (double)len) : 0.f;
       const float vinv = am > 0.f ? __fdiv_rn(448.0f, am) : 1.0f;
       s_kmean[tid] = km;
       s_vinv[tid] = vinv;
-      if (cluster_rank() == 0) {
-        const int64_t o = ((int64_t)b_kv * A.Hkv + h_kv) * kHeadDim + tid;
+      if (rank == 0) {
+        const int64_t o = ((int64_t)b * A.Hkv + h) * kHeadDim + tid;
         ws.kmean[o] = km;
         ws.vs[o] = am > 0.f ? __fdiv_rn(am, 448.0f) : 1.0f;
         ws.vinv[o] = vinv;
       }
     }
     bar_consumers();  // K mean and V scale in shared memory from here on (read per tile)
-    stats_done = true;
+    ++heads_done;
   };
   // this thread's 8 channels of the K mean (negated) / V 448 / amax
   auto load_pairs = [&](const float* src, float sign, float2 (&out)[4]) {
@@ -416,68 +467,56 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
     out[2] = make_float2(sign * c.x, sign * c.y); out[3] = make_float2(sign * c.z, sign * c.w);
   };
 
-  // next slot: wait (bounded) for its descriptor; false once a wait gave up
-  int slot = 0;
-  auto next = [&](int4& d) -> bool {
-    slot = (int)(n % kPrepStages);
-    const bool ok = mbar_wait(full + slot, (n / kPrepStages) & 1u);
-    ++n;
-    if (!__all_sync(0xffffffffu, ok)) {
-      if (lane == 0) atomicExch(ws.status, kDevTimeoutSoftmax);
-      dead = true;
-      return false;
-    }
-    d = s_item[slot];
-    return true;
-  };
-  // the tile of the current slot into registers, then the slot back to the producer
-  auto read_tile = [&](uint4 (&raw)[8]) {
-    const uint8_t* src = ring + slot * kPrepTile + rg * 256 + c8 * 16;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) raw[i] = *reinterpret_cast<const uint4*>(src + i * 16 * 256);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + slot);
-  };
-
-  // ---- phase 1 (K/V role): channel statistics of this CTA's K and V tiles ----
-  int4 d = make_int4(-1, 0, 0, 0);
-  while (next(d) && d.x >= 0 && (d.x >> 4) == 1) {
-    const int tensor = d.x & 15;
-    const int64_t tile = d.w;
-    uint4 raw[8];
-    read_tile(raw);
-    const int valid = (int)min((int64_t)kTile, seq_k(A.g, d.y).len - tile * kTile);
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      if (rg + 16 * r < valid) {
-        const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r]);
-        if (tensor == 1) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = unpack2<T>(wd[j]);
-            ksum[2 * j] += (double)f.x;
-            ksum[2 * j + 1] += (double)f.y;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) vmax[j] = absmax2<T>(vmax[j], wd[j]);
-        }
-      }
-    }
-  }
-  if (!stats_done) finish_stats();  // every warp exactly once, also after a wait gave up
-
-  // ---- phase 2: codes (d holds the first descriptor not yet processed) ----
   const float2 mul = make_float2(A.qmul, A.qmul);
   const float2 zero2 = make_float2(0.f, 0.f), magic2 = make_float2(kRintMagic, kRintMagic);
-  for (bool have = !dead; have && d.x >= 0; have = next(d)) {
-    const int tensor = d.x & 15, b = d.y, h = d.z;
+  int4 d = make_int4(-1, 0, 0, 0);
+  bool have = next(d);
+  while (have && d.x >= 0) {
+    if ((d.x >> 4) == 1) {
+      // ---- phase 1 of a head: channel statistics of this CTA's K and V tiles ----
+      double ksum[8];
+      uint32_t vmax[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ksum[j] = 0.0;
+      while ((d.x & 15) != 3) {
+        const int kind = d.x & 15;
+        const int64_t tile = d.w;
+        uint4 raw[8];
+        read_tile(raw);
+        const int valid = (int)min((int64_t)kTile, seq_k(A.g, d.y).len - tile * kTile);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          if (rg + 16 * r < valid) {
+            const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r]);
+            if (kind == 1) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = unpack2<T>(wd[j]);
+                ksum[2 * j] += (double)f.x;
+                ksum[2 * j + 1] += (double)f.y;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) vmax[j] = absmax2<T>(vmax[j], wd[j]);
+            }
+          }
+        }
+        if (!next(d)) break;
+      }
+      if (dead) break;
+      release();  // the exchange marker's slot
+      exchange(ksum, vmax);
+      have = next(d);
+      continue;
+    }
+    // ---- phase 2: codes ----
+    const int kind = d.x & 15, b = d.y, h = d.z;
     const int64_t tile = d.w;
     uint4 raw[8];
     read_tile(raw);
-    const SeqInfo si = tensor == 0 ? seq_q(A.g, b) : seq_k(A.g, b);
+    const SeqInfo si = kind == 0 ? seq_q(A.g, b) : seq_k(A.g, b);
     const int valid = (int)min((int64_t)kTile, si.len - tile * kTile);
-    if (tensor == 2) {
+    if (kind == 2) {
       // V: e4m3(v * (448 / amax_channel)), token-major
       float2 vinv2[4];
       load_pairs(s_vinv, 1.0f, vinv2);
@@ -496,10 +535,11 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
         *reinterpret_cast<uint2*>(dst + swz(r, c8 >> 1) + (c8 & 1) * 8) =
             make_uint2(in ? (e[0] | (e[1] << 16)) : 0u, in ? (e[2] | (e[3] << 16)) : 0u);
       }
+      have = next(d);
       continue;
     }
     // Q / K: x = q * qmul or k - mean; INT8 per 64-token block
-    const bool is_q = tensor == 0;
+    const bool is_q = kind == 0;
     float2 neg[4];
     if (!is_q) load_pairs(s_kmean, -1.0f, neg);
     float am[2] = {0.f, 0.f};
@@ -509,19 +549,20 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
       // next sequence's tokens in a varlen batch) are left out.
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
-        uint32_t m = 0u;
+        uint32_t m[4] = {0u, 0u, 0u, 0u};  // four independent chains
 #pragma unroll
         for (int r8 = 4 * hb; r8 < 4 * hb + 4; ++r8) {
           if (rg + 16 * r8 < valid) {
             const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r8]);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) m = absmax2<T>(m, wd[j]);
+            for (int j = 0; j < 4; ++j) m[j] = absmax2<T>(m[j], wd[j]);
           }
         }
-        const float2 f = unpack2<T>(m);
+        const float2 f = unpack2<T>(absmax2<T>(absmax2<T>(m[0], m[1]), absmax2<T>(m[2], m[3])));
         am[hb] = __fmul_rn(fmaxf(f.x, f.y), fabsf(A.qmul));
       }
     } else {
+      float a4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // four chains per block
 #pragma unroll
       for (int r8 = 0; r8 < 8; ++r8) {
         if (rg + 16 * r8 < valid) {
@@ -529,16 +570,16 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float2 x = fadd2(unpack2<T>(wd[j]), neg[j]);
-            am[r8 >> 2] = fmax3(am[r8 >> 2], fabsf(x.x), fabsf(x.y));
+            a4[r8 >> 2][j] = fmax3(a4[r8 >> 2][j], fabsf(x.x), fabsf(x.y));
           }
         }
       }
+      am[0] = fmaxf(fmaxf(a4[0][0], a4[0][1]), fmaxf(a4[0][2], a4[0][3]));
+      am[1] = fmaxf(fmaxf(a4[1][0], a4[1][1]), fmaxf(a4[1][2], a4[1][3]));
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      am[0] = fmaxf(am[0], __shfl_xor_sync(0xffffffffu, am[0], o));
-      am[1] = fmaxf(am[1], __shfl_xor_sync(0xffffffffu, am[1], o));
-    }
+    // warp max of non-negative floats: their bit patterns order like unsigned integers
+    am[0] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am[0])));
+    am[1] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am[1])));
     // block amax across the 8 warps: double-buffered, exchange k completes phase k >> 1
     // of bar_blk[k & 1]; buffer k & 1 is rewritten only after every warp passed exchange
     // k + 1, i.e. after it read buffer k
@@ -589,6 +630,12 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
       const float s1 = bm[1] > 0.f ? __fdiv_rn(bm[1], 127.0f) : 1.0f;
       *reinterpret_cast<float4*>(sc) = make_float4(s0, s1, 0.f, 0.f);
     }
+    have = next(d);
+  }
+  {
+    const double kz[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+    const uint32_t vz[4] = {0u, 0u, 0u, 0u};
+    while (heads_done < my_heads) exchange(kz, vz);  // only after a wait gave up
   }
   if (kv) {
     cluster_arrive();  // no CTA leaves while another may still read its partials
@@ -1132,15 +1179,18 @@ static int launch_quant(const Args& a) {
   QF2_CUDA_CHECK(qf2_sm_count(&sms));
   static std::atomic<uint64_t> attr_done{0};
   QF2_CUDA_CHECK(qf2_set_smem_once(sage_prep_kernel<T>, PrepSmem::total, &attr_done));
-  // One wave of CTAs, about two thirds of it with a K/V role (per element K/V read two
-  // tensors and write two codes, Q one and one); cluster size <= 8 and <= the tiles of a
-  // sequence.  The remaining CTAs start on Q tiles, which the K/V CTAs join when done.
+  // One wave of CTAs, about two thirds of it with the K/V role (per element K/V read two
+  // tensors and write two codes, Q one and one) in clusters of up to 8 CTAs (at most one
+  // per tile of the longest sequence) that walk the kv heads; fewer heads in flight keep
+  // phase 1's tiles in L2 for phase 2.  The other CTAs start on Q tiles, which the K/V
+  // CTAs join when they are done.
   const int64_t slots = (int64_t)sms * kPrepCtasPerSm;
   const int64_t heads = a.batch * a.Hkv;
-  int C = (int)std::min<int64_t>(kMaxCluster, std::max<int64_t>(1, std::llround((double)slots * 2.0 / 3.0 / heads)));
-  C = std::max(1, std::min(C, (int)std::max<int64_t>(1, mtk)));
-  const int64_t n_kv = heads * C;
-  const int64_t grid = std::max(n_kv, slots / C * C);
+  const int C = (int)std::min<int64_t>(kMaxCluster, std::max<int64_t>(1, mtk));
+  const int64_t n_cl = std::min(heads, std::max<int64_t>(1, std::llround((double)slots * 2.0 / 3.0 / C)));
+  const int64_t n_kv = n_cl * C;
+  const int64_t nq_tiles = a.batch * a.Hq * A.mtq;
+  const int64_t grid = std::max(n_kv, std::min(slots / C * C, n_kv + (nq_tiles + C - 1) / C * C));
   A.csize = C;
   A.n_kv_ctas = (uint32_t)n_kv;
   A.q_next = reinterpret_cast<uint32_t*>(A.ws.status) + 4;
