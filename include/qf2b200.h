@@ -159,7 +159,7 @@ int qf2_sageattn_varlen(const void* q, const int64_t* q_strides, const void* k, 
 
 /* Byte offsets inside the Sage workspace (for inspecting the quantized codes):
  * offsets[0..10] = status, q codes, q scales, k codes, k scales, v codes,
- * v scales, k mean, v inverse scales, k-sum partials, v-amax partials;
+ * v scales, k mean, v inverse scales, split-KV partial rows, split-KV row max/sum;
  * offsets[11] = total. */
 int qf2_sage_workspace_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
                               int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t D, int64_t* offsets);

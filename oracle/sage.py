@@ -79,13 +79,16 @@ def quantize_head(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float):
     return dict(qcodes=qcodes, qscales=qscales, kcodes=kcodes, kscales=kscales, kmean=kmean, v8=v8, vscale=vscale)
 
 
-def attention_from_codes(qz: dict) -> np.ndarray:
-    """Step 5-6 on the quantized codes of one head: returns O [Sq, D] float32."""
+def attention_from_codes(qz: dict, rows=None) -> np.ndarray:
+    """Step 5-6 on the quantized codes of one head: returns O [Sq, D] float32 (only the
+    query rows `rows`, in that order, when given)."""
     qc = qz["qcodes"].astype(np.int64)
     kc = qz["kcodes"].astype(np.int64)
     Sq, Skv = qc.shape[0], kc.shape[0]
-    s_int = qc @ kc.T
     sq = np.repeat(qz["qscales"], QBLOCK)[:Sq]
+    if rows is not None:
+        qc, sq = qc[rows], sq[rows]
+    s_int = qc @ kc.T
     sk = np.repeat(qz["kscales"], QBLOCK)[:Skv]
     sc = (sq[:, None] * sk[None, :]).astype(np.float32)
     logits = (s_int.astype(np.float32) * sc).astype(np.float32)

@@ -126,7 +126,7 @@ def sageattn_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlen
 
 def sage_workspace_layout(batch, Hq, Hkv, Sq, Skv, D=128, varlen_totals=None):
     """Byte offsets of the workspace regions (status, q codes, q scales, k codes, k scales,
-    v codes, v scales, k mean, v inverse scales, k partials, v partials, total)."""
+    v codes, v scales, k mean, v inverse scales, split-KV partial rows, split-KV row max/sum, total)."""
     offs = i64(*([0] * 12))
     if varlen_totals is None:
         check(_lib.load().qf2_sage_workspace_layout(batch, Hq, Hkv, -1, -1, Sq, Skv, D, offs), "layout")

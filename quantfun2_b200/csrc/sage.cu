@@ -35,6 +35,7 @@ constexpr int kQuantBlock = 64;     // tokens per INT8 scale block
 static_assert(kTile == 2 * kQuantBlock, "a Q/K tile holds two INT8 scale blocks");
 constexpr int kStages = 4;          // K/V smem ring depth
 constexpr int kMaxKvTiles = 512;    // k-scale smem capacity (65536 tokens)
+constexpr int kMaxSplits = 8;       // KV splits of the attention
 constexpr float kLog2_448 = 8.807354922057604f;
 
 struct SeqGeom {
@@ -80,7 +81,9 @@ struct Workspace {
   int8_t* kc; float* ks;
   uint8_t* vc; float* vs;
   float* kmean; float* vinv;
-  double* ksum_part; float* vamax_part;
+  __nv_bfloat16* part_o; float2* part_ml;  // split-KV partials (see sage_attn_kernel)
+  int64_t prows;                           // rows of one split's partials: Hq * tq * 128
+  int nsplit;                              // KV splits of the attention (1: none)
   int64_t tq, tk;   // tile slots per head
   int64_t nch;      // stats chunks per sequence
 };
@@ -728,17 +731,23 @@ QF2_DEV float2 ffma2(float2 a, float2 b, float2 c) {
 
 
 
-// grid (ceil(max q tiles / 2), Hq, batch)
+// grid (ceil(max q tiles / 2) * nsplit, Hq, batch).  With nsplit > 1 a CTA walks the KV
+// tiles [jb, jb + nkt) of its split and writes normalised partial rows (bf16) with their
+// running max and row sum to the workspace; sage_combine_kernel merges the splits.
 __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P) {
   extern __shared__ uint8_t smem_raw[];
-  const int pair = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int nsplit = P.ws.nsplit;
+  const int pair = blockIdx.x / nsplit, split = blockIdx.x - pair * nsplit, h = blockIdx.y, b = blockIdx.z;
   const SeqInfo sq = seq_q(P.g, b);
   const int64_t nqt = (sq.len + kTile - 1) / kTile;
   const int qt0 = 2 * pair;
   if (qt0 >= nqt) return;
   const int ntile = (qt0 + 1 < nqt) ? 2 : 1;  // Q tiles in this CTA
   const SeqInfo sk = seq_k(P.g, b);
-  const int nkt = (int)((sk.len + kTile - 1) / kTile);
+  const int nkt_all = (int)((sk.len + kTile - 1) / kTile);
+  const int per_split = (nkt_all + nsplit - 1) / nsplit;
+  const int jb = min(nkt_all, split * per_split);
+  const int nkt = min(nkt_all, jb + per_split) - jb;  // KV tiles of this CTA: [jb, jb + nkt)
   const int hk = h / (P.Hq / P.Hkv);
 
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -802,7 +811,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       // ------------------------------------------------------- producer --
       // the whole warp runs the loop (uniform addresses), lane 0 issues the copies
       const int64_t qslot = (int64_t)h * ws.tq + sq.tile0 + qt0;
-      const int64_t kslot0 = (int64_t)hk * ws.tk + sk.tile0;
+      const int64_t kslot0 = (int64_t)hk * ws.tk + sk.tile0 + jb;
       if (lane == 0) {
         mbar_arrive_expect_tx(bar_q, ntile * kTileBytes + nkt * 16);
         bulk_g2s(sQ, ws.qc + qslot * kTileBytes, ntile * kTileBytes, bar_q);
@@ -920,7 +929,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       float mf[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) mf[i] = __int_as_float((int)s[i] + kMagicBits);
-      const int64_t rem = sk.len - (int64_t)j * kTile;
+      const int64_t rem = sk.len - (int64_t)(jb + j) * kTile;
       if (rem < kTile) {
         // ragged last tile: 0.0 is below every magic-encoded value, so it acts as -inf
 #pragma unroll
@@ -1031,7 +1040,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         float of[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) of[i] = __uint_as_float(o[i]) * vsc[c * 32 + i] * inv_l;
-        if (r_tok < sq.len) store_row_out(P.out, P.os, P.g.cu_q ? 0 : b, h, sq.tok0 + r_tok, of, P.out_bf16, c * 32);
+        if (r_tok >= sq.len) continue;
+        if (nsplit == 1) {
+          store_row_out(P.out, P.os, P.g.cu_q ? 0 : b, h, sq.tok0 + r_tok, of, P.out_bf16, c * 32);
+        } else {
+          const int64_t prow = (int64_t)split * ws.prows + ((int64_t)h * ws.tq + sq.tile0 + qt) * kTile + row;
+          store_row_out(ws.part_o, Strides3{0, 0, kHeadDim}, 0, 0, prow, of, true, c * 32);
+          if (c == 0) ws.part_ml[prow] = make_float2(m_run, ok ? l_run : 0.f);
+        }
       }
     }
   }
@@ -1045,13 +1061,98 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   }
 }
 
+// ---------------------------------------------------------------- combine --
+// grid (tiles * 8, Hq, batch), 256 threads: 16 rows x 16 chunks of 8 channels.  Row r of
+// split s holds o_s = O_s / l_s (bf16) with the running max m_s and row sum l_s of its
+// base-2 softmax; the merged row is sum_s w_s o_s / sum_s w_s with w_s = l_s 2^(m_s - M).
+__global__ void __launch_bounds__(256) sage_combine_kernel(AttnParams P) {
+  const Workspace& ws = P.ws;
+  const int b = blockIdx.z, h = blockIdx.y;
+  const SeqInfo sq = seq_q(P.g, b);
+  const int64_t r_tok = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
+  if (r_tok >= sq.len) return;
+  const int c8 = threadIdx.x & 15;
+  const int64_t prow = ((int64_t)h * ws.tq + sq.tile0) * kTile + r_tok;
+  float m[kMaxSplits], w[kMaxSplits];
+  float M = -INFINITY;
+  for (int sp = 0; sp < ws.nsplit; ++sp) {
+    const float2 ml = ws.part_ml[sp * ws.prows + prow];
+    m[sp] = ml.y > 0.f ? ml.x : -INFINITY;
+    w[sp] = ml.y;
+    M = fmaxf(M, m[sp]);
+  }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (M > -INFINITY) {
+    float W = 0.f;
+    for (int sp = 0; sp < ws.nsplit; ++sp) {
+      w[sp] = m[sp] > -INFINITY ? w[sp] * fast_exp2(m[sp] - M) : 0.f;
+      W += w[sp];
+    }
+    const float invW = 1.0f / W;
+    for (int sp = 0; sp < ws.nsplit; ++sp) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(ws.part_o + (sp * ws.prows + prow) * kHeadDim + c8 * 8);
+      const float wn = w[sp] * invW;
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += wn * __bfloat162float(e[j]);
+    }
+  }
+  uint4 pk;
+  uint32_t* wd = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (P.out_bf16) {
+      __nv_bfloat162 t = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+      wd[j] = *reinterpret_cast<uint32_t*>(&t);
+    } else {
+      __half2 t = __floats2half2_rn(acc[2 * j], acc[2 * j + 1]);
+      wd[j] = *reinterpret_cast<uint32_t*>(&t);
+    }
+  }
+  uint8_t* dst = reinterpret_cast<uint8_t*>(P.out) +
+                 2 * ((int64_t)b * P.os.b + (int64_t)h * P.os.h + (sq.tok0 + r_tok) * P.os.s + c8 * 8);
+  *reinterpret_cast<uint4*>(dst) = pk;
+}
+
 // ------------------------------------------------------------------ host --
 struct Layout {
   int64_t off[12];
   int64_t tq, tk, nch;
+  int64_t prows;
+  int nsplit;
 };
 
 static int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// KV splits of the attention for a dense problem whose CTAs (pairs of Q tiles per head)
+// fill few waves: each split walks a contiguous part of the K/V tiles and leaves
+// normalised partial rows (bf16) with their running max and row sum; a combine kernel
+// merges them.  Cost model in KV-tile iterations of one CTA (~2.1 us each), fitted to
+// measured times at 3-24 heads and 4608 / 16896 tokens: waves x (tiles per split + a
+// fixed 4 per CTA for its prologue and pipeline fill) + the partial rows' write and read
+// (~135 KB per Q-tile pair and split, ~0.0105 iterations at HBM speed).  Varlen problems
+// do not split.
+static int attn_splits(int64_t batch, int64_t Hq, int64_t max_q, int64_t max_k, bool varlen) {
+  if (varlen) return 1;
+  int sms = 0;
+  if (qf2_sm_count(&sms) != cudaSuccess || sms <= 0) sms = 148;
+  const int64_t units = (((max_q + kTile - 1) / kTile + 1) / 2) * Hq * batch;
+  const int64_t nkt = (max_k + kTile - 1) / kTile;
+  if (units <= 0 || nkt < 4) return 1;
+  constexpr double kCtaFixed = 4.0, kPartialPerUnit = 0.0105;
+  auto cost = [&](int sp) {
+    const int64_t per = (nkt + sp - 1) / sp;
+    const double c = (double)((units * sp + sms - 1) / sms) * ((double)per + kCtaFixed);
+    return sp > 1 ? c + kPartialPerUnit * (double)(units * sp) : c;
+  };
+  int best = 1;
+  double best_c = cost(1);
+  for (int sp = 2; sp <= kMaxSplits && (nkt + sp - 1) / sp >= 2; ++sp) {
+    const double c = cost(sp);
+    if (c < best_c - 1e-9) { best_c = c; best = sp; }
+  }
+  return best;
+}
 
 static Layout make_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
                           int64_t max_q, int64_t max_k, bool varlen) {
@@ -1064,6 +1165,9 @@ static Layout make_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_
     L.tk = batch * ((max_k + kTile - 1) / kTile);
   }
   L.nch = std::max<int64_t>(1, (max_k + kTile - 1) / kTile);
+  L.nsplit = attn_splits(batch, Hq, max_q, max_k, varlen);
+  L.prows = Hq * L.tq * kTile;
+  const int64_t np = L.nsplit > 1 ? L.nsplit * L.prows : 0;
   int64_t o = 0;
   auto put = [&](int i, int64_t bytes) { L.off[i] = o; o = align_up(o + bytes, 1024); };
   put(0, 256);                                       // status word, Q tile counter at byte 16
@@ -1071,12 +1175,12 @@ static Layout make_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_
   put(2, Hq * L.tq * 16);                            // q scales
   put(3, Hkv * L.tk * kTileBytes);                   // k codes
   put(4, Hkv * L.tk * 16);                           // k scales
-  put(5, Hkv * L.tk * kTileBytes);                   // v codes (V^T tiles)
+  put(5, Hkv * L.tk * kTileBytes);                   // v codes (token-major tiles)
   put(6, batch * Hkv * kHeadDim * 4);                // v scales
   put(7, batch * Hkv * kHeadDim * 4);                // k mean
   put(8, batch * Hkv * kHeadDim * 4);                // v inverse scales (448 / amax)
-  put(9, batch * Hkv * L.nch * kHeadDim * 8);        // k sum partials (fp64)
-  put(10, batch * Hkv * L.nch * kHeadDim * 4);       // v amax partials
+  put(9, np * kHeadDim * 2);                         // split-KV partial rows (bf16)
+  put(10, np * 8);                                   // split-KV running max and row sum
   L.off[11] = o;
   return L;
 }
@@ -1093,8 +1197,10 @@ static Workspace bind_ws(void* w, const Layout& L) {
   ws.vs = reinterpret_cast<float*>(p + L.off[6]);
   ws.kmean = reinterpret_cast<float*>(p + L.off[7]);
   ws.vinv = reinterpret_cast<float*>(p + L.off[8]);
-  ws.ksum_part = reinterpret_cast<double*>(p + L.off[9]);
-  ws.vamax_part = reinterpret_cast<float*>(p + L.off[10]);
+  ws.part_o = reinterpret_cast<__nv_bfloat16*>(p + L.off[9]);
+  ws.part_ml = reinterpret_cast<float2*>(p + L.off[10]);
+  ws.prows = L.prows;
+  ws.nsplit = L.nsplit;
   ws.tq = L.tq; ws.tk = L.tk; ws.nch = L.nch;
   return ws;
 }
@@ -1226,9 +1332,13 @@ static int launch_attn(const Args& a) {
   if (mqt == 0) return QF2_OK;
   static std::atomic<uint64_t> attr_done{0};
   QF2_CUDA_CHECK(qf2_set_smem_once(sage_attn_kernel, AttnSmem::alloc, &attr_done));
-  sage_attn_kernel<<<dim3((unsigned)((mqt + 1) / 2), (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads,
+  sage_attn_kernel<<<dim3((unsigned)(((mqt + 1) / 2) * P.ws.nsplit), (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads,
                      AttnSmem::alloc, a.stream>>>(P);
   QF2_LAUNCH_CHECK();
+  if (P.ws.nsplit > 1) {
+    sage_combine_kernel<<<dim3((unsigned)(mqt * (kTile / 16)), (unsigned)a.Hq, (unsigned)a.batch), 256, 0, a.stream>>>(P);
+    QF2_LAUNCH_CHECK();
+  }
   return QF2_OK;
 }
 

@@ -103,6 +103,35 @@ class SeqParallel:
         return recv.permute(1, 2, 0, 3, 4).reshape(B, L // P, P * Hp, D)
 
 
+    def attention_packed(self, qkv3: torch.Tensor, out: torch.Tensor, attn_fn=None) -> None:
+        """qkv3 [B, L/P, 3, H, D] (q, k, v of this rank's tokens, contiguous) -> attention over
+        the whole sequence written into out [B, L/P, H, D] (any strides, 16-byte rows).
+        One all-to-all carries q, k and v together and one brings the output back; around
+        them one copy packs the send buffer, one unpacks the received heads and one scatters
+        the output heads.  attn_fn(q, k, v, o) writes o [B, L, H/P, D] (default: Sage)."""
+        attn_fn = attn_fn or (lambda a, b, c, o: sageattn(a, b, c, tensor_layout="NHD", out=o))
+        B, Ls, _, H, D = qkv3.shape
+        if self.world == 1:
+            attn_fn(qkv3[:, :, 0], qkv3[:, :, 1], qkv3[:, :, 2], out)
+            return
+        P, Hp = self.world, H // self.world
+        send = qkv3.view(B, Ls, 3, P, Hp, D).permute(3, 2, 0, 1, 4, 5).contiguous()  # [P, 3, B, Ls, Hp, D]
+        recv = torch.empty_like(send)
+        torch.distributed.all_to_all_single(recv, send, group=self.group)
+        heads = recv.permute(1, 2, 0, 3, 4, 5).reshape(3, B, P * Ls, Hp, D)  # token = src rank * Ls + local
+        # the output in the send order of the second exchange; for B = 1 [P, 1, Ls] is [1, L]
+        o_send = torch.empty(P, B, Ls, Hp, D, dtype=out.dtype, device=out.device)
+        if B == 1:
+            attn_fn(heads[0], heads[1], heads[2], o_send.view(1, P * Ls, Hp, D))
+        else:
+            o = torch.empty(B, P * Ls, Hp, D, dtype=out.dtype, device=out.device)
+            attn_fn(heads[0], heads[1], heads[2], o)
+            o_send.copy_(o.view(B, P, Ls, Hp, D).permute(1, 0, 2, 3, 4))
+        o_recv = torch.empty_like(o_send)
+        torch.distributed.all_to_all_single(o_recv, o_send, group=self.group)
+        out.view(B, Ls, P, Hp, D).copy_(o_recv.permute(1, 2, 0, 3, 4))  # heads of rank p -> [p*Hp, (p+1)*Hp)
+
+
 def ulysses_attention(q, k, v, sp: SeqParallel, attn_fn=None) -> torch.Tensor:
     """q/k/v [B, L_local, H, D] (NHD) -> attention output [B, L_local, H, D]."""
     attn_fn = attn_fn or (lambda a, b, c: sageattn(a, b, c, tensor_layout="NHD"))
@@ -161,10 +190,13 @@ class FluxDoubleBlock(nn.Module):
         im, tm = self.img_mod(sv), self.txt_mod(sv)  # [B, 6 * dim]
         T = txt_local
         L = T + img.shape[1]
-        q, k, v = (torch.empty(B, L, self.heads, self.hd, dtype=torch.bfloat16, device=img.device) for _ in range(3))
+        qkv3 = torch.empty(B, L, 3, self.heads, self.hd, dtype=torch.bfloat16, device=img.device)
+        q, k, v = qkv3.unbind(2)
         self._pre(txt, tm, self.txt_qkv, self.norms[2], self.norms[3], freqs[:, :T], q[:, :T], k[:, :T], v[:, :T])
         self._pre(img, im, self.img_qkv, self.norms[0], self.norms[1], freqs[:, T:], q[:, T:], k[:, T:], v[:, T:])
-        a = ulysses_attention(q, k, v, sp).reshape(B, -1, self.dim)
+        a = torch.empty(B, L, self.heads, self.hd, dtype=torch.bfloat16, device=img.device)
+        sp.attention_packed(qkv3, a)
+        a = a.view(B, L, self.dim)
         img = self._post(img, a[:, txt_local:], im, self.img_proj, self.img_mlp1, self.img_mlp2)
         txt = self._post(txt, a[:, :txt_local], tm, self.txt_proj, self.txt_mlp1, self.txt_mlp2)
         return img, txt
@@ -194,13 +226,10 @@ class FluxSingleBlock(nn.Module):
         qkv = self.linear1_qkv.run(*a)
         cat = torch.empty(B * L, D + self.mlp, dtype=torch.bfloat16, device=x.device)
         self.linear1_mlp.run(*a, out=cat[:, D:], gelu_col0=0)
-        q, k, v = (torch.empty(B, L, self.heads, self.hd, dtype=torch.bfloat16, device=x.device) for _ in range(3))
+        qkv3 = torch.empty(B, L, 3, self.heads, self.hd, dtype=torch.bfloat16, device=x.device)
+        q, k, v = qkv3.unbind(2)
         qkv_norm_rope(qkv.view(B, L, -1), self.heads, self.qn, self.kn, freqs, q, k, v)
-        attn_view = cat[:, :D].view(B, L, self.heads, self.hd)
-        if sp.world == 1:
-            sageattn(q, k, v, tensor_layout="NHD", out=attn_view)
-        else:
-            attn_view.copy_(ulysses_attention(q, k, v, sp))
+        sp.attention_packed(qkv3, cat[:, :D].view(B, L, self.heads, self.hd))
         self.linear2.run(*self.linear2.prep(cat), out=x2, residual=x2, gate=mod[:, 2 * D:3 * D], rows_per_gate=L)
         return x
 

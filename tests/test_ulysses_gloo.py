@@ -30,7 +30,19 @@ def _worker(rank, world, port, q):
         out = ulysses_attention(*local, sp, attn_fn=attn)
         ref = attn(*full)[:, rank * Ls:(rank + 1) * Ls]
         ok3 = torch.allclose(out, ref, atol=1e-6)
-        q.put((rank, ok1, ok2, ok3))
+        # packed form: one exchange for q, k, v together, one for the output (B = 2 and 1)
+        ok4 = True
+        for bsz in (2, 1):
+            qkv3 = torch.stack([t[:bsz] for t in local], dim=2).contiguous()  # [B, Ls, 3, H, D]
+            dst = torch.full((bsz, Ls, H, D + 8), float("nan"))[..., :D]  # strided output rows
+
+            def attn_o(a, b, c, o):
+                o.copy_(attn(a, b, c))
+
+            sp.attention_packed(qkv3, dst, attn_fn=attn_o)
+            ref_b = attn(*[t[:bsz] for t in full])[:, rank * Ls:(rank + 1) * Ls]
+            ok4 = ok4 and torch.allclose(dst, ref_b, atol=1e-6)
+        q.put((rank, ok1, ok2, ok3 and ok4))
     finally:
         dist.destroy_process_group()
 
