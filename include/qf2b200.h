@@ -249,6 +249,16 @@ int qf2_ln_modulate(const void* x, int64_t ldx, int x_dtype, const void* shift, 
                     int64_t rows_per_batch, int64_t M, int64_t N, float eps, void* out, int64_t ldo, int out_dtype,
                     float* scales, qf2_stream_t stream);
 
+/* Chunk permutation copy: dims[0..3] (dims[3] fastest) index n = d0*d1*d2*d3 chunks
+ * of chunk_bytes bytes; chunk (i0, i1, i2, i3) is copied from
+ * src + sum_k i_k * src_strides[k] to dst + sum_k i_k * dst_strides[k] (strides in bytes).
+ * chunk_bytes, the strides and both pointers must be multiples of 16 (QF2_ERR_ALIGN);
+ * source and destination must not overlap.  Used for the layout changes around the
+ * head-parallel all-to-all of the multi-GPU DiT step; the reference runs on one GPU and
+ * has no counterpart. */
+int qf2_copy_chunks(void* dst, const void* src, int64_t chunk_bytes, const int64_t* dims, const int64_t* src_strides,
+                    const int64_t* dst_strides, qf2_stream_t stream);
+
 /* No counterpart in the reference.  qf2_sageattn without a caller workspace, for
  * callers that cannot allocate device memory: programs that reserve all device memory
  * in their own pool, code that must avoid the device synchronization an allocation

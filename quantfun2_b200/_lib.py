@@ -103,6 +103,7 @@ SIGNATURES = {
         [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
          c_int64, c_int, c_void_p, c_void_p],
     ),
+    "qf2_copy_chunks": (c_int, [c_void_p, c_void_p, c_int64, _P64, _P64, _P64, c_void_p]),
     "qf2_sageattn_noalloc": (
         c_int,
         [c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64,

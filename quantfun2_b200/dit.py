@@ -17,6 +17,7 @@ into [B, L, H/P, D] and back (`ulysses_attention`).
 """
 from __future__ import annotations
 
+import itertools
 import math
 
 import torch
@@ -24,7 +25,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from .attention import sageattn
-from .kernels import qkv_norm_rope, rmsnorm_apply, rope_apply_
+from .kernels import copy_chunks, qkv_norm_rope, rmsnorm_apply, rope_apply_
 from .quant import QLinear, quantize_rows
 
 
@@ -115,10 +116,19 @@ class SeqParallel:
             attn_fn(qkv3[:, :, 0], qkv3[:, :, 1], qkv3[:, :, 2], out)
             return
         P, Hp = self.world, H // self.world
-        send = qkv3.view(B, Ls, 3, P, Hp, D).permute(3, 2, 0, 1, 4, 5).contiguous()  # [P, 3, B, Ls, Hp, D]
+        permute = _device_permute if qkv3.is_cuda else _host_permute
+        e = qkv3.element_size()
+        hb = Hp * D * e                                   # bytes of one token's heads of one rank
+        # [B, Ls, 3, P, Hp, D] -> [P, 3, B, Ls, Hp, D]: chunks of Hp*D, ordered (p, which, b, ls)
+        send = torch.empty(P, 3, B, Ls, Hp, D, dtype=qkv3.dtype, device=qkv3.device)
+        permute(send, qkv3, hb, (P, 3, B, Ls), (hb, P * hb, Ls * 3 * P * hb, 3 * P * hb),
+                (3 * B * Ls * hb, B * Ls * hb, Ls * hb, hb))
         recv = torch.empty_like(send)
         torch.distributed.all_to_all_single(recv, send, group=self.group)
-        heads = recv.permute(1, 2, 0, 3, 4, 5).reshape(3, B, P * Ls, Hp, D)  # token = src rank * Ls + local
+        # [P(src), 3, B, Ls, Hp, D] -> [3, B, P, Ls, Hp, D]: whole shards, token = src * Ls + local
+        heads = torch.empty(3, B, P * Ls, Hp, D, dtype=qkv3.dtype, device=qkv3.device)
+        sh = Ls * hb
+        permute(heads, recv, sh, (3, B, P), (B * sh, sh, 3 * B * sh), (B * P * sh, P * sh, sh))
         # the output in the send order of the second exchange; for B = 1 [P, 1, Ls] is [1, L]
         o_send = torch.empty(P, B, Ls, Hp, D, dtype=out.dtype, device=out.device)
         if B == 1:
@@ -126,10 +136,35 @@ class SeqParallel:
         else:
             o = torch.empty(B, P * Ls, Hp, D, dtype=out.dtype, device=out.device)
             attn_fn(heads[0], heads[1], heads[2], o)
-            o_send.copy_(o.view(B, P, Ls, Hp, D).permute(1, 0, 2, 3, 4))
+            permute(o_send, o, sh, (P, B), (sh, P * sh), (B * sh, sh))
         o_recv = torch.empty_like(o_send)
         torch.distributed.all_to_all_single(o_recv, o_send, group=self.group)
-        out.view(B, Ls, P, Hp, D).copy_(o_recv.permute(1, 2, 0, 3, 4))  # heads of rank p -> [p*Hp, (p+1)*Hp)
+        # [P(src), B, Ls, Hp, D] -> out [B, Ls, P*Hp, D] (heads of rank p at [p*Hp, (p+1)*Hp))
+        if out.stride(3) != 1:
+            raise ValueError("out needs contiguous head_dim rows")
+        ob, os_, oh = out.stride(0) * e, out.stride(1) * e, out.stride(2) * e
+        if oh == D * e:  # a token's Hp heads are one contiguous chunk of out
+            permute(out, o_recv, hb, (B, Ls, P), (Ls * hb, hb, B * Ls * hb), (ob, os_, hb))
+        else:
+            permute(out, o_recv, D * e, (B, Ls, P, Hp), (Ls * hb, hb, B * Ls * hb, D * e), (ob, os_, Hp * oh, oh))
+
+
+def _device_permute(dst, src, chunk, dims, ss, ds):
+    copy_chunks(dst, src, chunk, dims, ss, ds)
+
+
+def _host_permute(dst, src, chunk, dims, ss, ds):
+    """The same chunk copy through byte views on the host (gloo ranks in the CPU tests)."""
+    def flat(t):
+        n = t.untyped_storage().nbytes() // t.element_size()
+        return torch.as_strided(t, (n,), (1,), 0).view(torch.uint8), t.storage_offset() * t.element_size()
+
+    s8, bs = flat(src)
+    d8, bd = flat(dst)
+    for idx in itertools.product(*[range(n) for n in dims]):
+        so = bs + sum(i * st for i, st in zip(idx, ss))
+        do = bd + sum(i * st for i, st in zip(idx, ds))
+        d8[do:do + chunk].copy_(s8[so:so + chunk])
 
 
 def ulysses_attention(q, k, v, sp: SeqParallel, attn_fn=None) -> torch.Tensor:

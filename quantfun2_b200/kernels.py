@@ -23,6 +23,7 @@ from . import _lib
 from ._lib import QF2Error, check, dtype_code, i64, require_device, stream_ptr
 
 __all__ = [
+    "copy_chunks",
     "implemented_as",
     "rope_apply",
     "rope_apply_",
@@ -233,3 +234,17 @@ def rms_gate_residual(x: torch.Tensor, y: torch.Tensor | None = None, h: torch.T
         0 if gate is None else gate.stride(0), int(bool(gate_tanh)), p(wq), float(eps_pre or 0.0), p(scale),
         0 if scale is None else scale.stride(0), stream_ptr(x.device)), "qf2_rms_gate_residual")
     return h
+
+
+def copy_chunks(dst: torch.Tensor, src: torch.Tensor, chunk_bytes: int, dims, src_strides, dst_strides) -> None:
+    """Chunk permutation copy on the device: dims (up to 4, last fastest) index the chunks
+    of chunk_bytes bytes; chunk i goes from src's byte offset sum(i_k * src_strides[k]) to
+    dst's sum(i_k * dst_strides[k]).  Byte strides; everything 16-byte aligned."""
+    require_device(dst)
+    d, ss, ds = list(dims), list(src_strides), list(dst_strides)
+    while len(d) < 4:
+        d.insert(0, 1)
+        ss.insert(0, 0)
+        ds.insert(0, 0)
+    check(_lib.load().qf2_copy_chunks(dst.data_ptr(), src.data_ptr(), int(chunk_bytes), i64(*d), i64(*ss), i64(*ds),
+                                      stream_ptr(dst.device)), "qf2_copy_chunks")

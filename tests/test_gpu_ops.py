@@ -159,3 +159,30 @@ def test_qkv_norm_rope_fused(cuda):
         assert err < 0.02 * want.abs().max().item()
         assert not got[:, :off].any()
     assert torch.equal(v[:, off:].cpu(), qkv.view(B, L, 3, H, D)[:, :, 2])
+
+
+def test_copy_chunks_ulysses_layouts(cuda):
+    """qf2_copy_chunks against torch permute copies for the three layout changes around
+    the head-parallel all-to-all (pack q/k/v per destination rank, unpack received
+    shards, scatter output heads into a row-strided buffer)."""
+    from quantfun2_b200.kernels import copy_chunks
+
+    B, Ls, P, Hp, D = 2, 40, 4, 3, 128
+    e = 2
+    hb = Hp * D * e
+    qkv3 = torch.randn(B, Ls, 3, P * Hp, D, device=cuda).bfloat16()
+    send = torch.empty(P, 3, B, Ls, Hp, D, device=cuda, dtype=torch.bfloat16)
+    copy_chunks(send, qkv3, hb, (P, 3, B, Ls), (hb, P * hb, Ls * 3 * P * hb, 3 * P * hb),
+                (3 * B * Ls * hb, B * Ls * hb, Ls * hb, hb))
+    assert torch.equal(send, qkv3.view(B, Ls, 3, P, Hp, D).permute(3, 2, 0, 1, 4, 5))
+    sh = Ls * hb
+    heads = torch.empty(3, B, P * Ls, Hp, D, device=cuda, dtype=torch.bfloat16)
+    copy_chunks(heads, send, sh, (3, B, P), (B * sh, sh, 3 * B * sh), (B * P * sh, P * sh, sh))
+    assert torch.equal(heads, send.permute(1, 2, 0, 3, 4, 5).reshape(3, B, P * Ls, Hp, D))
+    o_recv = torch.randn(P, B, Ls, Hp, D, device=cuda).bfloat16()
+    big = torch.zeros(B, Ls, P * Hp * D + 64, device=cuda, dtype=torch.bfloat16)
+    out = big[:, :, :P * Hp * D].view(B, Ls, P * Hp, D)
+    copy_chunks(out, o_recv, hb, (B, Ls, P), (Ls * hb, hb, B * Ls * hb),
+                (out.stride(0) * e, out.stride(1) * e, hb))
+    assert torch.equal(out, o_recv.permute(1, 2, 0, 3, 4).reshape(B, Ls, P * Hp, D))
+    assert not big[:, :, P * Hp * D:].any()  # nothing written past the rows
