@@ -46,8 +46,8 @@ WORKLOAD = f"sage attention, B={B} H={H} S={S} (4096 img + 512 txt) D={D}, bf16 
 METRIC = "attention TFLOPS (Flux-shaped 4608 tok, Sage INT8 QK / FP8 PV)"
 # dram bytes (read + write) of one sage_attn_kernel launch at this workload, from the
 # ncu capture summarised in profiles/sage_attn_kernel_B2_H24_S4608.md
-# (85.154 MB read + 21.723 MB written)
-NCU_ATTN_TRAFFIC_BYTES = 106_877_184
+# (85.075 MB read + 25.301 MB written)
+NCU_ATTN_TRAFFIC_BYTES = 110_376_448
 
 
 def parse():
