@@ -131,7 +131,8 @@ int qf2_softmax_inplace(void* x, int64_t rows, int64_t n, int64_t row_stride, in
  * and sageattn_varlen (src/models/common/attn.py:109-120).
  * Algorithm: K smoothed by its per-(sequence, head, channel) token mean; Q
  * (pre-multiplied by sm_scale*log2(e)) and smoothed K quantized to INT8 per
- * 64-token block (code = rint(x * (127/amax)), scale = amax/127); V quantized
+ * 64-token block by the published SageAttention rule (scale = amax/127,
+ * t = x / scale, code = trunc(t + 0.5 * sign(t)), each step rounded in fp32); V quantized
  * to FP8 e4m3 per channel (code = e4m3(v * (448/amax)), scale = amax/448);
  * S = Qi8.Ki8^T on tcgen05 kind::i8 into
  * TMEM; online softmax in base 2; P quantized to e4m3 (x448) and P.V on
@@ -215,9 +216,9 @@ int qf2_blocksparse_attn(const void* q, const int64_t* q_strides, const void* k,
  * qf2_codes_to_bf16: int8 / e4m3 codes -> bf16 (exact).
  *
  * qf2_gemm: D[M, N] = (A . B^T) * row_scale[m] * col_scale[n] + bias[n] on tcgen05 tensor
- * cores, A [M, K] and B [N, K] both QF2_BF16 or both QF2_E4M3 with K contiguous (row
- * strides lda/ldb in elements), fp32 accumulation, D QF2_BF16 or QF2_F32 (row stride
- * ldd).  row_scale, col_scale and bias may be NULL; bias is QF2_BF16 or QF2_F32.
+ * cores, A [M, K] and B [N, K] both QF2_BF16, both QF2_F16 or both QF2_E4M3 with K
+ * contiguous (row strides lda/ldb in elements), fp32 accumulation, D QF2_BF16, QF2_F16
+ * or QF2_F32 (row stride ldd; the residual and SwiGLU epilogues need QF2_BF16).  row_scale, col_scale and bias may be NULL; bias is QF2_BF16 or QF2_F32.
  * N % 8 == 0.  Workspace: >= 256 bytes (status word).
  * Weight-only INT8/FP8 linear: D = qf2_gemm(x_bf16, bf16(codes), col_scale = w_scale).
  * W8A8 FP8 linear: D = qf2_gemm(e4m3(x), e4m3 codes, row_scale = x_scale, col_scale = w_scale). */
@@ -225,6 +226,20 @@ int qf2_quantize_rows(const void* x, int64_t ldx, int x_dtype, int64_t M, int64_
                       int q_dtype, float* scales, qf2_stream_t stream);
 int qf2_codes_to_bf16(const void* q, int64_t ldq, int q_dtype, int64_t M, int64_t K, void* out, int64_t ldo,
                       qf2_stream_t stream);
+/* Weight quantizer of the reference's quantize-on-load (src/quant.py:209-241 through
+ * torchao 0.7.0 choose_qparams_affine / quantize_affine, with the model already cast to
+ * the qdtype's activation dtype at src/quant.py:383).  w [M, K] in w_dtype T (QF2_F16,
+ * QF2_BF16 or QF2_F32), every step rounded in T as the library's tensor ops do:
+ *   scale = max(T(amax / D), FLT_EPSILON)   D = 127.5 (QF2_I8) or 448 (QF2_E4M3)
+ *   y = T(w * T(1 / scale));  QF2_I8: code = clamp(round_half_even(y), -128, 127)
+ *                             QF2_E4M3: code = e4m3(clamp(y, -448, 448))
+ * scales[m] = float(scale). */
+int qf2_quantize_weight_rows(const void* w, int64_t ldw, int w_dtype, int64_t M, int64_t K, void* q, int64_t ldq,
+                             int q_dtype, float* scales, qf2_stream_t stream);
+/* Codes -> QF2_BF16 or QF2_F16 values (exact for int8 and e4m3 codes); the fp16 form
+ * needs K % 16 == 0 and 16-byte aligned rows. */
+int qf2_codes_convert(const void* q, int64_t ldq, int q_dtype, int64_t M, int64_t K, void* out, int64_t ldo,
+                      int out_dtype, qf2_stream_t stream);
 int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M, int64_t N,
              int64_t K, int ab_dtype, int d_dtype, const float* row_scale, const float* col_scale, const void* bias,
              int bias_dtype, void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
@@ -272,12 +287,21 @@ int qf2_copy_chunks(void* dst, const void* src, int64_t chunk_bytes, const int64
  * for that device (it must be the current device); make that first call before any
  * stream capture.  All calls share the array and leave their contents in it; the
  * status word is cleared at the start of each call.  Calls that overlap on the GPU
- * (different streams, or host threads) race on the array: serialize them. */
+ * (different streams, or host threads) race on the array: serialize them.  The array's
+ * device address is looked up on every call with the calling thread's current device
+ * (after a cudaDeviceReset the next call finds the new address by itself; like the
+ * first call on a device, make it outside stream capture). */
 #define QF2_SAGE_NOALLOC_SCRATCH_BYTES (48ll << 20)
 int qf2_sageattn_noalloc(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
                          const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides, int64_t B,
                          int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, float sm_scale, int dtype,
                          qf2_stream_t stream);
+/* Error report of qf2_sageattn_noalloc on the current device: synchronizes `stream`,
+ * then returns QF2_ERR_TIMEOUT (and clears the word) if a kernel of the last call gave
+ * up a bounded wait, else QF2_OK -- qf2_workspace_status() for the static array, whose
+ * address callers do not see.  Call it before the next qf2_sageattn_noalloc call, which
+ * clears the word. */
+int qf2_sageattn_noalloc_status(qf2_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -48,7 +48,7 @@ def rmsnorm_apply(x: np.ndarray, w: np.ndarray, eps: float, x_dtype: str = "f32"
 
     eager (kernels/__init__.py:74-80): n = x * rsqrt(mean(x^2) + eps) in fp32,
     rounded to x's dtype (type_as), then * w, rounded to the promoted dtype.
-    fused (rmsnorm.py:179-203): (x * rsqrt) * w in fp32, one rounding at the end.
+    fused (src/kernels/triton/rmsnorm.py:62-68): (x * rsqrt) * w in fp32, one rounding at the end.
     """
     out_dtype = out_dtype or x_dtype
     x = np.asarray(x, dtype=np.float32)

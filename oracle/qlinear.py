@@ -1,14 +1,23 @@
 """Quantized linears restated on the CPU (test infrastructure only).
 
 The reference quantizes nn.Linear weights through torchao 0.7.0 (src/quant.py:209-241;
-version pinned only in get-lumina.bat:2, package absent here): symmetric int8 with
-one scale per output row (block_size=(1, in), eps = fp32 epsilon) and float8 e4m3
-with one scale per output row.  PARITY UNPINNED against torchao itself (not
-installed, no golden vectors in the reference); the rules below are this build's
-stated definitions, checked bit-exactly against the CUDA quantizers:
-  int8:  amax = max|row| (fp32); scale = max(amax / 127.5, FLT_EPSILON) (the symmetric
-         mapping's (qmax - qmin) / 2 denominator); code = rint(x / scale) clamped
-         to [-128, 127].
+version pinned only in get-lumina.bat:2, package absent here), after casting the model
+to the qdtype's activation dtype (fp16 for qint8 / qfloat8, src/quant.py:326,331,383).
+`quantize_weight_torchao` restates the steps of torchao 0.7.0's choose_qparams_affine and
+quantize_affine (torchao/quantization/quant_primitives.py) as the reference configures
+them -- symmetric, one block per output row (block_size=(1, in)), eps = fp32 epsilon,
+scale_dtype left to default to the weight's dtype T -- with each tensor op rounded to T
+as the library computes it (fp32 opmath, result rounded to T):
+  amax  = max(-min(min_row, 0), max(max_row, 0))
+  scale = clamp(T(amax / ((qmax - qmin) / 2)), min=eps)  -- 127.5 for int8, 448 for e4m3
+  int8:  code = clamp(round(T(w * T(1.0 / scale))) + 0, -128, 127).to(int8)
+  e4m3:  code = clamp(T(w * T(scale.reciprocal())), -448, 448).to(float8_e4m3fn)
+PARITY UNPINNED against torchao itself (not installed, no golden vectors in the
+reference); the CUDA weight quantizer is checked bit-exactly against this restatement.
+
+The W8A8 activation quantizer (per token, no counterpart in the reference) uses fp32:
+  int8:  amax = max|row| (fp32); scale = max(amax / 127.5, FLT_EPSILON); code = rint(x / scale)
+         clamped to [-128, 127].
   e4m3:  scale = amax / 448 (1.0 for a zero row); code = e4m3(x * (448 / amax)) with
          round-to-nearest-even, saturating.
 Linear outputs (float) are compared within tolerance:
@@ -19,9 +28,27 @@ from __future__ import annotations
 
 import numpy as np
 
-from .numerics import e4m3_bits_to_f32, to_e4m3_bits
+from .numerics import e4m3_bits_to_f32, round_to, to_e4m3_bits
 
 FLT_EPS = np.float32(np.finfo(np.float32).eps)
+
+
+def quantize_weight_torchao(w: np.ndarray, fmt: str, dtype: str = "f16"):
+    """w [N, K] (float32 values of `dtype`: "f16", "bf16" or "f32") -> (codes, fp32 scales):
+    int8 codes, or uint8 e4m3 bit patterns for fmt "e4m3"."""
+    w = round_to(np.asarray(w, dtype=np.float32), dtype)
+    lo = np.minimum(w.min(axis=1), np.float32(0))
+    hi = np.maximum(w.max(axis=1), np.float32(0))
+    amax = np.maximum(-lo, hi).astype(np.float32)
+    den = np.float32(127.5 if fmt == "int8" else 448.0)
+    scale = np.maximum(round_to((amax / den).astype(np.float32), dtype), FLT_EPS).astype(np.float32)
+    with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
+        recip = round_to((np.float32(1.0) / scale).astype(np.float32), dtype)
+        y = round_to((w * recip[:, None]).astype(np.float32), dtype)
+    if fmt == "int8":
+        c = np.clip(np.rint(y), -128, 127)
+        return np.where(np.isnan(y), 0, c).astype(np.int8), scale
+    return to_e4m3_bits(y), scale
 
 
 def quantize_rows_int8(x: np.ndarray):

@@ -14,11 +14,16 @@ so that the CUDA path can be checked bit-exactly against it:
      k' = float32(k) - km  (one fp32 rounding).
   2. Q pre-scale: q' = float32(q) * c with c = float32(float64(float32(sm_scale)) * log2(e)),
      which folds the softmax scale and the base-2 exponent into Q.
-  3. INT8 per 64-token block (per sequence, head): inv = 127 / amax and the dequant
-     scale = amax / 127, both one fp32 IEEE division (1.0 for an all-zero block);
-     code = rint(float32(x * inv)) (round half to even), clamped to [-127, 127].
-     (The published kernels divide by the scale; multiplying by the block reciprocal
-     is this build's definition -- one rounding per element either way.)
+  3. INT8 per 64-token block (per sequence, head), the rule of the published SageAttention
+     Triton quantizer (sageattention 1.0.x, `quant_per_block.py`, quant_per_block_int8_kernel:
+     `scale = max|x| / 127.`, `x_int8 = x / scale`, `x_int8 += 0.5 * where(x_int8 >= 0, 1, -1)`,
+     `x_int8.to(int8)`): scale = float32(amax / 127); t = float32(x / scale) (IEEE division;
+     Triton may lower `/` to an approximate divide -- the correctly rounded quotient is the
+     definition here so the CPU can reproduce it); u = float32(t + 0.5 * sign(t)) (+0.5 for
+     t >= 0, -0.5 otherwise); code = trunc(u) toward zero, which never leaves [-127, 127].
+     An all-zero block gets scale 1.0 and codes 0 (the Triton kernel divides 0 by 0 there).
+     Block size 64 for Q and K is the benchmarked configuration's (the Triton v1 kernels
+     use 128-token Q blocks).
   4. V per channel over the whole sequence: vinv = 448 / amax, vs = amax / 448 (fp32;
      1.0 if zero); v8 = e4m3(float32(v * vinv)) with round-to-nearest-even.
   5. Logits (base 2): S = (int32)(qcode . kcode) * (sq * sk)  (fp32 product of scales).
@@ -42,30 +47,35 @@ def q_prescale(sm_scale: float) -> np.float32:
     return np.float32(float(np.float32(sm_scale)) * LOG2E)
 
 
+def block_codes(x: np.ndarray, scale: np.float32) -> np.ndarray:
+    """Step 3's element rule for one block: x float32, scale float32 > 0 -> int8 codes."""
+    t = (np.asarray(x, np.float32) / np.float32(scale)).astype(np.float32)
+    u = (t + np.where(t >= 0, np.float32(0.5), np.float32(-0.5))).astype(np.float32)
+    return np.trunc(u).astype(np.int8)
+
+
 def _block_quant(x: np.ndarray):
     """x [S, D] float32 -> (codes int8 [S, D], scales float32 [ceil(S/64)])."""
-    S = x.shape[0]
+    x = np.asarray(x, dtype=np.float32)
+    S, D = x.shape
     nb = (S + QBLOCK - 1) // QBLOCK
-    codes = np.zeros(x.shape, dtype=np.int8)
-    scales = np.zeros(nb, dtype=np.float32)
-    for i in range(nb):
-        blk = x[i * QBLOCK:(i + 1) * QBLOCK]
-        am = np.float32(np.max(np.abs(blk))) if blk.size else np.float32(0)
-        sc = np.float32(am / np.float32(127.0)) if am > 0 else np.float32(1.0)
-        inv = np.float32(np.float32(127.0) / am) if am > 0 else np.float32(1.0)
-        scales[i] = sc
-        c = np.rint((blk * inv).astype(np.float32))
-        codes[i * QBLOCK:(i + 1) * QBLOCK] = np.clip(c, -127, 127).astype(np.int8)
+    pad = np.zeros((nb * QBLOCK, D), np.float32)
+    pad[:S] = x
+    blk = pad.reshape(nb, QBLOCK, D)
+    am = np.abs(blk).max(axis=(1, 2)).astype(np.float32) if nb else np.zeros(0, np.float32)
+    scales = np.where(am > 0, (am / np.float32(127.0)).astype(np.float32), np.float32(1.0)).astype(np.float32)
+    codes = block_codes(blk, scales[:, None, None]).reshape(nb * QBLOCK, D)[:S]
     return codes, scales
 
 
-def quantize_head(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float):
-    """One sequence, one (q head, kv head) pair.  q [Sq, D], k/v [Skv, D] float32 values.
-
-    Returns dict with qcodes, qscales, kcodes, kscales, kmean, v8 (uint8 e4m3 bits), vscale.
-    """
+def quantize_q(q: np.ndarray, sm_scale: float):
+    """Steps 2-3 for the query rows of one (sequence, head): (codes, scales)."""
     qx = (np.asarray(q, dtype=np.float32) * q_prescale(sm_scale)).astype(np.float32)
-    qcodes, qscales = _block_quant(qx)
+    return _block_quant(qx)
+
+
+def quantize_kv(k: np.ndarray, v: np.ndarray):
+    """Steps 1, 3 and 4 for one (sequence, kv head): dict with kcodes, kscales, kmean, v8, vscale."""
     k = np.asarray(k, dtype=np.float32)
     kmean = (np.sum(k.astype(np.float64), axis=0) / max(k.shape[0], 1)).astype(np.float32)
     kx = (k - kmean[None, :]).astype(np.float32)
@@ -76,7 +86,16 @@ def quantize_head(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float):
     vscale = np.where(am > 0, (safe / np.float32(448.0)).astype(np.float32), np.float32(1.0)).astype(np.float32)
     vinv = np.where(am > 0, (np.float32(448.0) / safe).astype(np.float32), np.float32(1.0)).astype(np.float32)
     v8 = to_e4m3_bits((v * vinv[None, :]).astype(np.float32))
-    return dict(qcodes=qcodes, qscales=qscales, kcodes=kcodes, kscales=kscales, kmean=kmean, v8=v8, vscale=vscale)
+    return dict(kcodes=kcodes, kscales=kscales, kmean=kmean, v8=v8, vscale=vscale)
+
+
+def quantize_head(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float):
+    """One sequence, one (q head, kv head) pair.  q [Sq, D], k/v [Skv, D] float32 values.
+
+    Returns dict with qcodes, qscales, kcodes, kscales, kmean, v8 (uint8 e4m3 bits), vscale.
+    """
+    qcodes, qscales = quantize_q(q, sm_scale)
+    return dict(qcodes=qcodes, qscales=qscales, **quantize_kv(k, v))
 
 
 def attention_from_codes(qz: dict, rows=None) -> np.ndarray:
@@ -132,12 +151,13 @@ def sdpa_reference(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float 
     return np.einsum("bhqk,bhkd->bhqd", p, vv).astype(np.float32)
 
 
+_UNSWZ = np.array([[r * 8 + (c ^ (r & 7)) for c in range(8)] for r in range(128)], dtype=np.int64).reshape(-1)
+
+
 def unswizzle_tile(tile: np.ndarray) -> np.ndarray:
-    """Inverse of the 128-byte swizzle used by the GPU tile layout: tile [16384] uint8
-    -> logical [128 rows, 128 bytes].  Row r, 16-byte chunk c lives at r*128 + (c ^ (r & 7))*16."""
-    t = np.asarray(tile, dtype=np.uint8).reshape(128, 8, 16)
-    out = np.empty_like(t)
-    for r in range(128):
-        for c in range(8):
-            out[r, c] = t[r, c ^ (r & 7)]
-    return out.reshape(128, 128)
+    """Inverse of the 128-byte swizzle used by the GPU tile layout: tile [..., 16384] uint8
+    -> logical [..., 128 rows, 128 bytes].  Row r, 16-byte chunk c lives at r*128 + (c ^ (r & 7))*16."""
+    t = np.asarray(tile, dtype=np.uint8)
+    lead = t.shape[:-1]
+    chunks = t.reshape(*lead, 1024, 16)
+    return chunks[..., _UNSWZ, :].reshape(*lead, 128, 128)

@@ -92,6 +92,10 @@ SIGNATURES = {
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
          c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p],
     ),
+    "qf2_quantize_weight_rows": (
+        c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "qf2_codes_convert": (
+        c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p]),
     "qf2_gemm_ex": (
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
@@ -109,6 +113,7 @@ SIGNATURES = {
         [c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64,
          c_int64, c_int64, c_float, c_int, c_void_p],
     ),
+    "qf2_sageattn_noalloc_status": (c_int, [c_void_p]),
 }
 
 _lib = None

@@ -1,8 +1,8 @@
 // Scaled GEMM for the quantized linears (sm_100a).
 //
 // D[M, N] = (A[M, K] . B[N, K]^T) * row_scale[m] * col_scale[n] + bias[n]
-// with A, B both bf16 (tcgen05.mma kind::f16) or both e4m3 (kind::f8f6f4), fp32
-// accumulation in TMEM, bf16 or fp32 output.  It is the compute core behind the
+// with A, B both bf16 or both fp16 (tcgen05.mma kind::f16) or both e4m3 (kind::f8f6f4),
+// fp32 accumulation in TMEM, bf16, fp16 or fp32 output.  It is the compute core behind the
 // reference's torchao linears (src/quant.py:209-241 int8 / float8 weight-only, bound
 // into nn.Linear at :131-148): weight-only INT8/FP8 runs it on bf16 activations and
 // bf16 copies of the weight codes with the per-channel scale in the epilogue; the
@@ -52,8 +52,10 @@ struct Args {
   const float* col_scale;
   const void* bias;
   int bias_f32;   // 1: fp32 bias, 0: bf16 bias
-  int d_f32;      // 1: fp32 output, 0: bf16 output
-  int fp8;        // operand type: 1 e4m3, 0 bf16
+  int d_f32;      // 1: fp32 output, 0: 16-bit output
+  int d_f16;      // 16-bit output: 1 fp16, 0 bf16
+  int fp8;        // operand type: 1 e4m3, 0 16-bit
+  int f16;        // 16-bit operands: 1 fp16, 0 bf16
   int64_t gelu_col0;                 // GELU (tanh form) on columns >= gelu_col0
   const __nv_bfloat16* residual;     // D = residual + gate * y when non-null
   int64_t ldr;
@@ -119,7 +121,7 @@ QF2_DEV void scale_bias32(const Args& A, int64_t n, float* o) {
 }
 
 
-// Output staging for one 32-row x 32-column bf16 chunk of a warp: each lane writes its
+// Output staging for one 32-row x 32-column bf16 / fp16 chunk of a warp: each lane writes its
 // row (64 bytes) into a 64-byte-swizzled tile, then lane 0 stores the tile with TMA.
 // Row-per-thread stores straight to global memory issue 32 scattered 16-byte writes per
 // warp instruction and stall the tensor pipe; one bulk store per chunk does not.
@@ -128,6 +130,7 @@ struct Stager {
   const CUtensorMap* map;  // D, box {32 columns, 32 rows}, 64-byte swizzle
   uint32_t ctr;
   int64_t rows;            // M: boxes starting at or below it are not issued
+  int f16;                 // 1: fp16 output, 0: bf16
 };
 
 QF2_DEV void stage_store(Stager& st, const float* o, int lane, int64_t col, int64_t row0) {
@@ -138,10 +141,18 @@ QF2_DEV void stage_store(Stager& st, const float* o, int lane, int64_t col, int6
   for (int j = 0; j < 4; ++j) {
     uint4 w;
     uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+    if (st.f16) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      __nv_bfloat162 t = __floats2bfloat162_rn(o[8 * j + 2 * q], o[8 * j + 2 * q + 1]);
-      wp[q] = *reinterpret_cast<uint32_t*>(&t);
+      for (int q = 0; q < 4; ++q) {
+        __half2 t = __floats2half2_rn(o[8 * j + 2 * q], o[8 * j + 2 * q + 1]);
+        wp[q] = *reinterpret_cast<uint32_t*>(&t);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __nv_bfloat162 t = __floats2bfloat162_rn(o[8 * j + 2 * q], o[8 * j + 2 * q + 1]);
+        wp[q] = *reinterpret_cast<uint32_t*>(&t);
+      }
     }
     *reinterpret_cast<uint4*>(b + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
   }
@@ -335,8 +346,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA --
-    constexpr uint32_t idesc = FP8 ? make_idesc(1, 0, 0, 0, 0, BM, BN)   // e4m3 x e4m3 -> f32
-                                   : make_idesc(1, 1, 1, 0, 0, BM, BN);  // bf16 x bf16 -> f32
+    // e4m3 x e4m3, bf16 x bf16 or fp16 x fp16 -> f32 (the 16-bit format is a descriptor
+    // field, not a branch between the MMAs)
+    const uint32_t fmt16 = A.f16 ? 0u : 1u;
+    const uint32_t idesc = FP8 ? make_idesc(1, 0, 0, 0, 0, BM, BN) : make_idesc(1, fmt16, fmt16, 0, 0, BM, BN);
     const uint64_t d0 = sdesc_sw128_kmajor(smem_u32(base));
     constexpr uint64_t kStageStep = kStageBytes >> 4, kBOff = kABytes >> 4;
     int64_t g = 0;
@@ -379,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    Stager stg{base + Smem::staging + (warp - 2) * 4096, &tmd, 0, A.M};
+    Stager stg{base + Smem::staging + (warp - 2) * 4096, &tmd, 0, A.M, A.d_f16};
     int it = 0;
     bool ok = true;
     for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
@@ -507,8 +520,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------ MMA (even CTA) --
     if (leader) {
+      const uint32_t fmt16 = A.f16 ? 0u : 1u;
       const uint32_t idesc = FP8 ? make_idesc(1, 0, 0, 0, 0, 2 * BM, bn)
-                                 : make_idesc(1, 1, 1, 0, 0, 2 * BM, bn);
+                                 : make_idesc(1, fmt16, fmt16, 0, 0, 2 * BM, bn);
       const uint64_t d0 = sdesc_sw128_kmajor(smem_u32(base));
       constexpr uint64_t kStageStep = pair::kStageBytes >> 4, kBOff = pair::kABytes >> 4;
       const uint32_t empty_own = smem_u32(empty), empty_peer = mapa_shared(smem_u32(empty), peer);
@@ -558,7 +572,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t acce0 = mapa_shared(smem_u32(acc_empty), 0);
-    Stager stg{base + pair::staging + (warp - 2) * 4096, &tmd, 0, A.M};
+    Stager stg{base + pair::staging + (warp - 2) * 4096, &tmd, 0, A.M, A.d_f16};
     int it = 0;
     bool ok = true;
     for (int64_t tile = cid; ok && tile < ntiles; tile += ncl, ++it) {
@@ -651,8 +665,10 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
                            const void* residual, int64_t ldr, const void* gate, int64_t gate_stride,
                            int64_t rows_per_gate, void* workspace, int64_t workspace_bytes, qf2_stream_t stream) {
   if (!a || !b || !d) return QF2_ERR_ARG;
-  if (ab_dtype != QF2_BF16 && ab_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
-  if (d_dtype != QF2_BF16 && d_dtype != QF2_F32) return QF2_ERR_DTYPE;
+  if (ab_dtype != QF2_BF16 && ab_dtype != QF2_F16 && ab_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
+  if (d_dtype != QF2_BF16 && d_dtype != QF2_F16 && d_dtype != QF2_F32) return QF2_ERR_DTYPE;
+  // the fused residual / SwiGLU epilogues read and write bf16 only
+  if (d_dtype == QF2_F16 && (residual || glu)) return QF2_ERR_DTYPE;
   if (bias && bias_dtype != QF2_BF16 && bias_dtype != QF2_F32) return QF2_ERR_DTYPE;
   if (M <= 0 || N <= 0 || K <= 0 || (N % 8)) return QF2_ERR_SHAPE;
   if (residual && (ldr < N || (gate && rows_per_gate <= 0))) return QF2_ERR_SHAPE;
@@ -662,8 +678,9 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
       ldd < (glu ? N / 2 : N))
     return QF2_ERR_ALIGN;
   if (!workspace || workspace_bytes < 256 || !al16(workspace)) return QF2_ERR_WORKSPACE;
-  const CUtensorMapDataType tdt =
-      ab_dtype == QF2_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType tdt = ab_dtype == QF2_E4M3  ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                  : ab_dtype == QF2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint32_t bk = ab_dtype == QF2_E4M3 ? 128 : 64;
   // CTA pairs (256-row tiles) once there are two 128-row tiles of A; single CTAs for the
   // thin products (adaLN / embedding linears on a few rows)
@@ -679,13 +696,15 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
   if (!qf2_make_tmap_2d(&ma, tdt, a, da, (uint64_t)lda * esz, ba) ||
       !qf2_make_tmap_2d(&mb, tdt, b, db, (uint64_t)ldb * esz, bb))
     return QF2_ERR_ALIGN;
-  // bf16 output goes out through 32 x 32 TMA stores; the fp32 output map is never used
+  // 16-bit output goes out through 32 x 32 TMA stores; the fp32 output map is never used
   CUtensorMap md;
   const uint64_t dd[2] = {(uint64_t)(glu ? N / 2 : N), (uint64_t)M};
   const uint32_t bd[2] = {32, 32};
-  if (d_dtype == QF2_BF16 && !qf2_make_tmap_2d_sw64(&md, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d, dd, (uint64_t)ldd * 2, bd))
+  if (d_dtype != QF2_F32 &&
+      !qf2_make_tmap_2d_sw64(&md, d_dtype == QF2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                             d, dd, (uint64_t)ldd * 2, bd))
     return QF2_ERR_ALIGN;
-  if (d_dtype != QF2_BF16) md = ma;
+  if (d_dtype == QF2_F32) md = ma;
   Args args;
   args.d = d;
   args.ldd = ldd;
@@ -695,7 +714,9 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
   args.bias = bias;
   args.bias_f32 = bias_dtype == QF2_F32;
   args.d_f32 = d_dtype == QF2_F32;
+  args.d_f16 = d_dtype == QF2_F16;
   args.fp8 = ab_dtype == QF2_E4M3;
+  args.f16 = ab_dtype == QF2_F16;
   args.gelu_col0 = gelu_col0 < 0 ? INT64_MAX : gelu_col0;
   args.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
   args.ldr = ldr;

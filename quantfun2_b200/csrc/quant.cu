@@ -3,7 +3,8 @@
 // Replaces the quantize-on-load transforms of the reference (src/quant.py):
 //   _int8_weight_only_transform   :209-224  (torchao symmetric int8, one scale per output row)
 //   _float8_weight_only_transform :227-241  (e4m3, one scale per output row)
-// and provides the per-token e4m3 activation quantizer of the W8A8 FP8 path.
+// with quantize_weight_rows_kernel (torchao's steps in the weight's dtype, below), and
+// provides the per-token e4m3 activation quantizer of the W8A8 FP8 path (fp32 rule):
 //   int8:  scale = max(amax / 127.5, FLT_EPSILON)   code = rint(x / scale) clamped to [-128, 127]
 //   e4m3:  scale = amax / 448 (1 for an all-zero row)   code = e4m3(x * (448 / amax)), RNE, saturating
 // amax is the row's max |x| in fp32; one CTA per row, the row is read twice (the
@@ -344,6 +345,77 @@ __global__ void __launch_bounds__(256) codes_to_bf16_vec_kernel(const uint8_t* _
   }
 }
 
+// ------------------------------------------------ weight quantizer (torchao) --
+// Per-output-row symmetric quantization of a weight [M, K] by the steps of torchao 0.7.0
+// (quant_primitives.py: choose_qparams_affine, then quantize_affine), which the reference
+// runs on weights it has already cast to the activation dtype T (fp16 for qint8 and
+// qfloat8: supported_dtypes at src/quant.py:326,331, applied by model.to(dtype) at :383),
+// with every tensor op in T and its fp32 opmath:
+//   amax   = max(-min(min_row, 0), max(max_row, 0))                         (exact in T)
+//   scale  = T(amax / D) (fp32 division, rounded to T), then max(scale, FLT_EPSILON)
+//            D = (qmax - qmin) / 2: 127.5 for int8 [-128, 127], 448 for e4m3 [-448, 448]
+//   recip  = T(1 / scale)                     (`1.0 / scale`, `scale.reciprocal()`)
+//   y      = T(w * recip)                     (the product of two T values, rounded to T)
+//   int8:  code = clamp(round_half_even(y), -128, 127);  NaN (0 * inf) -> 0
+//   e4m3:  code = e4m3_rne(clamp(y, -448, 448))
+// The fp32 scale written per row is float(scale).  An overflowing reciprocal (fp16 scale
+// below 1/65504) gives inf there too, and the same saturated codes.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_weight_rows_kernel(const T* __restrict__ w, int64_t ldw, int64_t K,
+                                                                   void* q, int64_t ldq, int fp8,
+                                                                   float* __restrict__ scales) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const T* wr = w + row * ldw;
+  float am = 0.f;
+  for (int64_t i = threadIdx.x; i < K; i += blockDim.x) am = fmaxf(am, fabsf(to_f32(wr[i])));
+  am = block_max<T>(am, red);
+  const float scale_t = fmaxf(to_f32(from_f32<T>(__fdiv_rn(am, fp8 ? 448.0f : 127.5f))), FLT_EPSILON);
+  const float recip_t = to_f32(from_f32<T>(__fdiv_rn(1.0f, scale_t)));
+  if (threadIdx.x == 0) scales[row] = scale_t;
+  for (int64_t i = threadIdx.x; i < K; i += blockDim.x) {
+    const float y = to_f32(from_f32<T>(__fmul_rn(to_f32(wr[i]), recip_t)));
+    if (fp8) {
+      const float c = fminf(fmaxf(y, -448.0f), 448.0f);  // fminf/fmaxf would drop a NaN: keep it
+      reinterpret_cast<uint8_t*>(q)[row * ldq + i] = (uint8_t)(f32x2_to_e4m3x2(y != y ? y : c, 0.f) & 0xff);
+    } else {
+      const float r = fminf(fmaxf(rintf(y), -128.0f), 127.0f);
+      reinterpret_cast<int8_t*>(q)[row * ldq + i] = y != y ? (int8_t)0 : (int8_t)(int)r;
+    }
+  }
+}
+
+// code -> fp16 (exact for int8 and e4m3 codes), 16 codes per thread as in the bf16 form
+__global__ void __launch_bounds__(256) codes_to_f16_vec_kernel(const uint8_t* __restrict__ q, int64_t ldq, int fp8,
+                                                               int64_t M, int64_t kv, __half* __restrict__ out,
+                                                               int64_t ldo) {
+  const int64_t total = M * kv;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / kv, c = (idx - r * kv) * 16;
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(q + r * ldq + c));
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
+    uint4 o[2];
+    uint32_t* ow = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float lo, hi;
+      if (fp8) {
+        lo = (float)*reinterpret_cast<const __nv_fp8_e4m3*>(b + 2 * i);
+        hi = (float)*reinterpret_cast<const __nv_fp8_e4m3*>(b + 2 * i + 1);
+      } else {
+        lo = (float)(int8_t)b[2 * i];
+        hi = (float)(int8_t)b[2 * i + 1];
+      }
+      __half2 t = __floats2half2_rn(lo, hi);
+      ow[i] = *reinterpret_cast<uint32_t*>(&t);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + r * ldo + c);
+    dst[0] = o[0];
+    dst[1] = o[1];
+  }
+}
+
 // Rows are held in registers, NV 16-byte vectors per thread of 256: the smallest NV that
 // covers the row keeps the register count (and so the number of resident rows per SM) up.
 static int vecs_per_thread(int64_t n) {
@@ -427,6 +499,54 @@ extern "C" int qf2_quantize_rows(const void* x, int64_t ldx, int x_dtype, int64_
       break;
     default: return QF2_ERR_DTYPE;
   }
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}
+
+extern "C" int qf2_quantize_weight_rows(const void* w, int64_t ldw, int w_dtype, int64_t M, int64_t K, void* q,
+                                        int64_t ldq, int q_dtype, float* scales, qf2_stream_t stream) {
+  using namespace qf2::quant;
+  if (!w || !q || !scales) return QF2_ERR_ARG;
+  if (q_dtype != QF2_I8 && q_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
+  if (M < 0 || K <= 0 || ldw < K || ldq < K || M > 0x7fffffff) return QF2_ERR_SHAPE;
+  if (M == 0) return QF2_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int fp8 = q_dtype == QF2_E4M3;
+  switch (w_dtype) {
+    case QF2_F16:
+      quantize_weight_rows_kernel<__half><<<(unsigned)M, 256, 0, s>>>((const __half*)w, ldw, K, q, ldq, fp8, scales);
+      break;
+    case QF2_BF16:
+      quantize_weight_rows_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, s>>>((const __nv_bfloat16*)w, ldw, K, q, ldq,
+                                                                            fp8, scales);
+      break;
+    case QF2_F32:
+      quantize_weight_rows_kernel<float><<<(unsigned)M, 256, 0, s>>>((const float*)w, ldw, K, q, ldq, fp8, scales);
+      break;
+    default: return QF2_ERR_DTYPE;
+  }
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}
+
+extern "C" int qf2_codes_convert(const void* q, int64_t ldq, int q_dtype, int64_t M, int64_t K, void* out,
+                                 int64_t ldo, int out_dtype, qf2_stream_t stream) {
+  using namespace qf2::quant;
+  if (out_dtype == QF2_BF16) return qf2_codes_to_bf16(q, ldq, q_dtype, M, K, out, ldo, stream);
+  if (out_dtype != QF2_F16) return QF2_ERR_DTYPE;
+  if (!q || !out) return QF2_ERR_ARG;
+  if (q_dtype != QF2_I8 && q_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
+  if (M < 0 || K <= 0 || ldq < K || ldo < K) return QF2_ERR_SHAPE;
+  if (M == 0) return QF2_OK;
+  if (K % 16 || ldq % 16 || ldo % 8 || (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return QF2_ERR_ALIGN;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t total = M * (K / 16);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  codes_to_f16_vec_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(q), ldq,
+                                                           q_dtype == QF2_E4M3, M, K / 16,
+                                                           reinterpret_cast<__half*>(out), ldo);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }

@@ -23,7 +23,6 @@
 
 #include <algorithm>
 #include <cmath>
-#include <mutex>
 
 namespace qf2 {
 namespace sage {
@@ -144,11 +143,25 @@ QF2_DEV uint32_t absmax2<__half>(uint32_t acc, uint32_t w) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// rint(x) for |x| < 2^22 as the low byte of the fp32 x + 1.5 * 2^23 (round to nearest
-// even, like cvt.rni); NaN gives 0.  The add must see the already rounded product: ptxas
-// contracts a packed mul.rn.f32x2 followed by add.rn.f32x2 into one fma, so this pair
-// uses the scalar __fmul_rn / __fadd_rn, which are never contracted.
-constexpr float kRintMagic = 12582912.0f;
+// INT8 code of x in a block with dequant scale s = RN(amax / 127) and r = RN(1 / s), by the
+// published SageAttention Triton rule (quant_per_block_int8_kernel: x / scale, += 0.5 *
+// sign, truncate): t = RN(x / s); code = trunc(RN(t + 0.5 sign(t))), +0.5 for t >= 0.
+// The quotient is RN(x r) corrected once (Markstein 1990: with r the correctly rounded
+// reciprocal and q0 = RN(x r) within an ulp of x / s, the fma remainder x - s q0 is exact
+// and RN(q0 + rem r) is the correctly rounded quotient).  RN(t + 0.5 sign t) = sign(t)
+// RN(|t| + 0.5), and its truncation is sign(t) floor(RN(|t| + 0.5)); the floor of a value
+// below 2^22 is the low bits of its round-toward-zero sum with 2^23.  Returns the code as
+// a two's-complement int32 (low byte = int8 code); |code| <= 127 since |t| <= 127 (1 + 2^-23).
+// The intrinsics are never contracted with one another.
+QF2_DEV uint32_t sage_code(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float rem = __fmaf_rn(-q0, s, x);
+  const float t = __fmaf_rn(rem, r, q0);
+  const float v = __fadd_rn(fabsf(t), 0.5f);
+  const uint32_t n = __float_as_uint(__fadd_rz(v, 8388608.0f)) - 0x4B000000u;
+  const uint32_t neg = (uint32_t)((int32_t)__float_as_uint(t) >> 31);
+  return (n ^ neg) - neg;
+}
 
 // ------------------------------------------------------------ preparation --
 // One persistent, TMA-fed, warp-specialised kernel launched in clusters of C CTAs
@@ -471,7 +484,6 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
   };
 
   const float2 mul = make_float2(A.qmul, A.qmul);
-  const float2 zero2 = make_float2(0.f, 0.f), magic2 = make_float2(kRintMagic, kRintMagic);
   int4 d = make_int4(-1, 0, 0, 0);
   bool have = next(d);
   while (have && d.x >= 0) {
@@ -603,24 +615,23 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
     float bm[2] = {0.f, 0.f};
 #pragma unroll
     for (int q = 0; q < 8; ++q) { bm[0] = fmaxf(bm[0], r2[q]); bm[1] = fmaxf(bm[1], r2[8 + q]); }
-    const float inv[2] = {bm[0] > 0.f ? __fdiv_rn(127.0f, bm[0]) : 1.0f, bm[1] > 0.f ? __fdiv_rn(127.0f, bm[1]) : 1.0f};
+    // dequant scales of the two 64-token blocks and their correctly rounded reciprocals
+    const float bs[2] = {bm[0] > 0.f ? __fdiv_rn(bm[0], 127.0f) : 1.0f, bm[1] > 0.f ? __fdiv_rn(bm[1], 127.0f) : 1.0f};
+    const float br[2] = {__frcp_rn(bs[0]), __frcp_rn(bs[1])};
     const int64_t tslot = (int64_t)h * (is_q ? ws.tq : ws.tk) + si.tile0 + tile;
     int8_t* dst = (is_q ? ws.qc : ws.kc) + tslot * kTileBytes;
 #pragma unroll
     for (int r8 = 0; r8 < 8; ++r8) {
       const int r = rg + 16 * r8;
-      const float2 iv = make_float2(inv[r8 >> 2], inv[r8 >> 2]);
+      const float sb = bs[r8 >> 2], rb = br[r8 >> 2];
       const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r8]);
       uint32_t y[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = unpack2<T>(wd[j]);
         const float2 x = is_q ? fmul2(f, mul) : fadd2(f, neg[j]);
-        // the product is rounded on its own (fma with a +0 addend: not a multiply that a
-        // following add could be contracted with), then the rounding add gives rint
-        const float2 z = fadd2(ffma2_rn(x, iv, zero2), magic2);
-        y[2 * j] = __float_as_uint(z.x);
-        y[2 * j + 1] = __float_as_uint(z.y);
+        y[2 * j] = sage_code(x.x, sb, rb);
+        y[2 * j + 1] = sage_code(x.y, sb, rb);
       }
       const uint32_t lo = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
       const uint32_t hi = __byte_perm(__byte_perm(y[4], y[5], 0x0040), __byte_perm(y[6], y[7], 0x0040), 0x5410);
@@ -629,9 +640,7 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
     }
     if (tid == 0) {
       float* sc = (is_q ? ws.qs : ws.ks) + tslot * 4;
-      const float s0 = bm[0] > 0.f ? __fdiv_rn(bm[0], 127.0f) : 1.0f;
-      const float s1 = bm[1] > 0.f ? __fdiv_rn(bm[1], 127.0f) : 1.0f;
-      *reinterpret_cast<float4*>(sc) = make_float4(s0, s1, 0.f, 0.f);
+      *reinterpret_cast<float4*>(sc) = make_float4(bs[0], bs[1], 0.f, 0.f);
     }
     have = next(d);
   }
@@ -1479,22 +1488,21 @@ namespace {
 constexpr int64_t kNoAllocScratchBytes = QF2_SAGE_NOALLOC_SCRATCH_BYTES;
 __device__ __align__(256) uint8_t g_sage_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mu;
-constexpr int kMaxDevices = 64;
-void* g_noalloc_addr[kMaxDevices] = {};
-
 // The array's name is only a host-side stand-in; the device address comes from
-// cudaGetSymbolAddress, looked up once per device with that device current.
+// cudaGetSymbolAddress with the target device current.  It is looked up on every call
+// (no cache), so a call after cudaDeviceReset, or under another driver context, never
+// uses an address from a context that is gone.  The workspace starts at the first
+// 1024-byte boundary inside the array.
 int noalloc_scratch(void** out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QF2_ERR_DEVICE;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_sage_noalloc_scratch) != cudaSuccess || p == nullptr) return QF2_ERR_LAUNCH;
-    g_noalloc_addr[dev] = p;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return QF2_ERR_DEVICE;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_sage_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    qf2_record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol, "cudaGetSymbolAddress(noalloc scratch)");
+    return QF2_ERR_LAUNCH;
   }
-  *out = g_noalloc_addr[dev];
+  *out = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
   return QF2_OK;
 }
 }  // namespace
@@ -1505,14 +1513,20 @@ extern "C" int qf2_sageattn_noalloc(const void* q, const int64_t* q_strides, con
                                     float sm_scale, int dtype, qf2_stream_t stream) {
   if (D != kHeadDim) return QF2_ERR_SHAPE;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq < 0 || Skv < 0) return QF2_ERR_SHAPE;
-  // the workspace starts at the first 1024-byte boundary inside the array
   const int64_t usable = kNoAllocScratchBytes - 1024;
   const Layout L = make_layout(B, Hq, Hkv, B * Sq, B * Skv, Sq, Skv, false);
   if (L.off[11] > usable) return QF2_ERR_WORKSPACE;
   void* base = nullptr;
   const int st = noalloc_scratch(&base);
   if (st != QF2_OK) return st;
-  const uintptr_t a = (reinterpret_cast<uintptr_t>(base) + 1023) & ~uintptr_t(1023);
   return qf2_sageattn(q, q_strides, k, k_strides, v, v_strides, out, out_strides, B, Hq, Hkv, Sq, Skv, D, sm_scale,
-                      dtype, reinterpret_cast<void*>(a), usable, stream);
+                      dtype, base, usable, stream);
+}
+
+extern "C" int qf2_sageattn_noalloc_status(qf2_stream_t stream) {
+  void* base = nullptr;
+  const int st = noalloc_scratch(&base);
+  if (st != QF2_OK) return st;
+  // the status word sits at the start of the workspace, as for the other entry points
+  return qf2_workspace_status(base, stream);
 }

@@ -8,8 +8,11 @@ Flux wiring corrected: txt tokens precede img tokens in the joint sequence, q/k 
 RoPE as [B, L, H, D] with complex frequencies, the attention output projection is the
 block's own linear.  Weights are random (no checkpoints); every linear is a QLinear
 (FP8 e4m3 W8A8 for Flux, INT8 weight-only for Lumina).  Attention runs the Sage
-INT8/FP8 kernel; RMSNorm and RoPE run the library kernels; LayerNorm, modulation,
-GELU/SiLU and residual gating are torch glue around them.
+INT8/FP8 kernel.  The glue around it is fused into library kernels too: adaLN
+LayerNorm + modulate (+ the e4m3 activation quantizer) in one row kernel, q/k RMSNorm +
+RoPE in one kernel over the QKV projection, GELU / SwiGLU and the gated residual adds in
+the GEMM epilogues, and Lumina's post-norm gated residual + pre-norm modulate in one
+row kernel.
 
 Sequence parallelism (Ulysses): with a process group of P ranks each rank holds L/P
 tokens of the joint sequence; around attention an all-to-all turns [B, L/P, H, D]
@@ -17,7 +20,6 @@ into [B, L, H/P, D] and back (`ulysses_attention`).
 """
 from __future__ import annotations
 
-import itertools
 import math
 
 import torch
@@ -104,19 +106,21 @@ class SeqParallel:
         return recv.permute(1, 2, 0, 3, 4).reshape(B, L // P, P * Hp, D)
 
 
-    def attention_packed(self, qkv3: torch.Tensor, out: torch.Tensor, attn_fn=None) -> None:
+    def attention_packed(self, qkv3: torch.Tensor, out: torch.Tensor, attn_fn=None, permute=None) -> None:
         """qkv3 [B, L/P, 3, H, D] (q, k, v of this rank's tokens, contiguous) -> attention over
         the whole sequence written into out [B, L/P, H, D] (any strides, 16-byte rows).
         One all-to-all carries q, k and v together and one brings the output back; around
         them one copy packs the send buffer, one unpacks the received heads and one scatters
-        the output heads.  attn_fn(q, k, v, o) writes o [B, L, H/P, D] (default: Sage)."""
+        the output heads.  attn_fn(q, k, v, o) writes o [B, L, H/P, D] (default: Sage);
+        permute(dst, src, chunk_bytes, dims, src_strides, dst_strides) is the chunk copy
+        (default: the qf2_copy_chunks kernel)."""
         attn_fn = attn_fn or (lambda a, b, c, o: sageattn(a, b, c, tensor_layout="NHD", out=o))
         B, Ls, _, H, D = qkv3.shape
         if self.world == 1:
             attn_fn(qkv3[:, :, 0], qkv3[:, :, 1], qkv3[:, :, 2], out)
             return
         P, Hp = self.world, H // self.world
-        permute = _device_permute if qkv3.is_cuda else _host_permute
+        permute = permute or copy_chunks
         e = qkv3.element_size()
         hb = Hp * D * e                                   # bytes of one token's heads of one rank
         # [B, Ls, 3, P, Hp, D] -> [P, 3, B, Ls, Hp, D]: chunks of Hp*D, ordered (p, which, b, ls)
@@ -147,24 +151,6 @@ class SeqParallel:
             permute(out, o_recv, hb, (B, Ls, P), (Ls * hb, hb, B * Ls * hb), (ob, os_, hb))
         else:
             permute(out, o_recv, D * e, (B, Ls, P, Hp), (Ls * hb, hb, B * Ls * hb, D * e), (ob, os_, Hp * oh, oh))
-
-
-def _device_permute(dst, src, chunk, dims, ss, ds):
-    copy_chunks(dst, src, chunk, dims, ss, ds)
-
-
-def _host_permute(dst, src, chunk, dims, ss, ds):
-    """The same chunk copy through byte views on the host (gloo ranks in the CPU tests)."""
-    def flat(t):
-        n = t.untyped_storage().nbytes() // t.element_size()
-        return torch.as_strided(t, (n,), (1,), 0).view(torch.uint8), t.storage_offset() * t.element_size()
-
-    s8, bs = flat(src)
-    d8, bd = flat(dst)
-    for idx in itertools.product(*[range(n) for n in dims]):
-        so = bs + sum(i * st for i, st in zip(idx, ss))
-        do = bd + sum(i * st for i, st in zip(idx, ds))
-        d8[do:do + chunk].copy_(s8[so:so + chunk])
 
 
 def ulysses_attention(q, k, v, sp: SeqParallel, attn_fn=None) -> torch.Tensor:

@@ -121,7 +121,7 @@ def rmsnorm_apply(x: torch.Tensor, weight: torch.Tensor, eps: float, fused: bool
     Default: the eager body's rounding (src/kernels/__init__.py:74-80): the
     normalized row is rounded to x.dtype, multiplied by weight, and the result has
     the promoted dtype of (x, weight).  fused=True: the Triton body's rounding
-    (src/kernels/triton/rmsnorm.py:179-203): one rounding to x.dtype at the end.
+    (src/kernels/triton/rmsnorm.py:62-68): one rounding to x.dtype at the end.
     """
     require_device(x)
     N = weight.shape[0]

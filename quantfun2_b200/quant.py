@@ -1,17 +1,25 @@
 """Quantized linears behind the reference's quantization seam (src/quant.py).
 
 The reference picks a `qdtype` (qint8 / qfloat8 ..., src/quant.py:318-360) and
-`quantize_model` (:402-412) walks the model, swapping torchao weight subclasses into
-every nn.Linear (linear_inserter, :131-148).  Here the same names build QLinear
-modules whose forward runs the sm_100a kernels of libqf2b200.so:
+`quantize_model` (:402-412) walks the model, casts each nn.Linear to the qdtype's
+activation dtype (fp16 for qint8 / qfloat8, :326,331,383) and swaps a torchao weight
+subclass into its `weight` (linear_inserter, :131-148), so F.linear dispatches to the
+quantized matmul.  The same names here do the same with `QuantizedWeight`, a tensor
+subclass whose F.linear runs the sm_100a kernels of libqf2b200.so:
 
-  qint8      weight-only INT8: per-output-row symmetric codes; y = (x . bf16(codes)^T) * s_w + b
-  qfloat8    weight-only FP8 e4m3: per-output-row codes; same GEMM on bf16 copies of the codes
+  qint8      weight-only INT8: per-output-row symmetric codes; y = (x . codes^T) * s_w + b
+  qfloat8    weight-only FP8 e4m3: per-output-row codes; same GEMM
   qfloat8_w8a8  FP8 e4m3 weights and per-token e4m3 activations on the FP8 tensor cores:
-             y = (e4m3(x) . codes^T) * s_x * s_w + b
+             y = (e4m3(x) . codes^T) * s_x * s_w + b   (no counterpart in the reference)
 
-Activations are bf16 (the reference casts int8/float8 models to fp16, `supported_dtypes`
-at :326,331; the B200 kernels run bf16).
+Weights are quantized by torchao 0.7.0's steps in the weight's dtype
+(`qf2_quantize_weight_rows`).  Activations stay in their own dtype (fp16 or bf16): the
+codes are expanded exactly to that dtype and the GEMM runs fp16 x fp16 or bf16 x bf16
+on the tensor cores with fp32 accumulation, the per-channel scale and the bias in its
+epilogue, and one rounding to the activation dtype.
+
+`QLinear` is the module form the DiT steps of this package build directly (it adds the
+fused LayerNorm-modulate prologue and the GEMM epilogues).
 """
 from __future__ import annotations
 
@@ -20,13 +28,15 @@ from dataclasses import dataclass, field
 from functools import partial
 
 import torch
+import torch.nn.functional as F
 from torch import nn
 
 from . import _lib
 from ._lib import QF2Error, check, require_device, stream_ptr
 
-__all__ = ["qdtype", "QLinear", "qint8", "qfloat8", "qfloat8_w8a8", "quantize_model", "linear_inserter",
-           "quantize_rows", "codes_to_bf16", "gemm", "ln_modulate", "glu_interleave"]
+__all__ = ["qdtype", "QLinear", "QuantizedWeight", "qint8", "qfloat8", "qfloat8_w8a8", "quantize_model",
+           "linear_inserter", "quantize_rows", "quantize_weight", "codes_to_bf16", "codes_to", "gemm",
+           "ln_modulate", "glu_interleave"]
 
 
 def _ws(device) -> torch.Tensor:
@@ -49,6 +59,35 @@ def quantize_rows(x: torch.Tensor, fmt: str):
     return q, scales
 
 
+def quantize_weight(w: torch.Tensor, fmt: str):
+    """Per-output-row quantization of a weight [N, K] by torchao 0.7.0's steps, every step
+    rounded in w's dtype (fp16, bf16 or fp32): fmt "int8" -> (int8 codes, fp32 scales),
+    "e4m3" -> (uint8 e4m3 codes, fp32 scales)."""
+    require_device(w)
+    if w.dim() != 2:
+        raise QF2Error("quantize_weight expects a 2-D weight")
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    M, K = w.shape
+    q = torch.empty(M, K, dtype=torch.int8 if fmt == "int8" else torch.uint8, device=w.device)
+    scales = torch.empty(M, dtype=torch.float32, device=w.device)
+    check(_lib.load().qf2_quantize_weight_rows(w.data_ptr(), w.stride(0), _lib.dtype_code(w.dtype), M, K,
+                                               q.data_ptr(), K, _lib.QF2_I8 if fmt == "int8" else _lib.QF2_E4M3,
+                                               scales.data_ptr(), stream_ptr(w.device)), "qf2_quantize_weight_rows")
+    return q, scales
+
+
+def codes_to(q: torch.Tensor, fmt: str, dtype: torch.dtype) -> torch.Tensor:
+    """int8 / e4m3 codes -> exact bf16 or fp16 values."""
+    require_device(q)
+    M, K = q.shape
+    out = torch.empty(M, K, dtype=dtype, device=q.device)
+    check(_lib.load().qf2_codes_convert(q.data_ptr(), q.stride(0), _lib.QF2_I8 if fmt == "int8" else _lib.QF2_E4M3,
+                                        M, K, out.data_ptr(), K, _lib.dtype_code(dtype), stream_ptr(q.device)),
+          "qf2_codes_convert")
+    return out
+
+
 def codes_to_bf16(q: torch.Tensor, fmt: str) -> torch.Tensor:
     require_device(q)
     M, K = q.shape
@@ -63,7 +102,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
          residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, rows_per_gate: int = 1,
          glu: bool = False) -> torch.Tensor:
     """D = (a . b^T) * row_scale[:, None] * col_scale[None, :] + bias on tcgen05.
-    a [M, K], b [N, K]: bf16, or uint8 e4m3 codes with fp8=True.
+    a [M, K], b [N, K]: both bf16, both fp16, or uint8 e4m3 codes with fp8=True.
+    out_dtype bf16, fp16 or fp32 (fused residual / SwiGLU: bf16).
     Fused epilogue: GELU (tanh) on columns >= gelu_col0; D = residual + gate * D when
     residual is given (gate [rows/rows_per_gate, N] bf16, may be a strided view); with
     glu=True b holds SwiGLU weights in `glu_interleave` order and D = silu(gate) * up
@@ -74,6 +114,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
     N = b.shape[0]
     if b.shape[1] != K:
         raise QF2Error("inner dimensions differ")
+    if not fp8 and (a.dtype not in (torch.bfloat16, torch.float16) or b.dtype != a.dtype):
+        raise QF2Error("16-bit GEMM operands must both be bf16 or both fp16")
     if a.stride(-1) != 1:
         a = a.contiguous()
     if b.stride(-1) != 1:
@@ -96,7 +138,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
     ws = _ws(a.device)
     check(_lib.load().qf2_gemm_ex(
         a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), out.data_ptr(), out.stride(0), M, N, K,
-        _lib.QF2_E4M3 if fp8 else _lib.QF2_BF16, _lib.QF2_F32 if out_dtype == torch.float32 else _lib.QF2_BF16,
+        _lib.QF2_E4M3 if fp8 else _lib.dtype_code(a.dtype), _lib.dtype_code(out_dtype),
         row_scale.data_ptr() if row_scale is not None else None,
         col_scale.data_ptr() if col_scale is not None else None,
         bias.data_ptr() if bias is not None else None, bias_dt, int(gelu_col0), int(bool(glu)),
@@ -137,9 +179,16 @@ def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, rows_
     return (out, scales) if fp8 else out
 
 
+def _check_act(x: torch.Tensor) -> None:
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise QF2Error(f"quantized linears take fp16 or bf16 activations, got {x.dtype} "
+                       "(the reference casts the model to the qdtype's dtype first)")
+
+
 class QLinear(nn.Module):
-    """nn.Linear replacement holding per-output-row quantized weights.
-    mode: "int8" (weight-only), "fp8" (weight-only e4m3), "fp8_w8a8" (e4m3 weights and activations)."""
+    """nn.Linear replacement holding per-output-row quantized weights (the module form the
+    DiT steps use).  mode: "int8" (weight-only), "fp8" (weight-only e4m3), "fp8_w8a8"
+    (e4m3 weights and activations).  Activations run in their own dtype (fp16 or bf16)."""
 
     def __init__(self, codes: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None, mode: str,
                  in_features: int, out_features: int):
@@ -156,8 +205,8 @@ class QLinear(nn.Module):
         w = lin.weight.detach().to(device or lin.weight.device)
         if not w.is_cuda:
             raise QF2Error("quantize on a CUDA device (no CPU quantizer on this path)")
-        codes, scale = quantize_rows(w, "int8" if mode == "int8" else "e4m3")
-        bias = None if lin.bias is None else lin.bias.detach().to(w.device, torch.bfloat16)
+        codes, scale = quantize_weight(w, "int8" if mode == "int8" else "e4m3")
+        bias = None if lin.bias is None else lin.bias.detach().to(w.device, torch.float32)
         return cls(codes, scale, bias, mode, lin.in_features, lin.out_features)
 
     @property
@@ -165,33 +214,116 @@ class QLinear(nn.Module):
         return self.mode == "fp8_w8a8"
 
     def prep(self, x2: torch.Tensor):
-        """Activation operand for this linear: (e4m3 codes, per-row scales) or (bf16, None)."""
-        if x2.dtype != torch.bfloat16:
-            x2 = x2.to(torch.bfloat16)
+        """Activation operand for this linear: (e4m3 codes, per-row scales) or (x, None)."""
+        _check_act(x2)
         if self.fp8_activations:
             return quantize_rows(x2, "e4m3")
         return x2, None
 
     def prep_ln_modulate(self, x2, shift, scale, rows_per_batch):
-        """Fused LayerNorm + modulate producing this linear's activation operand."""
+        """Fused LayerNorm + modulate producing this linear's activation operand (bf16)."""
         if self.fp8_activations:
             return ln_modulate(x2, shift, scale, rows_per_batch, "e4m3")
         return ln_modulate(x2, shift, scale, rows_per_batch, "bf16"), None
 
-    def run(self, a: torch.Tensor, row_scale, **epilogue) -> torch.Tensor:
-        """GEMM on a prepared operand; epilogue kwargs as in `gemm` (out, gelu_col0, residual, gate...)."""
+    def run(self, a: torch.Tensor, row_scale, out_dtype=torch.bfloat16, **epilogue) -> torch.Tensor:
+        """GEMM on a prepared operand; epilogue kwargs as in `gemm` (out, gelu_col0, residual, gate...).
+        A 16-bit operand sets the output dtype (its own); e4m3 operands use out_dtype."""
         if self.fp8_activations:
-            return gemm(a, self.codes, row_scale=row_scale, col_scale=self.scale, bias=self.bias, fp8=True, **epilogue)
-        wb = codes_to_bf16(self.codes, "int8" if self.mode == "int8" else "e4m3")
-        return gemm(a, wb, col_scale=self.scale, bias=self.bias, **epilogue)
+            return gemm(a, self.codes, row_scale=row_scale, col_scale=self.scale, bias=self.bias, fp8=True,
+                        out_dtype=out_dtype, **epilogue)
+        fmt = "int8" if self.mode == "int8" else "e4m3"
+        wb = codes_to_bf16(self.codes, fmt) if a.dtype == torch.bfloat16 else codes_to(self.codes, fmt, a.dtype)
+        return gemm(a, wb, col_scale=self.scale, bias=self.bias, out_dtype=a.dtype, **epilogue)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
-        y = self.run(*self.prep(x.reshape(-1, shape[-1])))
+        y = self.run(*self.prep(x.reshape(-1, shape[-1])), out_dtype=x.dtype)
         return y.reshape(*shape[:-1], self.out_features)
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, mode={self.mode}"
+
+
+class QuantizedWeight(torch.Tensor):
+    """Quantized nn.Linear weight, the counterpart of the torchao AffineQuantizedTensor the
+    reference sets as `lin.weight` (src/quant.py:131-148).  It keeps the per-output-row
+    codes and fp32 scales on the device and reports the weight's logical shape [out, in]
+    and the activation dtype; F.linear(x, w, b) with this weight runs the tcgen05 GEMM
+    (x in fp16 or bf16; mode "fp8_w8a8" quantizes x per token to e4m3 first).  Other ops
+    are refused: there is no dequantize-to-float fallback.  `.to(device)` moves the codes;
+    `.to(dtype)` changes the activation dtype (fp16 / bf16) without requantizing."""
+
+    @staticmethod
+    def __new__(cls, codes: torch.Tensor, scale: torch.Tensor, mode: str, dtype: torch.dtype, shape):
+        return torch.Tensor._make_wrapper_subclass(cls, tuple(shape), dtype=dtype, device=codes.device,
+                                                   requires_grad=False)
+
+    def __init__(self, codes: torch.Tensor, scale: torch.Tensor, mode: str, dtype: torch.dtype, shape):
+        self.codes = codes
+        self.scale = scale
+        self.mode = mode
+
+    @classmethod
+    def from_float(cls, w: torch.Tensor, mode: str) -> "QuantizedWeight":
+        """Quantize a float weight [out, in] (on an sm_100 device) in its own dtype."""
+        codes, scale = quantize_weight(w.detach(), "int8" if mode == "int8" else "e4m3")
+        act = w.dtype if w.dtype in (torch.float16, torch.bfloat16) else torch.float16
+        return cls(codes, scale, mode, act, w.shape)
+
+    def __repr__(self, *, tensor_contents=None) -> str:  # noqa: D105
+        return (f"QuantizedWeight(shape={tuple(self.shape)}, mode={self.mode}, act_dtype={self.dtype}, "
+                f"device={self.device})")
+
+    def _with(self, codes=None, scale=None, dtype=None) -> "QuantizedWeight":
+        return QuantizedWeight(self.codes if codes is None else codes, self.scale if scale is None else scale,
+                               self.mode, dtype or self.dtype, self.shape)
+
+    def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+        _check_act(x)
+        require_device(x)
+        N, K = self.shape
+        x2 = x.reshape(-1, K)
+        b = None if bias is None else bias.detach().float()
+        if self.mode == "fp8_w8a8":
+            xc, xs = quantize_rows(x2, "e4m3")
+            y = gemm(xc, self.codes, row_scale=xs, col_scale=self.scale, bias=b, fp8=True, out_dtype=x.dtype)
+        else:
+            wv = codes_to(self.codes, "int8" if self.mode == "int8" else "e4m3", x.dtype)
+            y = gemm(x2.contiguous() if x2.stride(-1) != 1 else x2, wv, col_scale=self.scale, bias=b,
+                     out_dtype=x.dtype)
+        return y.reshape(*x.shape[:-1], N)
+
+    @classmethod
+    def __torch_function__(cls, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        if func is F.linear:
+            x, w = args[0], args[1]
+            b = args[2] if len(args) > 2 else kwargs.get("bias")
+            if not isinstance(w, QuantizedWeight) or isinstance(x, QuantizedWeight):
+                raise QF2Error("F.linear with a QuantizedWeight expects it as the weight")
+            return w.linear(x, b)
+        if func is torch._has_compatible_shallow_copy_type:
+            return False  # module.to() swaps the parameter instead of set_data (src/quant.py:85-90)
+        with torch._C.DisableTorchFunctionSubclass():
+            return func(*args, **kwargs)
+
+    @classmethod
+    def __torch_dispatch__(cls, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        aten = torch.ops.aten
+        w = args[0] if args else None
+        if func is aten.detach.default or func is aten.alias.default:
+            return w._with()
+        if func is aten._to_copy.default:
+            dev = kwargs.get("device") or w.device
+            dt = kwargs.get("dtype") or w.dtype
+            if dt not in (torch.float16, torch.bfloat16):
+                raise QF2Error(f"a quantized weight runs fp16 or bf16 activations, not {dt}")
+            return w._with(codes=w.codes.to(dev), scale=w.scale.to(dev), dtype=dt)
+        if func is aten._has_compatible_shallow_copy_type.default:
+            return False
+        raise QF2Error(f"{func} is not defined on a quantized weight (only F.linear, detach and .to)")
 
 
 @dataclass
@@ -213,17 +345,30 @@ class qdtype:
         return self.apply_function(*args, **kwargs), self.supported_dtypes[0]
 
 
-def linear_inserter(mode: str):
-    """Mirror of src/quant.py:131-148: returns a function that converts one nn.Linear."""
+def linear_inserter(mode: str, allow_requires_grad: bool = False):
+    """Mirror of src/quant.py:131-148: returns a function that quantizes one nn.Linear in
+    place -- its weight becomes a QuantizedWeight parameter (on `device`, quantized on
+    `quant_device`) and the module itself is kept, so state-dict keys do not change."""
 
     def insert(lin: nn.Linear, device=None, quant_device=None):
-        return QLinear.from_linear(lin, mode, device=quant_device or device)
+        device = device if device is not None else lin.weight.device
+        quant_device = quant_device if quant_device is not None else lin.weight.device
+        w = lin.weight.detach().to(device=quant_device)
+        if not w.is_cuda:
+            raise QF2Error("quantize on a CUDA device (no CPU quantizer on this path)")
+        qw = QuantizedWeight.from_float(w, mode).to(device)
+        lin.weight = nn.Parameter(qw, requires_grad=False)
+        lin.extra_repr = types.MethodType(
+            lambda self: f"in_features={self.in_features}, out_features={self.out_features}, "
+                         f"weight={self.weight!r}", lin)
+        return lin
 
     return insert
 
 
-qint8 = qdtype("int8", partial(linear_inserter, "int8"), supported_dtypes=[torch.bfloat16])
-qfloat8 = qdtype("float8", partial(linear_inserter, "fp8"), supported_dtypes=[torch.bfloat16])
+# activation dtypes as the reference's supported_dtypes (src/quant.py:323-332)
+qint8 = qdtype("int8", partial(linear_inserter, "int8"), supported_dtypes=[torch.float16])
+qfloat8 = qdtype("float8", partial(linear_inserter, "fp8"), supported_dtypes=[torch.float16])
 qfloat8_w8a8 = qdtype("float8_w8a8", partial(linear_inserter, "fp8_w8a8"), supported_dtypes=[torch.bfloat16])
 
 
@@ -232,24 +377,24 @@ def _nil(module: nn.Module, fqn: str) -> bool:
 
 
 def _replace(model: nn.Module, replacement_map, filter_fn, cur_fqn: str, device, quant_device):
+    """src/quant.py:368-399: the selected module is cast to the qdtype's activation dtype
+    and converted; every other module is walked and then cast to that dtype."""
     if filter_fn(model, cur_fqn[:-1]):
-        conv, dt = (replacement_map[cur_fqn[:-1]] if isinstance(replacement_map, dict) else replacement_map)()
-        return conv(model.to(dtype=dt), device=device, quant_device=quant_device)
+        conv, dt = (replacement_map[cur_fqn] if isinstance(replacement_map, dict) else replacement_map)()
+        return conv(model.to(dtype=dt), device=device, quant_device=quant_device).to(device=device)
     for name, child in model.named_children():
         new = _replace(child, replacement_map, filter_fn, f"{cur_fqn}{name}.", device, quant_device)
         if new is not child:
             setattr(model, name, new)
-    return model
+    if isinstance(replacement_map, dict):
+        return model.to(replacement_map[cur_fqn]()[1])
+    return model.to(replacement_map()[1])
 
 
 def quantize_model(model: nn.Module, dtype_map, device="cuda", quantization_device="cuda", skip=_nil) -> nn.Module:
     """Mirror of src/quant.py:402-412: every module selected by `skip` (default: every
-    nn.Linear) is replaced by the converter of `dtype_map` (a qdtype, or a dict from
-    module path to qdtype); the rest of the model is moved to the qdtype's activation dtype."""
-    model = _replace(model, dtype_map, skip, "", device, quantization_device)
-    dt = (dtype_map if not isinstance(dtype_map, dict) else next(iter(dtype_map.values()))).supported_dtypes[0]
-    for m in model.modules():
-        if not isinstance(m, QLinear):
-            for p in m.parameters(recurse=False):
-                p.data = p.data.to(device=device, dtype=dt) if p.is_floating_point() else p.data.to(device)
-    return model.to(device)
+    nn.Linear) gets its weight quantized by the converter of `dtype_map` (a qdtype, or a
+    dict from module path + "." to qdtype, as the reference indexes it); the model ends up
+    in the qdtype's activation dtype."""
+    _replace(model, dtype_map, skip, "", device, quantization_device)
+    return model

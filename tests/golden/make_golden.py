@@ -1,13 +1,14 @@
 """Generate golden vectors from the reference implementation itself.
 
 Run in the build container, where the reference source tree is mounted:
-    python tests/golden/make_golden.py [path/to/reference]
+    python tests/golden/make_golden.py <path of the quantfun2 source tree>
 It imports the reference's eager kernel bodies (src/kernels/__init__.py) and its
 JointAttention block (src/models/common/attn.py) on the CPU, using the import shim
 the reference needs on a GPU-less host (triton absent -> eager bodies bound;
 src.models package inits skipped because they import diffusers), runs them on
-seeded inputs and writes tests/golden/ref_ops.npz.  bf16 tensors are stored as
-uint16 bit patterns.  The reference is not needed to *use* the fixtures.
+seeded inputs and writes tests/golden/ref_ops.npz and tests/golden/ref_jattn.npz.
+bf16 tensors are stored as uint16 bit patterns.  The reference is not needed to *use*
+the fixtures.
 """
 from __future__ import annotations
 
@@ -21,6 +22,27 @@ import numpy as np
 import torch
 
 OUT = Path(__file__).resolve().parent / "ref_ops.npz"
+OUT_JATTN = Path(__file__).resolve().parent / "ref_jattn.npz"
+
+# JointAttention blocks at the attention kernel's head dims: (tag, dim, q heads, kv heads,
+# seq, grid side).  Head dim 128 is the Flux / single-block configuration's, 96 Lumina's
+# (24 q / 8 kv heads there, the same 3:1 grouping here).
+JATTN_CASES = (("d128", 512, 4, 2, 320, 20), ("d96", 576, 6, 2, 320, 20))
+
+
+def jattn_weights(dim: int, heads: int, kv_heads: int, seed: int) -> dict[str, torch.Tensor]:
+    """Projection and norm weights of a JointAttention block, from a seeded CPU generator
+    (uniform +-1/sqrt(in), the nn.Linear default range) and rounded to bf16 so a bf16
+    device path holds them exactly.  The GPU test rebuilds them with this function."""
+    g = torch.Generator().manual_seed(seed)
+    hd = dim // heads
+    shapes = {"wq": (heads * hd, dim), "wk": (kv_heads * hd, dim), "wv": (kv_heads * hd, dim),
+              "wo": (dim, heads * hd)}
+    w = {n: ((torch.rand(*sh, generator=g) * 2 - 1) / math.sqrt(sh[1])).bfloat16().float()
+         for n, sh in shapes.items()}
+    w["q_norm"] = (torch.rand(hd, generator=g) + 0.5).bfloat16().float()
+    w["k_norm"] = (torch.rand(hd, generator=g) + 0.5).bfloat16().float()
+    return w
 
 
 def import_reference(root: str):
@@ -117,6 +139,40 @@ def main(root: str) -> None:
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(out)} arrays)")
 
+    # ---- JointAttention at head dims 128 and 96 (common/attn.py:133-236), SDPA branch,
+    #      fp32, GQA, 2-axis RoPE over a 16 x 20 grid (320 tokens: a ragged last 128-token tile);
+    #      bf16-representable x and weights
+    ja: dict[str, np.ndarray] = {}
+    for i, (tag, dim, heads, kvh, seq, side) in enumerate(JATTN_CASES):
+        hd = dim // heads
+        blk = A.JointAttention(0, 10000, dim, heads, kvh, qk_norm=True).eval()
+        w = jattn_weights(dim, heads, kvh, seed=100 + i)
+        gx = torch.Generator().manual_seed(200 + i)
+        with torch.no_grad():
+            for n in ["wq", "wk", "wv", "wo"]:
+                getattr(blk, n).weight.copy_(w[n])
+            blk.q_norm.weight.copy_(w["q_norm"])
+            blk.k_norm.weight.copy_(w["k_norm"])
+            x = torch.randn(1, seq, dim, generator=gx).bfloat16().float()
+            mask = torch.ones(1, seq, dtype=torch.bool)
+            third = hd // 2 // 3 * 2
+            axes = (hd - 2 * third, third, third)
+            emb3 = L.RopeEmbedder(theta=10000.0, axes_dims=axes, axes_lens=(1, 64, 64))
+            ids3 = torch.zeros(1, seq, 3, dtype=torch.int32)
+            ids3[0, :, 1] = torch.arange(seq) // side
+            ids3[0, :, 2] = torch.arange(seq) % side
+            f3 = emb3(ids3)
+            y = blk(x, mask, f3)
+        ja[f"{tag}_x_bf16"] = bf16_bits(x.bfloat16())
+        ja[f"{tag}_freqs"] = torch.view_as_real(f3).numpy()
+        ja[f"{tag}_y"] = y.numpy()
+        ja[f"{tag}_meta"] = np.array([dim, heads, kvh, seq, 100 + i], dtype=np.int64)
+        ja[f"{tag}_wsum"] = np.array([float(w[n].double().sum()) for n in ["wq", "wk", "wv", "wo", "q_norm", "k_norm"]])
+    np.savez_compressed(OUT_JATTN, **ja)
+    print(f"wrote {OUT_JATTN} ({OUT_JATTN.stat().st_size} bytes, {len(ja)} arrays)")
+
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the quantfun2 source tree>")
+    main(sys.argv[1])

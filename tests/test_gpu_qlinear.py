@@ -31,6 +31,44 @@ def test_quantize_rows_bit_exact(cuda, fmt):
     assert np.array_equal(q.cpu().numpy().view(np.uint8), ref_q.view(np.uint8))
 
 
+@pytest.mark.parametrize("fmt", ["int8", "e4m3"])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_quantize_weight_torchao_rule_bit_exact(cuda, fmt, dtype):
+    """Weight quantizer of the reference's quantize-on-load (torchao 0.7.0 steps in the
+    weight's dtype) against the restatement: codes and scales bit for bit, including an
+    all-zero row and, in fp16, a row whose reciprocal scale overflows to inf."""
+    from quantfun2_b200.quant import quantize_weight
+
+    g = torch.Generator().manual_seed(1)
+    w = (torch.randn(333, 1000, generator=g) * torch.rand(333, 1, generator=g) * 0.2).to(dtype)
+    w[5] = 0
+    w[9] = w[9] * 1e-3          # amax ~1e-4: fp16 scale ~1e-6 -> 1/scale overflows fp16
+    q, s = quantize_weight(w.to(cuda), fmt)
+    tag = {torch.float16: "f16", torch.bfloat16: "bf16", torch.float32: "f32"}[dtype]
+    ref_q, ref_s = oq.quantize_weight_torchao(w.float().numpy(), fmt, tag)
+    assert np.array_equal(s.cpu().numpy(), ref_s)
+    assert np.array_equal(q.cpu().numpy().view(np.uint8), ref_q.view(np.uint8))
+
+
+@pytest.mark.parametrize("mnk", [(128, 256, 64), (300, 776, 200), (2304, 3072, 1024)])
+def test_gemm_fp16(cuda, mnk):
+    """fp16 x fp16 operands (kind::f16 with the f16 format), fp16 and fp32 output."""
+    from quantfun2_b200.quant import gemm
+
+    M, N, K = mnk
+    g = torch.Generator(device=cuda).manual_seed(M + 1)
+    a = torch.randn(M, K, device=cuda, generator=g).half()
+    b = torch.randn(N, K, device=cuda, generator=g).half()
+    cs = torch.rand(N, device=cuda, generator=g) + 0.5
+    bias = torch.randn(N, device=cuda, generator=g)
+    ref = (a.double() @ b.double().T) * cs.double()[None, :] + bias.double()[None, :]
+    d32 = gemm(a, b, col_scale=cs, bias=bias, out_dtype=torch.float32)
+    assert rel_err(d32.cpu(), ref.cpu()) < 1e-5
+    d16 = gemm(a, b, col_scale=cs, bias=bias, out_dtype=torch.float16)
+    assert d16.dtype == torch.float16
+    assert rel_err(d16.float().cpu(), ref.cpu()) < 1e-3
+
+
 @pytest.mark.parametrize("mnk", [(128, 256, 64), (300, 776, 200), (4608, 3072, 3072), (257, 2304, 6144)])
 def test_gemm_bf16(cuda, mnk):
     from quantfun2_b200.quant import gemm
@@ -92,42 +130,82 @@ def test_gemm_e4m3(cuda, mnk):
 
 
 @pytest.mark.parametrize("mode", ["int8", "fp8", "fp8_w8a8"])
-def test_qlinear_vs_oracle_and_float(cuda, mode):
+@pytest.mark.parametrize("act", [torch.bfloat16, torch.float16])
+def test_qlinear_vs_oracle_and_float(cuda, mode, act):
     from quantfun2_b200.quant import QLinear
 
     torch.manual_seed(1)
     lin = torch.nn.Linear(2304, 768, bias=True)
-    x = torch.randn(4, 300, 2304).bfloat16()
-    ql = QLinear.from_linear(lin.to(cuda).bfloat16(), mode)
-    y = ql(x.to(cuda)).float().cpu().numpy().reshape(-1, 768)
+    x = torch.randn(4, 300, 2304).to(act)
+    ql = QLinear.from_linear(lin.to(cuda).to(act), mode)
+    y = ql(x.to(cuda))
+    assert y.dtype == act
+    y = y.float().cpu().numpy().reshape(-1, 768)
     codes = ql.codes.cpu().numpy()
     scale = ql.scale.cpu().numpy()
     bias = ql.bias.float().cpu().numpy()
     xs = x.float().numpy().reshape(-1, 2304)
+    tag = "f16" if act == torch.float16 else "bf16"
+    ref_q, ref_s = oq.quantize_weight_torchao(lin.weight.detach().to(act).float().cpu().numpy(),
+                                              "int8" if mode == "int8" else "e4m3", tag)
+    assert np.array_equal(codes.view(np.uint8), ref_q.view(np.uint8)) and np.array_equal(scale, ref_s)
     if mode == "fp8_w8a8":
         ref = oq.linear_w8a8_e4m3(xs, codes.view(np.uint8), scale, bias)
     else:
         ref = oq.linear_weight_only(xs, codes.view(np.uint8) if mode == "fp8" else codes, scale, bias,
                                     fp8=mode == "fp8")
     assert rel_err(y, ref) < 8e-3
-    full = (xs.astype(np.float64) @ lin.weight.detach().bfloat16().float().cpu().numpy().astype(np.float64).T
-            + lin.bias.detach().bfloat16().float().cpu().numpy())
+    full = (xs.astype(np.float64) @ lin.weight.detach().to(act).float().cpu().numpy().astype(np.float64).T
+            + lin.bias.detach().to(act).float().cpu().numpy())
     cos = float((y.ravel() @ full.ravel()) / math.sqrt((y.ravel() @ y.ravel()) * (full.ravel() @ full.ravel())))
     assert cos > (0.9999 if mode == "int8" else 0.999), cos
 
 
-def test_quantize_model_swaps_linears(cuda):
-    from quantfun2_b200.quant import QLinear, qint8, quantize_model
+class _AttnLinears(torch.nn.Module):
+    """The linears of the reference's JointAttention (src/models/common/attn.py:133-188):
+    wq / wk / wv without bias, wo without bias, plus a biased MLP pair."""
+
+    def __init__(self, dim=512, kv=256):
+        super().__init__()
+        self.wq = torch.nn.Linear(dim, dim, bias=False)
+        self.wk = torch.nn.Linear(dim, kv, bias=False)
+        self.wv = torch.nn.Linear(dim, kv, bias=False)
+        self.wo = torch.nn.Linear(dim, dim, bias=False)
+        self.mlp = torch.nn.Sequential(torch.nn.Linear(dim, 1024), torch.nn.SiLU(), torch.nn.Linear(1024, dim))
+
+    def forward(self, x):
+        return self.wo(self.wq(x)) + self.mlp(x) + self.wk(x).sum(-1, keepdim=True) * self.wv(x).mean()
+
+
+@pytest.mark.parametrize("qname", ["qint8", "qfloat8"])
+def test_quantize_model_keeps_modules_and_keys(cuda, qname):
+    """quantize_model as the reference defines it (src/quant.py:131-148, :368-412): the
+    nn.Linear modules stay, their weights become quantized tensor subclasses, the model
+    ends in fp16 (the qdtype's activation dtype) and the state-dict keys do not change;
+    F.linear on an fp16 activation runs the fp16 tcgen05 GEMM."""
+    from quantfun2_b200 import quant
 
     torch.manual_seed(0)
-    m = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.SiLU(), torch.nn.Linear(512, 256))
-    x = torch.randn(64, 256)
-    ref = m(x)
-    qm = quantize_model(m, qint8, device="cuda", quantization_device="cuda")
-    assert isinstance(qm[0], QLinear) and isinstance(qm[2], QLinear)
-    y = qm(x.to(cuda).bfloat16()).float().cpu()
-    cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
-    assert cos > 0.999
+    m = _AttnLinears()
+    keys = list(m.state_dict().keys())
+    wq0 = m.wq.weight.detach().half().float().numpy()
+    x = torch.randn(3, 200, 512)
+    ref = m(x).double()
+    qm = quant.quantize_model(m, getattr(quant, qname), device="cuda", quantization_device="cuda")
+    assert list(qm.state_dict().keys()) == keys
+    for name in ["wq", "wk", "wv", "wo"]:
+        lin = getattr(qm, name)
+        assert type(lin) is torch.nn.Linear and isinstance(lin.weight, quant.QuantizedWeight)
+        assert lin.weight.dtype == torch.float16 and lin.weight.shape == (lin.out_features, lin.in_features)
+    assert qm.mlp[0].bias.dtype == torch.float16
+    y = qm(x.to(cuda).half())
+    assert y.dtype == torch.float16
+    cos = torch.nn.functional.cosine_similarity(y.double().cpu().flatten(), ref.flatten(), dim=0).item()
+    assert cos > (0.9999 if qname == "qint8" else 0.999), cos
+    # the codes are torchao's, computed in fp16 arithmetic
+    ref_q, ref_s = oq.quantize_weight_torchao(wq0, "int8" if qname == "qint8" else "e4m3", "f16")
+    assert np.array_equal(qm.wq.weight.codes.cpu().numpy().view(np.uint8), ref_q.view(np.uint8))
+    assert np.array_equal(qm.wq.weight.scale.cpu().numpy(), ref_s)
 
 
 def test_gemm_fused_gelu_residual_gate(cuda):

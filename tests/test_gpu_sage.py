@@ -29,13 +29,12 @@ def cosine(a, b):
 def check_codes(dec, q, k, v, B, Hq, Hkv, sm_scale):
     for b in range(B):
         for h in range(Hq):
-            hk = h // (Hq // Hkv)
-            ref = sage.quantize_head(q[b][h], k[b][hk], v[b][hk], sm_scale)
+            rq, rs = sage.quantize_q(q[b][h], sm_scale)
             gq = dec[("q", b, h)]
-            assert np.array_equal(gq["codes"], ref["qcodes"]), (b, h)
-            assert np.array_equal(gq["scales"], ref["qscales"]), (b, h)
+            assert np.array_equal(gq["codes"], rq), (b, h)
+            assert np.array_equal(gq["scales"], rs), (b, h)
         for h in range(Hkv):
-            ref = sage.quantize_head(q[b][0], k[b][h], v[b][h], sm_scale)
+            ref = sage.quantize_kv(k[b][h], v[b][h])
             gk = dec[("k", b, h)]
             assert np.array_equal(gk["kmean"], ref["kmean"]), (b, h)
             assert np.array_equal(gk["codes"], ref["kcodes"]), (b, h)
@@ -58,6 +57,47 @@ def test_sage_quant_codes_bit_exact(cuda, layout, shape):
     dec = decode(ws.cpu().numpy(), offs, B, Hq, Hkv, [Sq] * B, [Skv] * B,
                  [b * ((Sq + 127) // 128) for b in range(B)], [b * ((Skv + 127) // 128) for b in range(B)])
     check_codes(dec, q.float().numpy(), k.float().numpy(), v.float().numpy(), B, Hq, Hkv, sm)
+
+
+def test_sage_quant_codes_bit_exact_flux_config(cuda):
+    """The benchmarked configuration, B=2 x 24 heads x 4608 tokens, every head: 48 kv heads
+    against the ~25 K/V clusters the quantization kernel forms on 148 SMs, so each cluster
+    walks two heads one after another (the exchange marker between them)."""
+    from quantfun2_b200.attention import sage_quantize
+
+    B, H, S = 2, 24, 4608
+    q, k, v = make_qkv(B, H, H, S, S, seed=1234)
+    sm = 1.0 / math.sqrt(128)
+    ws, offs = sage_quantize(q.to(cuda), k.to(cuda), v.to(cuda), sm)
+    torch.cuda.synchronize()
+    nt = (S + 127) // 128
+    dec = decode(ws.cpu().numpy(), offs, B, H, H, [S] * B, [S] * B, [b * nt for b in range(B)],
+                 [b * nt for b in range(B)])
+    check_codes(dec, q.float().numpy(), k.float().numpy(), v.float().numpy(), B, H, H, sm)
+
+
+def test_sage_quant_codes_bit_exact_lumina_varlen(cuda):
+    """The Lumina-shaped batch: 8 packed sequences of 4352 tokens (4096 image + 256 caption),
+    24 query / 8 kv heads (GQA), varlen form; every head."""
+    from quantfun2_b200.attention import sage_quantize
+
+    lens = [4352] * 8
+    Hq, Hkv = 24, 8
+    g = torch.Generator().manual_seed(8)
+    T = sum(lens)
+    q = torch.randn(T, Hq, 128, generator=g).bfloat16()
+    k = (torch.randn(T, Hkv, 128, generator=g) + 3 * torch.randn(1, Hkv, 128, generator=g)).bfloat16()
+    v = torch.randn(T, Hkv, 128, generator=g).bfloat16()
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    sm = 1.0 / math.sqrt(128)
+    ws, offs = sage_quantize(q.to(cuda), k.to(cuda), v.to(cuda), sm, cu_seqlens_q=cu.to(cuda),
+                             cu_seqlens_k=cu.to(cuda), max_seqlen_q=max(lens), max_seqlen_k=max(lens))
+    torch.cuda.synchronize()
+    tile0 = [int(cu[b]) // 128 + b for b in range(len(lens))]
+    dec = decode(ws.cpu().numpy(), offs, len(lens), Hq, Hkv, lens, lens, tile0, tile0)
+    per = lambda t, b: t[cu[b]:cu[b + 1]].float().permute(1, 0, 2).numpy()  # noqa: E731
+    check_codes(dec, [per(q, b) for b in range(8)], [per(k, b) for b in range(8)], [per(v, b) for b in range(8)],
+                len(lens), Hq, Hkv, sm)
 
 
 def test_sage_quant_codes_varlen_bit_exact(cuda):

@@ -6,6 +6,7 @@ import numpy as np
 import pytest
 
 from oracle import ops, sage
+from tests.golden_cases import jattn_case
 from oracle.numerics import bf16_bits_to_f32, f32_to_bf16_bits, round_bf16
 
 
@@ -89,11 +90,51 @@ def test_sage_oracle_close_to_sdpa():
 
 
 def test_sage_quant_rules():
-    """Hand-checkable cases of the stated quantization rules."""
+    """Hand-checkable cases of the published rule (x / scale, + 0.5 * sign, truncate)."""
     x = np.zeros((64, 128), np.float32)
-    x[0, 0], x[1, 1], x[2, 2] = 127.0, 63.5, -0.5   # scale 1.0, inverse 1.0: ties go to even
+    x[0, 0], x[1, 1], x[2, 2], x[3, 3] = 127.0, 63.5, -0.5, 2.5   # scale 1.0: halves go away from zero
+    x[4, 4] = np.nextafter(np.float32(0.5), np.float32(0))         # 0.5 - 2^-25: the fp32 add rounds to 1.0
+    x[5, 5] = np.float32(-2.4999998)
     codes, scales = sage._block_quant(x)
     assert scales[0] == np.float32(1.0)
-    assert codes[0, 0] == 127 and codes[1, 1] == 64 and codes[2, 2] == 0
+    assert codes[0, 0] == 127 and codes[1, 1] == 64 and codes[2, 2] == -1 and codes[3, 3] == 3
+    assert codes[4, 4] == 1 and codes[5, 5] == -2
     z, zs = sage._block_quant(np.zeros((70, 128), np.float32))
     assert (z == 0).all() and (zs == 1.0).all() and zs.shape == (2,)
+
+
+def test_torchao_weight_rule_cases():
+    """Hand-checkable cases of the torchao 0.7.0 weight rule in fp16."""
+    from oracle import qlinear as oq
+
+    w = np.zeros((3, 4), np.float32)
+    w[0] = [1.0, -0.5, 0.25, 0.0]        # scale = f16(1/127.5); codes round half to even in fp16
+    w[2] = [1e-4, -1e-4, 0.0, 5e-5]      # fp16 scale ~7.8e-7: 1/scale overflows fp16 -> inf
+    q, s = oq.quantize_weight_torchao(w, "int8", "f16")
+    assert s[0] == np.float32(np.float16(np.float32(1.0) / np.float32(127.5)))
+    assert q[0, 0] == 127 and q[0, 3] == 0
+    assert s[1] == np.float32(np.finfo(np.float32).eps) and (q[1] == 0).all()   # zero row: clamp to eps
+    assert q[2, 0] == 127 and q[2, 1] == -128 and q[2, 2] == 0                   # inf * 0 = nan -> 0
+    q8, s8 = oq.quantize_weight_torchao(w, "e4m3", "f16")
+    assert q8[0, 0] == 0x7E   # 448
+
+
+@pytest.mark.parametrize("tag", ["d128", "d96"])
+def test_joint_attention_golden_head_dims(tag):
+    """The oracle composition reproduces the reference JointAttention at head dims 128 and
+    96 with GQA and a ragged last tile (tests/golden/ref_jattn.npz)."""
+    c = jattn_case(tag)
+    D = c["dim"] // c["heads"]
+    x = c["x"][0].astype(np.float64)
+    w = c["w"]
+    q = (x @ w["wq"].T.astype(np.float64)).astype(np.float32).reshape(1, c["seq"], c["heads"], D)
+    k = (x @ w["wk"].T.astype(np.float64)).astype(np.float32).reshape(1, c["seq"], c["kvh"], D)
+    v = (x @ w["wv"].T.astype(np.float64)).astype(np.float32).reshape(1, c["seq"], c["kvh"], D)
+    q = ops.rmsnorm_apply(q, w["q_norm"], 1e-6, "f32")
+    k = ops.rmsnorm_apply(k, w["k_norm"], 1e-6, "f32")
+    q, k = ops.rope_apply(q, k, cplx(c["freqs"]).astype(np.complex64), "f32")
+    o = sage.sdpa_reference(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3),
+                            1.0 / math.sqrt(D))
+    y = (o.transpose(0, 2, 1, 3).reshape(1, c["seq"], c["dim"]).astype(np.float64)
+         @ w["wo"].T.astype(np.float64)).astype(np.float32)
+    np.testing.assert_allclose(y, c["y"], rtol=1e-4, atol=2e-5)

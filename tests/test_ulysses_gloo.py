@@ -1,11 +1,26 @@
 """CPU, world_size 2 (gloo): the Ulysses sequence<->head all-to-all layout used around
 attention by the multi-GPU DiT step."""
+import itertools
 import os
 
 import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+
+
+def _host_permute(dst, src, chunk, dims, ss, ds):
+    """qf2_copy_chunks restated through byte views on the host (gloo ranks have no GPU)."""
+    def flat(t):
+        n = t.untyped_storage().nbytes() // t.element_size()
+        return torch.as_strided(t, (n,), (1,), 0).view(torch.uint8), t.storage_offset() * t.element_size()
+
+    s8, bs = flat(src)
+    d8, bd = flat(dst)
+    for idx in itertools.product(*[range(n) for n in dims]):
+        so = bs + sum(i * st for i, st in zip(idx, ss))
+        do = bd + sum(i * st for i, st in zip(idx, ds))
+        d8[do:do + chunk].copy_(s8[so:so + chunk])
 
 
 def _worker(rank, world, port, q):
@@ -39,7 +54,7 @@ def _worker(rank, world, port, q):
             def attn_o(a, b, c, o):
                 o.copy_(attn(a, b, c))
 
-            sp.attention_packed(qkv3, dst, attn_fn=attn_o)
+            sp.attention_packed(qkv3, dst, attn_fn=attn_o, permute=_host_permute)
             ref_b = attn(*[t[:bsz] for t in full])[:, rank * Ls:(rank + 1) * Ls]
             ok4 = ok4 and torch.allclose(dst, ref_b, atol=1e-6)
         q.put((rank, ok1, ok2, ok3 and ok4))

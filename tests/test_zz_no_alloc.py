@@ -19,12 +19,12 @@ pytestmark = pytest.mark.gpu
 QF2_ERR_WORKSPACE = -6
 
 
-def _inputs(dev, B, H, S, seed):
+def _inputs(dev, B, Hq, Hkv, S, seed, dtype=torch.bfloat16):
     g = torch.Generator(device=dev).manual_seed(seed)
-    q = torch.randn(B, H, S, 128, device=dev, generator=g).bfloat16()
-    k = (torch.randn(B, H, S, 128, device=dev, generator=g)
-         + 3.0 * torch.randn(1, H, 1, 128, device=dev, generator=g)).bfloat16()
-    v = torch.randn(B, H, S, 128, device=dev, generator=g).bfloat16()
+    q = torch.randn(B, Hq, S, 128, device=dev, generator=g).to(dtype)
+    k = (torch.randn(B, Hkv, S, 128, device=dev, generator=g)
+         + 3.0 * torch.randn(1, Hkv, 1, 128, device=dev, generator=g)).to(dtype)
+    v = torch.randn(B, Hkv, S, 128, device=dev, generator=g).to(dtype)
     return q, k, v
 
 
@@ -32,38 +32,51 @@ def _strides(t):
     return i64(t.stride(0), t.stride(1), t.stride(2))
 
 
+def _dt(t):
+    return _lib.QF2_BF16 if t.dtype == torch.bfloat16 else _lib.QF2_F16
+
+
 def _with_workspace(lib, q, k, v, sm):
     """The existing entry point, with a caller-provided workspace."""
-    B, H, S, D = q.shape
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
     out = torch.empty_like(q)
-    nbytes = int(lib.qf2_sage_workspace_bytes(B, H, H, B * S, B * S, S, S, D))
+    nbytes = int(lib.qf2_sage_workspace_bytes(B, Hq, Hkv, B * S, B * S, S, S, D))
     raw = torch.empty(nbytes + 1024, dtype=torch.uint8, device=q.device)
     ws = raw[(-raw.data_ptr()) % 1024:][:nbytes]
     st = lib.qf2_sageattn(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(), _strides(v),
-                          out.data_ptr(), _strides(out), B, H, H, S, S, D, sm, _lib.QF2_BF16, ws.data_ptr(), nbytes,
+                          out.data_ptr(), _strides(out), B, Hq, Hkv, S, S, D, sm, _dt(q), ws.data_ptr(), nbytes,
                           stream_ptr(q.device))
     assert st == 0, lib.qf2_status_string(st)
     return out
 
 
 def _noalloc(lib, q, k, v, sm):
-    B, H, S, D = q.shape
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
     out = torch.empty_like(q)
     st = lib.qf2_sageattn_noalloc(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(), _strides(v),
-                                  out.data_ptr(), _strides(out), B, H, H, S, S, D, sm, _lib.QF2_BF16,
+                                  out.data_ptr(), _strides(out), B, Hq, Hkv, S, S, D, sm, _dt(q),
                                   stream_ptr(q.device))
     assert st == 0, lib.qf2_status_string(st)
     return out
 
 
-def test_noalloc_matches_workspace_entry_point_twice(cuda):
+@pytest.mark.parametrize("B,Hq,Hkv,S,seed,dtype", [
+    (1, 24, 24, 4608, 1, torch.bfloat16),   # one Flux-shaped sequence
+    (2, 3, 3, 777, 2, torch.bfloat16),      # ragged length
+    (1, 4, 4, 1000, 3, torch.float16),      # fp16 inputs
+    (2, 6, 2, 777, 4, torch.bfloat16),      # GQA: 3 query heads per kv head
+])
+def test_noalloc_matches_workspace_entry_point_twice(cuda, B, Hq, Hkv, S, seed, dtype):
     lib = _lib.load()
     sm = 1.0 / math.sqrt(128)
-    # two calls in a row: different sizes and inputs, so the second call runs over the
-    # first call's leftovers in the shared static array
-    for B, H, S, seed in ((1, 24, 4608, 1), (2, 3, 777, 2)):
-        q, k, v = _inputs(cuda, B, H, S, seed)
+    q, k, v = _inputs(cuda, B, Hq, Hkv, S, seed, dtype)
+    # two calls in a row: the second runs over the first call's leftovers in the shared
+    # static array (and over the previous case's, when the cases run in one process)
+    for _ in range(2):
         got = _noalloc(lib, q, k, v, sm)
+        assert lib.qf2_sageattn_noalloc_status(stream_ptr(cuda)) == 0   # no bounded wait gave up
         ref = _with_workspace(lib, q, k, v, sm)
         torch.cuda.synchronize()
         assert torch.isfinite(got).all()
@@ -76,7 +89,7 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda):
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
     lib = _lib.load()
-    q, k, v = _inputs(cuda, 2, 24, 4608, 3)   # ~85 MB of codes: more than the 48 MiB array
+    q, k, v = _inputs(cuda, 2, 24, 24, 4608, 3)   # ~85 MB of codes: more than the 48 MiB array
     out = torch.zeros_like(q)
     st = lib.qf2_sageattn_noalloc(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(), _strides(v),
                                   out.data_ptr(), _strides(out), 2, 24, 24, 4608, 4608, 128, 0.088, _lib.QF2_BF16,
