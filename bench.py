@@ -367,7 +367,7 @@ def run_lumina_step(rank: int, world: int, dev, batch: int = 1, warmup: int = 2,
             "batch_per_gpu": batch, "global_batch": batch * world, "samples_per_s": batch * world / sec,
             "tokens": Lc + Li, **r, "parallelism": f"batch-parallel dp{world}" if world > 1 else "single GPU",
             "linears": "INT8 weight-only (per-channel scales), bf16 activations",
-            "attention": "Sage INT8 QK / FP8 PV, GQA 24/8, head_dim 96 zero-padded to 128"}
+            "attention": "Sage INT8 QK / FP8 PV, GQA 24/8, head_dim 96"}
 
 
 def run_ours(args, rank: int, world: int, dev):

@@ -136,7 +136,9 @@ int qf2_softmax_inplace(void* x, int64_t rows, int64_t n, int64_t row_stride, in
  * to FP8 e4m3 per channel (code = e4m3(v * (448/amax)), scale = amax/448);
  * S = Qi8.Ki8^T on tcgen05 kind::i8 into
  * TMEM; online softmax in base 2; P quantized to e4m3 (x448) and P.V on
- * tcgen05 kind::f8f6f4 with fp32 accumulation in TMEM.  D = 128 only.
+ * tcgen05 kind::f8f6f4 with fp32 accumulation in TMEM.  D = 64, 96 or 128 (the
+ * Flux blocks' 128, Lumina's 96): channels past D are zero in the code tiles, QK^T
+ * runs D/32 MMA K-steps, the output has D columns.
  *
  * Dense: q/k/v/out strides = {batch, head, seq} in elements (HND and NHD both
  * expressible); dtype QF2_BF16 or QF2_F16; Hq % Hkv == 0 (GQA).
@@ -164,6 +166,17 @@ int qf2_sageattn_varlen(const void* q, const int64_t* q_strides, const void* k, 
  * offsets[11] = total. */
 int qf2_sage_workspace_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
                               int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t D, int64_t* offsets);
+
+/* Failure injection for tests of the bounded waits (no counterpart in the reference; the
+ * reference has no failure detection).  Process-wide, read by every later Sage attention
+ * launch: wait_limit_us > 0 bounds each of the attention kernel's mbarrier waits to about
+ * that many microseconds (<= 0: the default, about 2 s); skip_kv_tile >= 0 makes the
+ * producer never issue the load of that K/V tile of each CTA, so the waits on it run out,
+ * the kernel records a timeout in the workspace status word (qf2_workspace_status then
+ * returns QF2_ERR_TIMEOUT), lets its issued copies land, drains its MMAs, frees its TMEM
+ * and returns; the output of that call is undefined.  Nothing faults: the context stays
+ * usable.  qf2_sage_fault_injection(0, -1) restores normal operation. */
+int qf2_sage_fault_injection(int64_t wait_limit_us, int skip_kv_tile);
 
 /* Quantization stage alone (same arguments as qf2_sageattn / _varlen; pass
  * cu_seqlens NULL for the dense form).  Leaves codes and scales in the

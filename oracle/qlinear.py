@@ -48,6 +48,9 @@ def quantize_weight_torchao(w: np.ndarray, fmt: str, dtype: str = "f16"):
     if fmt == "int8":
         c = np.clip(np.rint(y), -128, 127)
         return np.where(np.isnan(y), 0, c).astype(np.int8), scale
+    # 0 * inf (a row whose reciprocal scale overflowed) is the positive canonical NaN on the
+    # GPU, where the reference quantizes; the host's default NaN can carry the sign bit
+    y = np.where(np.isnan(y), np.float32(np.nan), y).astype(np.float32)
     return to_e4m3_bits(y), scale
 
 

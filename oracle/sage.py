@@ -101,8 +101,9 @@ def quantize_head(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float):
 def attention_from_codes(qz: dict, rows=None) -> np.ndarray:
     """Step 5-6 on the quantized codes of one head: returns O [Sq, D] float32 (only the
     query rows `rows`, in that order, when given)."""
-    qc = qz["qcodes"].astype(np.int64)
-    kc = qz["kcodes"].astype(np.int64)
+    # integer dot products in float64 (exact: |sum| <= 128 * 127^2 < 2^53), through BLAS
+    qc = qz["qcodes"].astype(np.float64)
+    kc = qz["kcodes"].astype(np.float64)
     Sq, Skv = qc.shape[0], kc.shape[0]
     sq = np.repeat(qz["qscales"], QBLOCK)[:Sq]
     if rows is not None:

@@ -114,6 +114,7 @@ SIGNATURES = {
          c_int64, c_int64, c_float, c_int, c_void_p],
     ),
     "qf2_sageattn_noalloc_status": (c_int, [c_void_p]),
+    "qf2_sage_fault_injection": (c_int, [c_int64, c_int]),
 }
 
 _lib = None

@@ -52,7 +52,7 @@ def sageattn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tensor_layout: s
              is_causal: bool = False, sm_scale: float | None = None, return_lse: bool = False,
              out: torch.Tensor | None = None, **kwargs) -> torch.Tensor:
     """INT8 QK^T / FP8 PV attention.  q [B, Hq, Sq, D] (HND) or [B, Sq, Hq, D] (NHD);
-    k, v with Hkv heads (Hq % Hkv == 0).  D = 128.  Returns a tensor in q's layout;
+    k, v with Hkv heads (Hq % Hkv == 0).  D = 64, 96 or 128.  Returns a tensor in q's layout;
     `out` may be any strided view of that shape (16-byte aligned rows)."""
     if is_causal:
         raise QF2Error("causal masking is not on the DiT path (bidirectional attention only)")

@@ -21,6 +21,7 @@
 #endif
 
 #define QF2_DEV __device__ __forceinline__
+#define QF2_DEV_HOST_INLINE __host__ __device__ __forceinline__
 
 namespace qf2 {
 
@@ -92,14 +93,15 @@ QF2_DEV bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on the phase with the given parity.  Returns false on timeout.
-QF2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait on the phase with the given parity: gives up after `limit` SM clocks.
+// Returns false on timeout.
+QF2_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, long long limit = kWaitClocks) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
-    if (clock64() - t0 > kWaitClocks) return false;
+    if (clock64() - t0 > limit) return false;
   }
 }
 

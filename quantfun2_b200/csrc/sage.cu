@@ -28,7 +28,12 @@ namespace qf2 {
 namespace sage {
 
 constexpr int kTile = 128;          // tokens per tile (MMA M and N)
-constexpr int kHeadDim = 128;       // D
+constexpr int kHeadDim = 128;       // channels of a code tile row (D <= 128 is zero-padded there)
+// head dims the entry points take: D = 64, 96 or 128 channels are read from the inputs,
+// codes of the missing channels are 0 (the TMA box is 128 channels wide over a D-wide
+// tensor, so the loads fill them with zeros), QK^T runs D / 32 MMA K-steps and the
+// epilogue stores D columns
+QF2_DEV_HOST_INLINE bool head_dim_ok(int64_t D) { return D == 64 || D == 96 || D == 128; }
 constexpr int kTileBytes = 16384;   // 128 rows x 128 bytes of 8-bit codes
 constexpr int kQuantBlock = 64;     // tokens per INT8 scale block
 static_assert(kTile == 2 * kQuantBlock, "a Q/K tile holds two INT8 scale blocks");
@@ -692,6 +697,9 @@ struct AttnParams {
   Strides3 os;
   int Hq, Hkv;
   int out_bf16;
+  int D;          // head dim of the inputs and output (64, 96 or 128)
+  long long wait_clocks;  // bound of every mbarrier wait (SM clocks)
+  int skip_kv;    // failure-injection tests only: K/V tile index whose load is never issued (-1: none)
 };
 
 QF2_DEV void store_row_out(void* out, const Strides3& os, int b, int h, int64_t tok, const float* o, bool bf16,
@@ -743,6 +751,9 @@ QF2_DEV float2 ffma2(float2 a, float2 b, float2 c) {
 // grid (ceil(max q tiles / 2) * nsplit, Hq, batch).  With nsplit > 1 a CTA walks the KV
 // tiles [jb, jb + nkt) of its split and writes normalised partial rows (bf16) with their
 // running max and row sum to the workspace; sage_combine_kernel merges the splits.
+// KSTEPS = D / 32: the QK^T MMA K-steps (32 INT8 channels each).  PV keeps N = 128 (the V
+// codes of channels >= D are 0) -- its MMA time is hidden behind the exp-bound softmax.
+template <int KSTEPS>
 __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P) {
   extern __shared__ uint8_t smem_raw[];
   const int nsplit = P.ws.nsplit;
@@ -811,7 +822,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   // warp-uniform bounded wait: every lane agrees on the outcome, so .sync.aligned
   // instructions and elected issue that follow always see a converged warp
   auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
-    const bool w = mbar_wait(bar, parity) && (*abort_flag == 0);
+    const bool w = mbar_wait(bar, parity, P.wait_clocks) && (*abort_flag == 0);
     return __all_sync(0xffffffffu, w);
   };
 
@@ -830,7 +841,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       for (int j = 0; j < nkt; ++j) {
         const int s = j % kStages, r = j / kStages;
         if (!wwait(bar_kv_empty + s, (r & 1) ^ 1)) { if (lane == 0) fail(kDevTimeoutProducer); break; }
-        if (lane == 0) {
+        if (lane == 0 && jb + j != P.skip_kv) {
           mbar_arrive_expect_tx(bar_kv_full + s, 2 * kTileBytes);
           uint8_t* dK = sKV + s * 2 * kTileBytes;
           bulk_g2s(dK, ws.kc + (kslot0 + j) * kTileBytes, kTileBytes, bar_kv_full + s);
@@ -841,9 +852,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       }
       if (*abort_flag && lane == 0) {
         // let the copies already issued land before the CTA's shared memory goes away
-        mbar_wait(bar_q, 0);
+        // (a load that was never issued only costs its bounded wait)
+        mbar_wait(bar_q, 0, P.wait_clocks);
         for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
-          mbar_wait(bar_kv_full + (j % kStages), (j / kStages) & 1);
+          mbar_wait(bar_kv_full + (j % kStages), (j / kStages) & 1, P.wait_clocks);
       }
     } else if (warp == 1 && nkt > 0) {
       // ------------------------------------------------------------ MMA --
@@ -888,7 +900,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
           const uint64_t dQ = dQ0 + (uint64_t)t * kTileStep;
           if (lane == 0) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + t * 128, dQ + 2 * kk, dK + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < KSTEPS; ++kk)
+              mma_i8(tmem + t * 128, dQ + 2 * kk, dK + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
             tc_commit(bar_s_full + t);
           }
           __syncwarp();
@@ -1037,7 +1050,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       }
       const float inv_l = (ok && l_run > 0.f) ? 1.0f / l_run : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < KSTEPS; ++c) {
         uint32_t o[32];
         if (ok && nkt > 0) {
           tmem_ld32(tO + c * 32, o);
@@ -1081,6 +1094,7 @@ __global__ void __launch_bounds__(256) sage_combine_kernel(AttnParams P) {
   const int64_t r_tok = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
   if (r_tok >= sq.len) return;
   const int c8 = threadIdx.x & 15;
+  if (c8 * 8 >= P.D) return;
   const int64_t prow = ((int64_t)h * ws.tq + sq.tile0) * kTile + r_tok;
   float m[kMaxSplits], w[kMaxSplits];
   float M = -INFINITY;
@@ -1132,6 +1146,11 @@ struct Layout {
 };
 
 static int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// Failure-injection settings of the attention launches (qf2_sage_fault_injection): the
+// bound of every mbarrier wait, and a K/V tile whose load the producer never issues.
+static std::atomic<long long> g_attn_wait_clocks{kWaitClocks};
+static std::atomic<int> g_attn_skip_kv{-1};
 
 // KV splits of the attention for a dense problem whose CTAs (pairs of Q tiles per head)
 // fill few waves: each split walks a contiguous part of the K/V tiles and leaves
@@ -1232,7 +1251,7 @@ struct Args {
 static int validate(const Args& a, bool need_out) {
   if (!a.q || !a.k || !a.v || !a.workspace || (need_out && !a.out)) return QF2_ERR_ARG;
   if (a.dtype != QF2_BF16 && a.dtype != QF2_F16) return QF2_ERR_DTYPE;
-  if (a.D != kHeadDim) return QF2_ERR_SHAPE;
+  if (!head_dim_ok(a.D)) return QF2_ERR_SHAPE;
   if (a.Hq <= 0 || a.Hkv <= 0 || a.Hq % a.Hkv != 0 || a.batch <= 0) return QF2_ERR_SHAPE;
   if (a.max_q < 0 || a.max_k < 0 || a.max_k > (int64_t)kMaxKvTiles * kTile) return QF2_ERR_SHAPE;
   if (a.Hq > 65535 || a.Hq + 2 * a.Hkv > 65535 || a.batch > 65535) return QF2_ERR_SHAPE;
@@ -1252,13 +1271,14 @@ static int validate(const Args& a, bool need_out) {
   return QF2_OK;
 }
 
-// Tensor map over q, k or v as {channels, tokens, heads, batch} with a 128 x 128 box and
-// no swizzle (the consumers read whole 256-byte rows).  Varlen inputs have one batch
-// entry whose stride is only a placeholder.
+// Tensor map over q, k or v as {channels (D), tokens, heads, batch} with a 128 x 128 box
+// and no swizzle (the consumers read whole 256-byte rows; for D < 128 the box's channels
+// past D lie outside the tensor and arrive as zeros).  Varlen inputs have one batch entry
+// whose stride is only a placeholder.
 static bool make_prep_map(CUtensorMap* m, const void* base, const Strides3& st, int64_t tokens, int64_t H,
-                          int64_t batch_ext, int dtype) {
+                          int64_t batch_ext, int dtype, int64_t D) {
   const uint64_t esz = 2;
-  const uint64_t dims[4] = {(uint64_t)kHeadDim, (uint64_t)tokens, (uint64_t)H, (uint64_t)batch_ext};
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)tokens, (uint64_t)H, (uint64_t)batch_ext};
   const uint64_t sb = st.b != 0 ? (uint64_t)st.b * esz : (uint64_t)st.s * esz * (uint64_t)tokens;
   const uint64_t strides[3] = {(uint64_t)st.s * esz, (uint64_t)st.h * esz, sb};
   const uint32_t box[4] = {(uint32_t)kHeadDim, (uint32_t)kTile, 1, 1};
@@ -1286,9 +1306,9 @@ static int launch_quant(const Args& a) {
   memset(&mq, 0, sizeof(mq));
   memset(&mk, 0, sizeof(mk));
   memset(&mv, 0, sizeof(mv));
-  if (A.mtq > 0 && !make_prep_map(&mq, a.q, a.qs, tok_q, a.Hq, bext, a.dtype)) return QF2_ERR_ALIGN;
-  if (mtk > 0 && (!make_prep_map(&mk, a.k, a.ks, tok_k, a.Hkv, bext, a.dtype) ||
-                  !make_prep_map(&mv, a.v, a.vs, tok_k, a.Hkv, bext, a.dtype)))
+  if (A.mtq > 0 && !make_prep_map(&mq, a.q, a.qs, tok_q, a.Hq, bext, a.dtype, a.D)) return QF2_ERR_ALIGN;
+  if (mtk > 0 && (!make_prep_map(&mk, a.k, a.ks, tok_k, a.Hkv, bext, a.dtype, a.D) ||
+                  !make_prep_map(&mv, a.v, a.vs, tok_k, a.Hkv, bext, a.dtype, a.D)))
     return QF2_ERR_ALIGN;
   int sms = 0;
   QF2_CUDA_CHECK(qf2_sm_count(&sms));
@@ -1337,12 +1357,16 @@ static int launch_attn(const Args& a) {
   P.os = a.os;
   P.Hq = (int)a.Hq; P.Hkv = (int)a.Hkv;
   P.out_bf16 = a.dtype == QF2_BF16;
+  P.D = (int)a.D;
+  P.wait_clocks = g_attn_wait_clocks.load(std::memory_order_relaxed);
+  P.skip_kv = g_attn_skip_kv.load(std::memory_order_relaxed);
   const int64_t mqt = (a.max_q + kTile - 1) / kTile;
   if (mqt == 0) return QF2_OK;
-  static std::atomic<uint64_t> attr_done{0};
-  QF2_CUDA_CHECK(qf2_set_smem_once(sage_attn_kernel, AttnSmem::alloc, &attr_done));
-  sage_attn_kernel<<<dim3((unsigned)(((mqt + 1) / 2) * P.ws.nsplit), (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads,
-                     AttnSmem::alloc, a.stream>>>(P);
+  static std::atomic<uint64_t> attr_done[3];
+  auto kern = a.D == 64 ? sage_attn_kernel<2> : a.D == 96 ? sage_attn_kernel<3> : sage_attn_kernel<4>;
+  QF2_CUDA_CHECK(qf2_set_smem_once(kern, AttnSmem::alloc, &attr_done[a.D / 32 - 2]));
+  kern<<<dim3((unsigned)(((mqt + 1) / 2) * P.ws.nsplit), (unsigned)a.Hq, (unsigned)a.batch), kAttnThreads,
+         AttnSmem::alloc, a.stream>>>(P);
   QF2_LAUNCH_CHECK();
   if (P.ws.nsplit > 1) {
     sage_combine_kernel<<<dim3((unsigned)(mqt * (kTile / 16)), (unsigned)a.Hq, (unsigned)a.batch), 256, 0, a.stream>>>(P);
@@ -1378,16 +1402,24 @@ static Strides3 s2v(const int64_t* p) { return p ? Strides3{0, p[1], p[0]} : Str
 
 extern "C" int64_t qf2_sage_workspace_bytes(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
                                             int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t D) {
-  if (D != kHeadDim) return (int64_t)QF2_ERR_SHAPE;
+  if (!head_dim_ok(D)) return (int64_t)QF2_ERR_SHAPE;
   // dense callers pass total = batch * S; the varlen capacity bound covers both forms
   const Layout L = make_layout(batch, Hq, Hkv, total_q, total_k, max_seqlen_q, max_seqlen_k, true);
   const Layout Ld = make_layout(batch, Hq, Hkv, total_q, total_k, max_seqlen_q, max_seqlen_k, false);
   return std::max(L.off[11], Ld.off[11]);
 }
 
+extern "C" int qf2_sage_fault_injection(int64_t wait_limit_us, int skip_kv_tile) {
+  // SM clocks per microsecond: the B200's 1965 MHz maximum rounded up, so the bound is at
+  // least the requested time
+  g_attn_wait_clocks.store(wait_limit_us > 0 ? wait_limit_us * 2000 : qf2::kWaitClocks, std::memory_order_relaxed);
+  g_attn_skip_kv.store(skip_kv_tile >= 0 ? skip_kv_tile : -1, std::memory_order_relaxed);
+  return QF2_OK;
+}
+
 extern "C" int qf2_sage_workspace_layout(int64_t batch, int64_t Hq, int64_t Hkv, int64_t total_q, int64_t total_k,
                                          int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t D, int64_t* offsets) {
-  if (D != kHeadDim) return QF2_ERR_SHAPE;
+  if (!head_dim_ok(D)) return QF2_ERR_SHAPE;
   if (!offsets) return QF2_ERR_ARG;
   // total_q < 0 selects the dense layout (batch * ceil(S / 128) tiles per head)
   const bool varlen = total_q >= 0;
@@ -1511,7 +1543,7 @@ extern "C" int qf2_sageattn_noalloc(const void* q, const int64_t* q_strides, con
                                     const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides,
                                     int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
                                     float sm_scale, int dtype, qf2_stream_t stream) {
-  if (D != kHeadDim) return QF2_ERR_SHAPE;
+  if (!head_dim_ok(D)) return QF2_ERR_SHAPE;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq < 0 || Skv < 0) return QF2_ERR_SHAPE;
   const int64_t usable = kNoAllocScratchBytes - 1024;
   const Layout L = make_layout(B, Hq, Hkv, B * Sq, B * Skv, Sq, Skv, false);

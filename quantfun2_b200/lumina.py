@@ -9,9 +9,8 @@ parameter.  Weights are random; every linear is an INT8 weight-only QLinear (the
 path of src/quant.py:209-224, 323-327).
 
 Per block (B*L rows, dim columns):
-  qkv GEMM -> fused q/k RMSNorm + RoPE (head_dim 96 zero-padded to 128 for the attention
-  kernel) -> Sage attention (GQA 24/8) -> wo GEMM (K = 24 x 128, zero weight columns on
-  the padding) -> x += tanh(gate) * RMSNorm(.) and the next norm-modulate in one pass ->
+  qkv GEMM -> fused q/k RMSNorm + RoPE -> Sage attention at head_dim 96 (GQA 24/8) -> wo
+  GEMM -> x += tanh(gate) * RMSNorm(.) and the next norm-modulate in one pass ->
   w1/w3 GEMM with the SwiGLU epilogue -> w2 GEMM -> the same fused residual pass producing
   the next block's input.
 
@@ -64,11 +63,11 @@ class LuminaBlock(nn.Module):
     (modulation=True), or plain residuals (context refiner, modulation=False)."""
 
     def __init__(self, dim, heads, kv_heads, ffn_hidden, mode, device, gen=None, modulation=True, norm_eps=1e-5,
-                 hd_pad=128):
+                 hd_pad=None):
         super().__init__()
         self.dim, self.heads, self.kv_heads = dim, heads, kv_heads
         self.hd = dim // heads
-        self.hd_pad = hd_pad
+        self.hd_pad = hd_pad or self.hd   # attention head width (wider only to test zero padding)
         self.ffn = ffn_hidden
         self.modulation = modulation
         self.eps = norm_eps

@@ -31,10 +31,11 @@ def test_argument_validation_without_device():
                            1e-6, 0, None) == -1
     assert lib.qf2_softmax_inplace(None, 1, 1, 1, 0, None) == -8
     assert lib.qf2_rope_apply(None, None, 1, s, s, None, None, 0, None, None, None, s, 1, 1, 2, 0, 0, None) == -8
-    assert lib.qf2_sage_workspace_bytes(1, 24, 24, 4608, 4608, 4608, 4608, 64) == -1   # D must be 128
+    assert lib.qf2_sage_workspace_bytes(1, 24, 24, 4608, 4608, 4608, 4608, 80) == -1   # D in {64, 96, 128}
+    assert lib.qf2_sage_workspace_bytes(1, 24, 24, 4608, 4608, 4608, 4608, 96) > 0
     p = ctypes.c_void_p(1024)
-    # D != 128 and bad dtype are rejected before any launch
-    assert lib.qf2_sageattn(p, s, p, s, p, s, p, s, 1, 2, 2, 64, 64, 64, 0.1, 2, p, 1 << 30, None) == -1
+    # an unsupported D and a bad dtype are rejected before any launch
+    assert lib.qf2_sageattn(p, s, p, s, p, s, p, s, 1, 2, 2, 64, 64, 48, 0.1, 2, p, 1 << 30, None) == -1
     assert lib.qf2_sageattn(p, s, p, s, p, s, p, s, 1, 2, 2, 64, 64, 128, 0.1, 0, p, 1 << 30, None) == -2
     assert lib.qf2_sageattn(p, s, p, s, p, s, p, s, 1, 3, 2, 64, 64, 128, 0.1, 2, p, 1 << 30, None) == -1  # GQA ratio
     assert lib.qf2_sageattn(p, s, p, s, p, s, p, s, 1, 2, 2, 64, 64, 128, 0.1, 2, p, 16, None) == -6        # workspace

@@ -18,7 +18,7 @@ from tests.golden_cases import jattn_case
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("tag", ["d128"])
+@pytest.mark.parametrize("tag", ["d128", "d96"])
 def test_b200_joint_attention_block_vs_reference_golden(cuda, tag):
     from quantfun2_b200.attention import sageattn
     from quantfun2_b200.kernels import qkv_norm_rope

@@ -12,11 +12,11 @@ from tests.sage_workspace import decode
 pytestmark = pytest.mark.gpu
 
 
-def make_qkv(B, Hq, Hkv, Sq, Skv, seed=0, outlier=3.0, dtype=torch.bfloat16):
+def make_qkv(B, Hq, Hkv, Sq, Skv, seed=0, outlier=3.0, dtype=torch.bfloat16, D=128):
     g = torch.Generator().manual_seed(seed)
-    q = torch.randn(B, Hq, Sq, 128, generator=g)
-    k = torch.randn(B, Hkv, Skv, 128, generator=g) + outlier * torch.randn(1, Hkv, 1, 128, generator=g)
-    v = torch.randn(B, Hkv, Skv, 128, generator=g)
+    q = torch.randn(B, Hq, Sq, D, generator=g)
+    k = torch.randn(B, Hkv, Skv, D, generator=g) + outlier * torch.randn(1, Hkv, 1, D, generator=g)
+    v = torch.randn(B, Hkv, Skv, D, generator=g)
     return q.to(dtype), k.to(dtype), v.to(dtype)
 
 
@@ -27,20 +27,26 @@ def cosine(a, b):
 
 
 def check_codes(dec, q, k, v, B, Hq, Hkv, sm_scale):
+    """GPU codes (128-channel tile rows) against the oracle on D-channel inputs: channels
+    past D must be zero codes (K mean 0, V scale 1)."""
     for b in range(B):
         for h in range(Hq):
+            D = q[b][h].shape[-1]
             rq, rs = sage.quantize_q(q[b][h], sm_scale)
             gq = dec[("q", b, h)]
-            assert np.array_equal(gq["codes"], rq), (b, h)
+            assert np.array_equal(gq["codes"][:, :D], rq), (b, h)
+            assert not gq["codes"][:, D:].any(), (b, h)
             assert np.array_equal(gq["scales"], rs), (b, h)
         for h in range(Hkv):
+            D = k[b][h].shape[-1]
             ref = sage.quantize_kv(k[b][h], v[b][h])
             gk = dec[("k", b, h)]
-            assert np.array_equal(gk["kmean"], ref["kmean"]), (b, h)
-            assert np.array_equal(gk["codes"], ref["kcodes"]), (b, h)
+            assert np.array_equal(gk["kmean"][:D], ref["kmean"]), (b, h)
+            assert np.array_equal(gk["codes"][:, :D], ref["kcodes"]), (b, h)
             assert np.array_equal(gk["scales"], ref["kscales"]), (b, h)
-            assert np.array_equal(gk["vscale"], ref["vscale"]), (b, h)
-            assert np.array_equal(gk["v8"], ref["v8"]), (b, h)
+            assert np.array_equal(gk["vscale"][:D], ref["vscale"]), (b, h)
+            assert np.array_equal(gk["v8"][:, :D], ref["v8"]), (b, h)
+            assert not gk["codes"][:, D:].any() and not gk["v8"][:, D:].any() and not gk["kmean"][D:].any()
 
 
 @pytest.mark.parametrize("layout", ["HND", "NHD"])
@@ -78,18 +84,18 @@ def test_sage_quant_codes_bit_exact_flux_config(cuda):
 
 def test_sage_quant_codes_bit_exact_lumina_varlen(cuda):
     """The Lumina-shaped batch: 8 packed sequences of 4352 tokens (4096 image + 256 caption),
-    24 query / 8 kv heads (GQA), varlen form; every head."""
+    24 query / 8 kv heads (GQA) of head_dim 96, varlen form; every head."""
     from quantfun2_b200.attention import sage_quantize
 
     lens = [4352] * 8
-    Hq, Hkv = 24, 8
+    Hq, Hkv, D = 24, 8, 96
     g = torch.Generator().manual_seed(8)
     T = sum(lens)
-    q = torch.randn(T, Hq, 128, generator=g).bfloat16()
-    k = (torch.randn(T, Hkv, 128, generator=g) + 3 * torch.randn(1, Hkv, 128, generator=g)).bfloat16()
-    v = torch.randn(T, Hkv, 128, generator=g).bfloat16()
+    q = torch.randn(T, Hq, D, generator=g).bfloat16()
+    k = (torch.randn(T, Hkv, D, generator=g) + 3 * torch.randn(1, Hkv, D, generator=g)).bfloat16()
+    v = torch.randn(T, Hkv, D, generator=g).bfloat16()
     cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
-    sm = 1.0 / math.sqrt(128)
+    sm = 1.0 / math.sqrt(D)
     ws, offs = sage_quantize(q.to(cuda), k.to(cuda), v.to(cuda), sm, cu_seqlens_q=cu.to(cuda),
                              cu_seqlens_k=cu.to(cuda), max_seqlen_q=max(lens), max_seqlen_k=max(lens))
     torch.cuda.synchronize()
@@ -123,12 +129,42 @@ def test_sage_quant_codes_varlen_bit_exact(cuda):
     check_codes(dec, qs, ks, vs, len(lens), Hq, Hkv, sm)
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 2, 256, 256), (2, 4, 2, 200, 333), (1, 2, 1, 1000, 77)])
+@pytest.mark.parametrize("layout", ["HND", "NHD"])
+@pytest.mark.parametrize("D", [64, 96])
+def test_sage_quant_codes_bit_exact_small_head_dims(cuda, layout, D):
+    from quantfun2_b200.attention import sage_quantize
+
+    B, Hq, Hkv, Sq, Skv = 2, 6, 2, 333, 200
+    q, k, v = make_qkv(B, Hq, Hkv, Sq, Skv, seed=D, D=D)
+    sm = 1.0 / math.sqrt(D)
+    tr = (lambda t: t) if layout == "HND" else (lambda t: t.transpose(1, 2).contiguous())
+    ws, offs = sage_quantize(tr(q).to(cuda), tr(k).to(cuda), tr(v).to(cuda), sm, tensor_layout=layout)
+    torch.cuda.synchronize()
+    dec = decode(ws.cpu().numpy(), offs, B, Hq, Hkv, [Sq] * B, [Skv] * B,
+                 [b * ((Sq + 127) // 128) for b in range(B)], [b * ((Skv + 127) // 128) for b in range(B)])
+    check_codes(dec, q.float().numpy(), k.float().numpy(), v.float().numpy(), B, Hq, Hkv, sm)
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 2, 256, 256, 128), (2, 4, 2, 200, 333, 128), (1, 2, 1, 1000, 77, 128),
+                                   (2, 6, 2, 300, 300, 96), (1, 3, 3, 500, 257, 64), (1, 24, 8, 4352, 4352, 96)])
 def test_sage_attention_matches_oracle(cuda, shape):
     from quantfun2_b200.attention import sageattn
 
-    B, Hq, Hkv, Sq, Skv = shape
-    q, k, v = make_qkv(B, Hq, Hkv, Sq, Skv, seed=7)
+    B, Hq, Hkv, Sq, Skv, D = shape
+    q, k, v = make_qkv(B, Hq, Hkv, Sq, Skv, seed=7, D=D)
+    if Sq > 2000:   # the Lumina shape: check a sample of heads against the CPU oracle
+        o = sageattn(q.to(cuda), k.to(cuda), v.to(cuda)).float().cpu().numpy()[:, ::5]
+        q, k, v = q[:, ::5], k[:, [h // 3 for h in range(0, 24, 5)]], v[:, [h // 3 for h in range(0, 24, 5)]]
+        o_ref_q = q.float().numpy()
+        qf, kf, vf = o_ref_q, k.float().numpy(), v.float().numpy()
+        ro = np.stack([np.stack([sage.attention_from_codes(sage.quantize_head(qf[b, i], kf[b, i], vf[b, i],
+                                                                              1 / math.sqrt(D)))
+                                 for i in range(qf.shape[1])]) for b in range(B)])
+        rs = sage.sdpa_reference(qf, kf, vf)
+        c_or, c_sd = cosine(o, ro), cosine(o, rs)
+        print(f"D={D} lumina shape: cos(oracle)={c_or:.6f} cos(sdpa)={c_sd:.6f}")
+        assert c_or >= 0.9995 and c_sd >= 0.998
+        return
     o = sageattn(q.to(cuda), k.to(cuda), v.to(cuda)).float().cpu().numpy()
     qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
     ro = sage.sageattn(qf, kf, vf)

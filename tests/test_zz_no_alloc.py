@@ -17,6 +17,7 @@ from quantfun2_b200._lib import i64, stream_ptr
 pytestmark = pytest.mark.gpu
 
 QF2_ERR_WORKSPACE = -6
+QF2_ERR_TIMEOUT = -4
 
 
 def _inputs(dev, B, Hq, Hkv, S, seed, dtype=torch.bfloat16):
@@ -97,3 +98,23 @@ def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
     assert st == QF2_ERR_WORKSPACE
     torch.cuda.synchronize()
     assert not out.any()   # nothing was launched
+
+
+def test_noalloc_status_reports_a_timed_out_call(cuda):
+    """A caller without a workspace pointer still learns that a bounded device wait gave
+    up: the test makes one (qf2_sage_fault_injection: ~2 ms waits, one K/V load never
+    issued), qf2_sageattn_noalloc_status reports it once and clears it, and the next
+    normal call matches the workspace entry point again."""
+    lib = _lib.load()
+    sm = 1.0 / math.sqrt(128)
+    q, k, v = _inputs(cuda, 1, 2, 2, 1024, 7)
+    assert lib.qf2_sage_fault_injection(2000, 2) == 0
+    try:
+        _noalloc(lib, q, k, v, sm)
+        assert lib.qf2_sageattn_noalloc_status(stream_ptr(cuda)) == QF2_ERR_TIMEOUT
+        assert lib.qf2_sageattn_noalloc_status(stream_ptr(cuda)) == 0
+    finally:
+        lib.qf2_sage_fault_injection(0, -1)
+    got = _noalloc(lib, q, k, v, sm)
+    assert lib.qf2_sageattn_noalloc_status(stream_ptr(cuda)) == 0
+    assert torch.equal(got, _with_workspace(lib, q, k, v, sm))
