@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--no-flux", action="store_true")
     p.add_argument("--no-lumina", action="store_true")
     p.add_argument("--no-blocksparse", action="store_true")
+    p.add_argument("--no-bandwidth", action="store_true", help="skip the bandwidth-kernel measurements")
+    p.add_argument("--no-cpu-baselines", action="store_true", help="skip the CPU baselines of configs 1, 3, 4, 5")
     p.add_argument("--flux-sides", default="64,128",
                    help="image-token grid sides of the Flux step (64 -> 4608 tokens, 128 -> 16,896)")
     p.add_argument("--profile", action="store_true",
@@ -158,29 +160,165 @@ def fp8_gemm_peak_tflops(dev) -> float | None:
 
 # --------------------------------------------------------------- reference --
 def run_reference(args, rank: int, world: int):
+    """The reference's CPU path for this workload: its torch-eager SDPA branch
+    (src/models/flux/attn.py:42-43), fp32, on the full B x H x S x D problem each step,
+    on all host cores.  Rank 0 alone runs it; the other ranks exit."""
     if rank != 0:
         return
-    from oracle.baseline import sdpa_cpu_sample
+    from oracle.baseline import sdpa_cpu
 
-    heads = 2
     for _ in range(max(args.warmup, 0)):
-        sdpa_cpu_sample(heads=heads, S=S, D=D)
+        sdpa_cpu(B, H, S, D)
     tot_t, tot_f, threads = 0.0, 0.0, 1
     for _ in range(args.steps):
-        dt, fl, threads = sdpa_cpu_sample(heads=heads, S=S, D=D)
+        dt, fl, threads = sdpa_cpu(B, H, S, D)
         tot_t += dt
         tot_f += fl
     tflops = tot_f / tot_t / 1e12
-    sample = f"{heads} heads x {S} tokens x D={D}, fp32 torch SDPA on the host (src/models/flux/attn.py:42-43)"
+    sample = (f"the full workload each step: B={B} x {H} heads x {S} tokens x D={D}, fp32 torch SDPA "
+              f"on the host (src/models/flux/attn.py:42-43)")
     line = {
         "metric": METRIC, "value": tflops, "unit": "TFLOPS", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": tot_t / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD + " (CPU sample: " + sample + ")"},
+        "config": {"workload": WORKLOAD, "same_config": True},
         "cpu_baseline": {"value": tflops, "unit": "TFLOPS", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": tflops, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_cpu_baselines() -> dict:
+    """CPU baselines of the other benchmark configurations (torch fp32 restatements of the
+    reference's eager paths on all host cores; oracle/baseline.py)."""
+    from oracle import baseline as cb
+    from quantfun2_b200.dit import flux_step_flops
+    from quantfun2_b200.lumina import lumina_step_flops
+
+    out = {}
+    dt, fl, thr = cb.joint_attention_cpu()
+    out["config1_joint_attention_block"] = {
+        "ms": dt * 1e3, "tflops": fl / dt / 1e12, "cores": thr, "kind": "port",
+        "what": "JointAttention fp32, B=1, S=1024, dim 3072 (24 x 128), RMSNorm q/k, 2-D RoPE, SDPA, best of 3"}
+    dt, fl, thr = cb.blocktopk_cpu()
+    out["config3_block_topk"] = {
+        "ms": dt * 1e3, "tflops": fl / dt / 1e12, "cores": thr, "kind": "port",
+        "what": "block top-k, B=1 H=24 S=16384 D=128, keep 16/128 blocks, fp32 (pool, scores, top-k, "
+                "softmax over kept blocks)"}
+    dt, fl, thr = cb.lumina_block_cpu()
+    step = lumina_step_flops(1)
+    out["config4_lumina_step"] = {
+        "ms": dt * step / fl * 1e3, "block_ms": dt * 1e3, "cores": thr, "kind": "port",
+        "what": "one Lumina 2B JointTransformerBlock fp32 at 4352 tokens timed, step extrapolated by FLOPs "
+                f"({step:.3e} / {fl:.3e})"}
+    td, ts, thr = cb.flux_blocks_cpu()
+    out["config5_flux_step_4608"] = {
+        "ms": (19 * td + 38 * ts) * 1e3, "double_block_ms": td * 1e3, "single_block_ms": ts * 1e3,
+        "tflops": flux_step_flops(4608) / (19 * td + 38 * ts) / 1e12, "cores": thr, "kind": "port",
+        "what": "one double and one single Flux block fp32 at 4608 tokens timed, step = 19 x double + 38 x single "
+                "(extrapolation)"}
+    return out
+
+
+def _bw_time(fn, iters: int = 10) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / iters
+
+
+def run_bandwidth_kernels(dev, hbm_gbs: float, prep_s: float) -> dict:
+    """Achieved HBM bandwidth of each bandwidth-bound kernel: algorithmic bytes (each input
+    read once, each output written once) / CUDA-event time, on inputs of 0.2-1.2 GB (above
+    the 126 MB L2) in the DiT steps' row shapes."""
+    from quantfun2_b200 import kernels as K
+    from quantfun2_b200 import quant as Q
+    from quantfun2_b200.attention import block_topk_select
+    from quantfun2_b200.dit import flux_position_ids, rope_freqs
+
+    res = {}
+
+    def add(name, kernel, t, nbytes, shape):
+        res[name] = {"kernel": kernel, "ms": t * 1e3, "bytes": nbytes, "gbs": nbytes / t / 1e9,
+                     "frac_hbm": nbytes / t / 1e9 / hbm_gbs, "shape": shape}
+
+    g = torch.Generator(device=dev).manual_seed(5)
+    bf = torch.bfloat16
+    add("sage_quantization", "sage_prep_kernel (+ 32-byte memset)", prep_s, 3 * B * H * S * D * 3,
+        f"B={B} H={H} S={S} D={D}: q, k, v read once (2 B/elem), codes written (1 B/elem); timed in the main loop")
+    # RoPE in place on q and k [8, 4608, 24, 128]
+    Bq, L = 8, 4608
+    q = torch.randn(Bq, L, 24, 128, device=dev, generator=g).to(bf)
+    k = torch.randn(Bq, L, 24, 128, device=dev, generator=g).to(bf)
+    fr = rope_freqs(flux_position_ids(Bq, 512, 64, 64, dev), (16, 56, 56))
+    t = _bw_time(lambda: K.rope_apply_(q, k, fr, fp16_trig=False))
+    add("rope", "rope_kernel", t, 4 * q.numel() * 2 + fr.numel() * 8, "q, k [8, 4608, 24, 128] bf16, in place")
+    # fused q/k RMSNorm + RoPE on the QKV projection [4, 4608, 3 x 3072]
+    qkv = torch.randn(4, L, 3 * 3072, device=dev, generator=g).to(bf)
+    qo = torch.empty(4, L, 24, 128, device=dev, dtype=bf)
+    ko, vo = torch.empty_like(qo), torch.empty_like(qo)
+    w1 = torch.ones(128, device=dev, dtype=bf)
+    t = _bw_time(lambda: K.qkv_norm_rope(qkv, 24, w1, w1, fr[:4], qo, ko, vo))
+    add("qkv_norm_rope", "qkv_norm_rope_kernel", t, 2 * qkv.numel() * 2 + fr[:4].numel() * 8,
+        "qkv [4, 4608, 9216] bf16 -> q, k, v")
+    del q, k, qkv, qo, ko, vo
+    # RMSNorm over rows of 2304 (eager and fused rounding)
+    x = torch.randn(131072, 2304, device=dev, generator=g).to(bf)
+    w = torch.ones(2304, device=dev, dtype=bf)
+    t = _bw_time(lambda: K.rmsnorm_apply(x, w, 1e-5))
+    add("rmsnorm_eager", "rmsnorm kernel (eager rounding)", t, 2 * x.numel() * 2, "x [131072, 2304] bf16")
+    t = _bw_time(lambda: K.rmsnorm_apply(x, w, 1e-5, fused=True))
+    add("rmsnorm_fused", "rmsnorm kernel (fused rounding)", t, 2 * x.numel() * 2, "x [131072, 2304] bf16")
+    # Lumina gated residual + next norm-modulate: reads y, x; writes x, h
+    M = 65536
+    xr, yr, hr = (torch.randn(M, 2304, device=dev, generator=g).to(bf) for _ in range(3))
+    gate = torch.randn(1, 2304, device=dev, generator=g).to(bf)
+    t = _bw_time(lambda: K.rms_gate_residual(xr, yr, hr, M, w, 1e-5, gate, True, w, 1e-5, gate))
+    add("rms_gate_residual", "gate_residual_kernel", t, 4 * xr.numel() * 2, "x, y, h [65536, 2304] bf16")
+    del x, xr, yr, hr
+    # softmax rows of 16384
+    sm = torch.randn(16384, 16384, device=dev, generator=g).to(bf)
+    t = _bw_time(lambda: K.inplace_softmax(sm))
+    add("softmax", "softmax_rows_kernel", t, 2 * sm.numel() * 2, "x [16384, 16384] bf16, in place")
+    del sm
+    # adaLN LayerNorm + modulate (+ e4m3 quantizer), activation quantizer, code expansion
+    xa = torch.randn(36864, 3072, device=dev, generator=g).to(bf)
+    mod = torch.randn(1, 6 * 3072, device=dev, generator=g).to(bf)
+    sh, sc = mod[:, :3072], mod[:, 3072:6144]
+    t = _bw_time(lambda: Q.ln_modulate(xa, sh, sc, 36864, "bf16"))
+    add("ln_modulate_bf16", "ln_modulate_warp_kernel", t, 2 * xa.numel() * 2, "x [36864, 3072] bf16 -> bf16")
+    t = _bw_time(lambda: Q.ln_modulate(xa, sh, sc, 36864, "e4m3"))
+    add("ln_modulate_e4m3", "ln_modulate_warp_kernel (e4m3 out)", t, xa.numel() * 3 + 36864 * 4,
+        "x [36864, 3072] bf16 -> e4m3 codes + row scales")
+    t = _bw_time(lambda: Q.quantize_rows(xa, "e4m3"))
+    add("quantize_rows_e4m3", "quantize_rows_vec_kernel", t, xa.numel() * 3 + 36864 * 4,
+        "x [36864, 3072] bf16 -> e4m3 codes + row scales")
+    codes, _ = Q.quantize_rows(xa, "int8")
+    t = _bw_time(lambda: Q.codes_to_bf16(codes, "int8"))
+    add("codes_to_bf16", "codes_to_bf16_vec_kernel", t, codes.numel() * 3, "int8 [36864, 3072] -> bf16")
+    # chunk permutation copy (the Ulysses layout change): [P=8, 3, 1, L, 3 heads x 128] bf16
+    src = torch.randn(8 * 3 * 4 * 4608 * 3 * 128, device=dev, generator=g).to(bf)
+    dst = torch.empty_like(src)
+    hb = 3 * 128 * 2
+    t = _bw_time(lambda: K.copy_chunks(dst, src, hb, (8, 3, 4 * 4608), (hb, 8 * hb, 3 * 8 * hb),
+                                       (3 * 4 * 4608 * hb, 4 * 4608 * hb, hb)))
+    add("copy_chunks", "copy_chunks_kernel", t, 2 * src.numel() * 2, "8 x 3 x 18432 chunks of 768 B (170 MB)")
+    del xa, codes, src, dst
+    # block top-k selection: pooling reads Q and K once
+    qs = torch.randn(1, 24, 16384, 128, device=dev, generator=g).to(bf)
+    ks = torch.randn(1, 24, 16384, 128, device=dev, generator=g).to(bf)
+    t = _bw_time(lambda: block_topk_select(qs, ks, 16))
+    add("blocktopk_select", "blocktopk_pool_kernel + blocktopk_select_kernel", t, 2 * qs.numel() * 2,
+        "q, k [1, 24, 16384, 128] bf16 read once (pooling); select on 128 x 128 pooled scores")
+    del qs, ks
+    torch.cuda.empty_cache()
+    return res
 
 
 # --------------------------------------------------------------------- ours --
@@ -192,19 +330,25 @@ def make_inputs(dev, seed):
     return q.bfloat16(), k.bfloat16(), v.bfloat16()
 
 
-def run_flux_step(rank: int, world: int, dev, sides=(64, 128), warmup: int = 2, steps: int = 5) -> dict:
+def run_flux_step(rank: int, world: int, dev, sides=(64, 128), warmup: int = 2, steps: int = 5,
+                  mode: str = "fp8_w8a8", check_side: int | None = 64) -> dict:
     """Flux-dev-shaped forwards (19 double + 38 single blocks, hidden 3072, 24 x 128 heads,
-    512 txt tokens + a side x side image-token grid, FP8 W8A8 linears, Sage attention):
-    side 64 -> 4608 tokens (the metric's shape), side 128 -> 16,896 tokens (2048^2 latent).
+    512 txt tokens + a side x side image-token grid, Sage attention; linears FP8 e4m3 W8A8
+    by default, "fp8" = the reference's qfloat8 weight-only form): side 64 -> 4608 tokens
+    (the metric's shape), side 128 -> 16,896 tokens (2048^2 latent).
     With N ranks the joint sequence is split N ways and attention runs head-parallel
-    (Ulysses all-to-all).  One model, one entry per image side."""
+    (Ulysses all-to-all).  At N > 1 and side `check_side`, rank 0 also runs the same
+    inputs on one GPU alone: the gathered Ulysses output is compared with it (cosine,
+    max-abs) and its time is the strong-scaling reference."""
     from quantfun2_b200.dit import FluxDiT, SeqParallel, flux_position_ids, flux_step_flops, rope_freqs
 
     T = 512
     if T % world or 24 % world:
         return {"skipped": f"{world} ranks do not divide 512 txt tokens and 24 heads"}
-    model = FluxDiT(device=dev, seed=0)
+    model = FluxDiT(device=dev, seed=0, mode=mode)
     sp = SeqParallel(torch.distributed.group.WORLD if world > 1 else None)
+    linears = ("FP8 e4m3 W8A8 (per-token activation, per-channel weight scales)" if mode == "fp8_w8a8"
+               else "FP8 e4m3 weight-only (per-channel scales), bf16 activations")
     out = {}
     for side in sides:
         I = side * side
@@ -221,18 +365,45 @@ def run_flux_step(rank: int, world: int, dev, sides=(64, 128), warmup: int = 2, 
         fwd = lambda: model(img_l, txt_l, t, y, f_l, sp)  # noqa: E731
         nsteps = steps if I <= 4096 else max(2, steps // 2)
         r = _time_forward(fwd, world, dev, warmup if I <= 4096 else 1, nsteps)
-        del img, txt, img_l, txt_l, f_l, freqs
-        torch.cuda.empty_cache()
         fl = flux_step_flops(T + I)
         sec = r.pop("sec")
-        out[f"tokens_{T + I}"] = {
-            "ms_per_step": sec * 1e3, "tflops": fl / sec / 1e12, "flops_per_step": fl, "tokens": T + I, **r,
-            "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU",
-            "linears": "FP8 e4m3 W8A8 (per-token activation, per-channel weight scales)",
-            "attention": "Sage INT8 QK / FP8 PV"}
+        entry = {"ms_per_step": sec * 1e3, "tflops": fl / sec / 1e12, "flops_per_step": fl, "tokens": T + I, **r,
+                 "parallelism": f"ulysses sp{world}" if world > 1 else "single GPU", "linears": linears,
+                 "attention": "Sage INT8 QK / FP8 PV"}
+        if world > 1 and side == check_side:
+            entry.update(_flux_ulysses_check(model, fwd, rank, world, dev, img, txt, t, y, freqs, il, sec))
+        out[f"tokens_{T + I}"] = entry
+        del img, txt, img_l, txt_l, f_l, freqs
+        torch.cuda.empty_cache()
     del model
     torch.cuda.empty_cache()
     return out
+
+
+def _flux_ulysses_check(model, fwd, rank, world, dev, img, txt, t, y, freqs, il, sec_sp) -> dict:
+    """The gathered N-rank output against rank 0's single-GPU forward of the same inputs,
+    and rank 0's single-GPU step time (CUDA graph) for the strong-scaling efficiency."""
+    from quantfun2_b200.dit import SeqParallel
+
+    with torch.inference_mode():
+        o_l = fwd().contiguous()
+        parts = [torch.empty_like(o_l) for _ in range(world)]
+        torch.distributed.all_gather(parts, o_l)
+        res = {}
+        if rank == 0:
+            o_sp = torch.cat(parts, 1).float()
+            single = lambda: model(img, txt, t, y, freqs, SeqParallel(None))  # noqa: E731
+            o_1 = single().float()
+            cos = torch.nn.functional.cosine_similarity(o_sp.flatten(), o_1.flatten(), dim=0).item()
+            res = {"vs_single_gpu": {"cosine": cos, "max_abs": (o_sp - o_1).abs().max().item(),
+                                     "ref_max_abs": o_1.abs().max().item(),
+                                     "what": "gathered Ulysses output vs rank 0 alone, same inputs and weights"}}
+            r1 = _time_forward(single, 1, dev, 2, 5)
+            res["single_gpu_ms_per_step"] = r1["sec"] * 1e3
+            res["strong_scaling_efficiency"] = r1["sec"] / (world * sec_sp)
+            del o_sp, o_1
+        torch.distributed.barrier()
+    return res
 
 
 def run_blocksparse(dev, S: int = 16384, H: int = 24, D: int = 128, keep_frac: float = 0.125, warmup: int = 3,
@@ -497,17 +668,27 @@ def run_ours(args, rank: int, world: int, dev):
                "output_finite": ok_out}
         del hq, hk, hv, houts, dins, douts
 
-    # ---- the Flux-shaped denoise step (Ulysses over the ranks when N > 1)
-    flux = None
-    if not args.no_flux:
+    quant_s = total_s / args.steps - attn_s
+    # ---- achieved HBM bandwidth of the bandwidth-bound kernels (one GPU's view; rank 0)
+    bandwidth = None
+    if world == 1 and not args.profile and not args.no_bandwidth:
         del q, k, v, out, ws
         torch.cuda.empty_cache()
+        bandwidth = run_bandwidth_kernels(dev, peaks.get("hbm_gbs") or 6650.0, quant_s)
+    # ---- the Flux-shaped denoise step (Ulysses over the ranks when N > 1)
+    flux, flux_wo = None, None
+    if not args.no_flux:
+        if bandwidth is None:
+            del q, k, v, out, ws
+            torch.cuda.empty_cache()
         flux = run_flux_step(rank, world, dev, sides=tuple(int(x) for x in args.flux_sides.split(",")))
+        if world == 1 and not args.profile:
+            flux_wo = run_flux_step(rank, world, dev, sides=(64,), mode="fp8")
     # ---- the Lumina-shaped denoise step (batch-parallel: one sample per rank; on one GPU
     # also the 8-sample batch)
     lumina = None
     if not args.no_lumina:
-        if flux is None:
+        if flux is None and bandwidth is None:
             del q, k, v, out, ws
             torch.cuda.empty_cache()
         lumina = {"b1_per_gpu": run_lumina_step(rank, world, dev, batch=1)}
@@ -520,16 +701,20 @@ def run_ours(args, rank: int, world: int, dev):
 
     if rank != 0:
         return
-    # ---- CPU baseline: the reference's SDPA branch on a bounded sample (rank 0, N=1 only)
-    cpu = None
+    # ---- CPU baseline: the reference's SDPA branch on the same workload (rank 0, N=1 only),
+    # and the other configurations' CPU paths
+    cpu, cpu_more = None, None
     if world == 1 and not args.profile:
-        from oracle.baseline import sdpa_cpu_sample
+        from oracle.baseline import sdpa_cpu
 
-        sdpa_cpu_sample(heads=1, S=S, D=D)
-        dt, fl, thr = sdpa_cpu_sample(heads=4, S=S, D=D)
+        sdpa_cpu(1, 2, S, D)
+        dt, fl, thr = sdpa_cpu(B, H, S, D)
         cpu = {"value": fl / dt / 1e12, "unit": "TFLOPS", "cores": thr, "kind": "port",
-               "sample": f"4 heads x {S} tokens x D={D}, fp32 torch SDPA on the host "
-                         "(the reference's SDPA branch, src/models/flux/attn.py:42-43), one call"}
+               "sample": f"the full workload, B={B} x {H} heads x {S} tokens x D={D}, fp32 torch SDPA on the "
+                         "host (the reference's SDPA branch, src/models/flux/attn.py:42-43), one call",
+               "ms": dt * 1e3}
+        if not args.no_cpu_baselines:
+            cpu_more = run_cpu_baselines()
 
     per_step = total_s / args.steps
     value = world * flops_step / per_step / 1e12
@@ -557,10 +742,19 @@ def run_ours(args, rank: int, world: int, dev):
         "e2e": e2e,
         "gpu_launches": 2 * args.steps,  # sage_prep_kernel and sage_attn_kernel per step (no KV split at this shape)
         "clocks": clocks,
-        "flux_step": flux,
+        "cpu_baselines_other_configs": cpu_more,
+        "bandwidth_kernels": bandwidth,
         "lumina_step": lumina,
         "blocksparse": blocksparse,
+        "flux_step_weight_only_fp8": flux_wo,
+        "flux_step": flux,
     }
+    # the Flux step summary last (ms per step, and at N > 1 the single-GPU comparison)
+    if flux and "skipped" not in flux:
+        line["flux_summary"] = {
+            k: {kk: v[kk] for kk in ("ms_per_step", "tflops", "single_gpu_ms_per_step", "strong_scaling_efficiency",
+                                     "vs_single_gpu") if kk in v}
+            for k, v in flux.items()}
     print(json.dumps(line), flush=True)
 
 

@@ -72,8 +72,8 @@ class LuminaBlock(nn.Module):
         self.modulation = modulation
         self.eps = norm_eps
         self.qkv = _rand_qlin(dim, (heads + 2 * kv_heads) * self.hd, mode, device, gen, bias=False)
-        self.wo = _qlin(pad_head_columns(_rand_weight(dim, heads * self.hd, device, gen), heads, self.hd, hd_pad),
-                        None, mode)
+        self.wo = _qlin(pad_head_columns(_rand_weight(dim, heads * self.hd, device, gen), heads, self.hd,
+                                         self.hd_pad), None, mode)
         w1 = _rand_weight(ffn_hidden, dim, device, gen)
         w3 = _rand_weight(ffn_hidden, dim, device, gen)
         self.w13 = _qlin(glu_interleave(w1, w3), None, mode)

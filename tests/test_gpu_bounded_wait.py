@@ -46,17 +46,22 @@ def test_attention_wait_times_out_then_recovers(cuda):
     q, k, v = qc.to(cuda), kc.to(cuda), vc.to(cuda)
     out = torch.zeros_like(q)
     ws = _workspace(int(lib.qf2_sage_workspace_bytes(B, H, H, B * S, B * S, S, S, 128)), cuda)
+    assert _call(lib, q, k, v, out, ws) == 0               # a clean call first
+    assert lib.qf2_workspace_status(ws.data_ptr(), stream_ptr(cuda)) == 0
+    clean = out.clone()
     assert lib.qf2_sage_fault_injection(2000, 3) == 0
     try:
+        out.zero_()
         assert _call(lib, q, k, v, out, ws) == 0            # launched fine
         assert lib.qf2_workspace_status(ws.data_ptr(), stream_ptr(cuda)) == QF2_ERR_TIMEOUT
         assert lib.qf2_workspace_status(ws.data_ptr(), stream_ptr(cuda)) == 0   # read clears it
     finally:
         lib.qf2_sage_fault_injection(0, -1)
-    # the context is intact: a normal call on it is right
+    # the context is intact: a normal call on it gives the clean call's output bit for bit
     assert _call(lib, q, k, v, out, ws) == 0
     assert lib.qf2_workspace_status(ws.data_ptr(), stream_ptr(cuda)) == 0
+    assert torch.equal(out, clean)
     o = out.float().cpu().numpy()
     ref = sage.sageattn(qc.float().numpy(), kc.float().numpy(), vc.float().numpy())
     cos = float((o * ref).sum() / np.sqrt((o * o).sum() * (ref * ref).sum()))
-    assert cos >= 0.9995, cos
+    assert cos >= 0.999, cos

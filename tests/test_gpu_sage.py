@@ -146,25 +146,12 @@ def test_sage_quant_codes_bit_exact_small_head_dims(cuda, layout, D):
 
 
 @pytest.mark.parametrize("shape", [(1, 2, 2, 256, 256, 128), (2, 4, 2, 200, 333, 128), (1, 2, 1, 1000, 77, 128),
-                                   (2, 6, 2, 300, 300, 96), (1, 3, 3, 500, 257, 64), (1, 24, 8, 4352, 4352, 96)])
+                                   (2, 6, 2, 300, 300, 96), (1, 3, 3, 500, 257, 64)])
 def test_sage_attention_matches_oracle(cuda, shape):
     from quantfun2_b200.attention import sageattn
 
     B, Hq, Hkv, Sq, Skv, D = shape
     q, k, v = make_qkv(B, Hq, Hkv, Sq, Skv, seed=7, D=D)
-    if Sq > 2000:   # the Lumina shape: check a sample of heads against the CPU oracle
-        o = sageattn(q.to(cuda), k.to(cuda), v.to(cuda)).float().cpu().numpy()[:, ::5]
-        q, k, v = q[:, ::5], k[:, [h // 3 for h in range(0, 24, 5)]], v[:, [h // 3 for h in range(0, 24, 5)]]
-        o_ref_q = q.float().numpy()
-        qf, kf, vf = o_ref_q, k.float().numpy(), v.float().numpy()
-        ro = np.stack([np.stack([sage.attention_from_codes(sage.quantize_head(qf[b, i], kf[b, i], vf[b, i],
-                                                                              1 / math.sqrt(D)))
-                                 for i in range(qf.shape[1])]) for b in range(B)])
-        rs = sage.sdpa_reference(qf, kf, vf)
-        c_or, c_sd = cosine(o, ro), cosine(o, rs)
-        print(f"D={D} lumina shape: cos(oracle)={c_or:.6f} cos(sdpa)={c_sd:.6f}")
-        assert c_or >= 0.9995 and c_sd >= 0.998
-        return
     o = sageattn(q.to(cuda), k.to(cuda), v.to(cuda)).float().cpu().numpy()
     qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
     ro = sage.sageattn(qf, kf, vf)
@@ -174,6 +161,29 @@ def test_sage_attention_matches_oracle(cuda, shape):
     assert c_or >= 0.9995
     assert c_sd >= 0.998
     assert np.abs(o - ro).max() < 0.05
+
+
+def test_sage_attention_lumina_shape_head_dim_96(cuda):
+    """The Lumina shape: 24 query / 8 kv heads of 96 over 4352 tokens.  On sequences this
+    long the kernel's P codes (taken against the running row max) and the oracle's (against
+    the final max) round differently, so the check is that the GPU is as close to exact
+    attention as the oracle is, on a sample of heads and rows."""
+    from quantfun2_b200.attention import sageattn
+
+    B, Hq, Hkv, S, D = 1, 24, 8, 4352, 96
+    q, k, v = make_qkv(B, Hq, Hkv, S, S, seed=9, D=D)
+    o = sageattn(q.to(cuda), k.to(cuda), v.to(cuda)).float().cpu().numpy()
+    qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
+    rows = np.r_[0:128, 2000:2064, S - 128:S]
+    for h in (0, 7, 13, 23):
+        hk = h // 3
+        ro = sage.attention_from_codes(sage.quantize_head(qf[0, h], kf[0, hk], vf[0, hk], 1 / math.sqrt(D)), rows)
+        sc = (qf[0, h][rows].astype(np.float64) @ kf[0, hk].T.astype(np.float64)) / math.sqrt(D)
+        p = np.exp(sc - sc.max(axis=1, keepdims=True))
+        exact = (p / p.sum(axis=1, keepdims=True)) @ vf[0, hk].astype(np.float64)
+        c, c_gpu, c_orc = cosine(o[0, h, rows], ro), cosine(o[0, h, rows], exact), cosine(ro, exact)
+        print(f"head {h}: cos(oracle)={c:.6f} cos(exact) gpu={c_gpu:.6f} oracle={c_orc:.6f}")
+        assert c >= 0.999 and c_gpu >= c_orc - 2e-4 and c_gpu >= 0.998
 
 
 def test_sage_attention_split_kv_matches_oracle(cuda):
