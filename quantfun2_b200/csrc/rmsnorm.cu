@@ -41,10 +41,28 @@ QF2_DEV void store_vec(T* p, const float* f) {
 template <typename T>
 QF2_DEV float round_to(float v) { return to_f32(from_f32<T>(v)); }
 
+// V weights starting at element i as fp32: 16-byte vector loads when the weight is aligned
+template <typename TW, int V>
+QF2_DEV void load_w(const TW* w, int64_t i, bool vec, float* f) {
+  if (vec && sizeof(TW) * V % 16 == 0) {
+#pragma unroll
+    for (int b = 0; b < (int)(sizeof(TW) * V / 16); ++b) {
+      const uint4 r = __ldg(reinterpret_cast<const uint4*>(w + i) + b);
+      const TW* e = reinterpret_cast<const TW*>(&r);
+#pragma unroll
+      for (int j = 0; j < (int)(16 / sizeof(TW)); ++j) f[b * (16 / sizeof(TW)) + j] = to_f32(e[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < V; ++j) f[j] = to_f32(w[i + j]);
+  }
+}
+
 // EAGER: y = round_O( float(round_X(x * r)) * w );  FUSED: y = round_O((x * r) * w)
 template <typename TX, typename TW, typename TO, int LPR, int MAXC, bool EAGER>
 __global__ void __launch_bounds__(256) rmsnorm_reg_kernel(const TX* __restrict__ x, int64_t xs, const TW* __restrict__ w,
-                                                          TO* __restrict__ y, int64_t ys, int64_t M, int64_t N, float eps) {
+                                                          TO* __restrict__ y, int64_t ys, int64_t M, int64_t N, float eps,
+                                                          int w_vec) {
   constexpr int V = 16 / sizeof(TX);
   const int64_t nvec = N / V;
   const int rows_per_block = blockDim.x / LPR;
@@ -71,12 +89,12 @@ __global__ void __launch_bounds__(256) rmsnorm_reg_kernel(const TX* __restrict__
     for (int c = 0; c < MAXC; ++c) {
       const int64_t vi = sub + (int64_t)c * LPR;
       if (vi < nvec) {
-        float o[V];
+        float o[V], wv[V];
+        load_w<TW, V>(w, vi * V, w_vec != 0, wv);
 #pragma unroll
         for (int i = 0; i < V; ++i) {
-          const float wv = to_f32(w[vi * V + i]);
           const float n = __fmul_rn(v[c][i], r);
-          o[i] = EAGER ? __fmul_rn(round_to<TX>(n), wv) : __fmul_rn(n, wv);
+          o[i] = EAGER ? __fmul_rn(round_to<TX>(n), wv[i]) : __fmul_rn(n, wv[i]);
         }
         if constexpr (sizeof(TO) == sizeof(TX)) {
           store_vec(yr + vi * V, o);
@@ -132,12 +150,18 @@ static void dispatch(const void* x, int64_t xs, const void* w, void* y, int64_t 
     if (g > 148 * 16) g = 148 * 16;
     return (unsigned)(g < 1 ? 1 : g);
   };
+  const int wv = al16(w) ? 1 : 0;
+  // a warp per row for wide rows, the per-lane register tile sized to the row (one HBM read)
   if (vec_ok && nvec <= 8) {
-    rmsnorm_reg_kernel<TX, TW, TO, 8, 1, EAGER><<<grid_for(32), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
+    rmsnorm_reg_kernel<TX, TW, TO, 8, 1, EAGER><<<grid_for(32), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps, wv);
   } else if (vec_ok && nvec <= 16) {
-    rmsnorm_reg_kernel<TX, TW, TO, 16, 1, EAGER><<<grid_for(16), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
+    rmsnorm_reg_kernel<TX, TW, TO, 16, 1, EAGER><<<grid_for(16), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps, wv);
+  } else if (vec_ok && nvec <= 32 * 4) {
+    rmsnorm_reg_kernel<TX, TW, TO, 32, 4, EAGER><<<grid_for(8), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps, wv);
+  } else if (vec_ok && nvec <= 32 * 9) {
+    rmsnorm_reg_kernel<TX, TW, TO, 32, 9, EAGER><<<grid_for(8), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps, wv);
   } else if (vec_ok && nvec <= 32 * 16) {
-    rmsnorm_reg_kernel<TX, TW, TO, 32, 16, EAGER><<<grid_for(8), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
+    rmsnorm_reg_kernel<TX, TW, TO, 32, 16, EAGER><<<grid_for(8), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps, wv);
   } else {
     rmsnorm_generic_kernel<TX, TW, TO, EAGER><<<grid_for(8), 256, 0, st>>>(X, xs, W, Y, ys, M, N, eps);
   }

@@ -953,10 +953,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       for (int i = 0; i < 128; ++i) mf[i] = __int_as_float((int)s[i] + kMagicBits);
       const int64_t rem = sk.len - (int64_t)(jb + j) * kTile;
       if (rem < kTile) {
-        // ragged last tile: 0.0 is below every magic-encoded value, so it acts as -inf
+        // ragged last tile: keys past the sequence end get -inf (below every magic-encoded
+        // value in the max, and fma(-inf, sc > 0, c) = -inf gives P = 0 whatever the scales)
 #pragma unroll
         for (int i = 0; i < 128; ++i)
-          if (i >= rem) mf[i] = 0.0f;
+          if (i >= rem) mf[i] = -INFINITY;
       }
       // row max per 64-column half (one K scale each): 4 independent fmax3 chains
       float mq[8];
@@ -980,9 +981,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         m_run = m_new;
         l_run *= alpha;
       }
-      // P_fp8 = 2^(x - m_run + kPScaleLog2), x = (mf - magic) * sc: exact subtraction, one fma
+      // P_fp8 = 2^(x - m_run + kPScaleLog2) with x = (mf - magic) * sc, as one fma on the
+      // magic-encoded integer: fma(mf, sc, -(magic * sc + bias)).  The product is exact inside
+      // the fma; the folded constant's rounding shifts a row half's exponents by at most
+      // half an ulp of magic * sc (~1e-4 in log2 units for these scales), a common factor
+      // of that half's P and row sum, far below the e4m3 rounding of P.
       const float bias = m_run - kPScaleLog2;
-      const float2 nb = make_float2(-bias, -bias), nmag = make_float2(-kMagic, -kMagic);
+      const float c0 = -fmaf(kMagic, sc0, bias), c1 = -fmaf(kMagic, sc1, bias);
+      const float2 cv0 = make_float2(c0, c0), cv1 = make_float2(c1, c1);
       const float2 sc0v = make_float2(sc0, sc0), sc1v = make_float2(sc1, sc1);
       // P_t was last read by PV_t(j-1); its completion also orders the O rescale below
       if (j >= 1 && !wwait(bar_o_done + t, (j - 1) & 1)) { ok = false; break; }
@@ -994,13 +1000,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int chunk = 0; chunk < 8; ++chunk) {
-        const float2 scv = chunk < 4 ? sc0v : sc1v;
+        const float2 scv = chunk < 4 ? sc0v : sc1v, cv = chunk < 4 ? cv0 : cv1;
         uint32_t w[4];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const int i0 = chunk * 16 + q4 * 4;
-          const float2 x01 = ffma2(fadd2(make_float2(mf[i0], mf[i0 + 1]), nmag), scv, nb);
-          const float2 x23 = ffma2(fadd2(make_float2(mf[i0 + 2], mf[i0 + 3]), nmag), scv, nb);
+          const float2 x01 = ffma2(make_float2(mf[i0], mf[i0 + 1]), scv, cv);
+          const float2 x23 = ffma2(make_float2(mf[i0 + 2], mf[i0 + 3]), scv, cv);
           const float2 p01 = make_float2(fast_exp2(x01.x), fast_exp2(x01.y));
           const float2 p23 = make_float2(fast_exp2(x23.x), fast_exp2(x23.y));
           acc = fadd2(acc, fadd2(p01, p23));

@@ -134,6 +134,27 @@ def test_softmax_golden_and_long_rows(cuda, golden):
     np.testing.assert_allclose(out, r, rtol=1e-5, atol=1e-9)
 
 
+@pytest.mark.parametrize("n,dtype", [(16384, torch.bfloat16), (2048, torch.float16), (8192, torch.float32),
+                                     (96, torch.bfloat16), (4100, torch.float32)])
+def test_softmax_register_rows(cuda, n, dtype):
+    """Rows that fit one CTA's registers (read once, written once), with -inf entries and
+    a -inf tail; within one ulp of the output dtype of the fp64 softmax (96 bf16 elements
+    leave most threads of the CTA idle)."""
+    from quantfun2_b200.kernels import inplace_softmax
+
+    g = torch.Generator().manual_seed(n)
+    z = (torch.randn(37, n, generator=g) * 4).to(dtype)
+    z[3, n // 3:] = -float("inf")
+    z[5, ::7] = -float("inf")
+    ref = torch.softmax(z.double(), -1)
+    out = inplace_softmax(z.to(cuda)).cpu()
+    # one ulp of the output dtype relative to the value (fp32: the SFU exponential's error)
+    ulp = {torch.bfloat16: 2.0 ** -7, torch.float16: 2.0 ** -10, torch.float32: 1e-5}[dtype]
+    tiny = {torch.bfloat16: 1e-38, torch.float16: 2.0 ** -24, torch.float32: 1e-38}[dtype]  # underflow floor
+    err = (out.double() - ref).abs()
+    assert bool((err <= ulp * ref.abs() + tiny).all()), (err / ref.abs().clamp_min(1e-30)).max().item()
+
+
 def test_qkv_norm_rope_fused(cuda):
     """Fused q/k RMSNorm + RoPE + v copy into offset views of joint buffers."""
     from quantfun2_b200.kernels import qkv_norm_rope
@@ -161,13 +182,15 @@ def test_qkv_norm_rope_fused(cuda):
     assert torch.equal(v[:, off:].cpu(), qkv.view(B, L, 3, H, D)[:, :, 2])
 
 
-def test_copy_chunks_ulysses_layouts(cuda):
+@pytest.mark.parametrize("Ls", [40, 37])
+def test_copy_chunks_ulysses_layouts(cuda, Ls):
     """qf2_copy_chunks against torch permute copies for the three layout changes around
     the head-parallel all-to-all (pack q/k/v per destination rank, unpack received
-    shards, scatter output heads into a row-strided buffer)."""
+    shards, scatter output heads into a row-strided buffer); 768-byte chunks take the
+    warp-per-chunk path, whole shards the segment path."""
     from quantfun2_b200.kernels import copy_chunks
 
-    B, Ls, P, Hp, D = 2, 40, 4, 3, 128
+    B, P, Hp, D = 2, 4, 3, 128
     e = 2
     hb = Hp * D * e
     qkv3 = torch.randn(B, Ls, 3, P * Hp, D, device=cuda).bfloat16()
