@@ -56,8 +56,9 @@ const char* qf2_status_string(int status);
 const char* qf2_last_error(void);
 /* 0 when the current CUDA device is compute capability 10.0, else QF2_ERR_DEVICE. */
 int qf2_device_check(void);
-/* Synchronizes `stream`, then returns QF2_ERR_TIMEOUT if the status word at
- * the start of `workspace` is nonzero (and clears it), else QF2_OK. */
+/* Synchronizes `stream`, then reads (and clears) the status word at the start of
+ * `workspace`: QF2_ERR_TIMEOUT if a bounded wait gave up, QF2_ERR_ARG if a kernel met an
+ * index outside its range (and skipped it), else QF2_OK. */
 int qf2_workspace_status(void* workspace, qf2_stream_t stream);
 
 /* ---------------------------------------------------------------- RoPE --
@@ -91,6 +92,18 @@ int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_t B, int64_
                       const int64_t* k_strides, void* v_out, const int64_t* v_strides, const void* q_weight,
                       const void* k_weight, float eps, const void* freqs_cis, const int64_t* freqs_strides,
                       qf2_stream_t stream);
+
+/* RoPE with row scatter, the RoPE of the reference's RAS partial ops (PYCUDA_ROPE_KERNEL,
+ * src/kernels/cuda/ras.cu:12-52): y[b, idx[n], h, :] = rotate(x[b, n, h, :], f[n]) for the
+ * N rows of x [B, N, H, D] into y [B, M, H, D]; f holds D/2 complex factors per row as
+ * interleaved (cos, sin) floats, row stride f_stride floats; idx int64 [N] on the device.
+ * bf16 only (as the reference); strides {batch, row, head} in elements, D % 8 == 0, 16-byte
+ * aligned rows.  Rows of y not named by idx are left untouched.  workspace (optional, a
+ * 256-byte status word area): an index outside [0, M) skips its row and makes
+ * qf2_workspace_status return QF2_ERR_ARG. */
+int qf2_rope_scatter(const void* x, const int64_t* x_strides, const float* f, int64_t f_stride, const int64_t* idx,
+                     void* y, const int64_t* y_strides, int64_t B, int64_t N, int64_t M, int64_t H, int64_t D,
+                     int dtype, void* workspace, qf2_stream_t stream);
 
 /* ------------------------------------------------------------- RMSNorm --
  * Replaces rmsnorm_apply (src/kernels/__init__.py:73-80) and the Triton
@@ -269,6 +282,17 @@ int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d,
                 const void* bias, int bias_dtype, int64_t gelu_col0, int glu, const void* residual, int64_t ldr,
                 const void* gate, int64_t gate_stride, int64_t rows_per_gate, void* workspace,
                 int64_t workspace_bytes, qf2_stream_t stream);
+/* Row-indexed product of the reference's RAS partial ops (_partially_linear,
+ * src/kernels/triton/ras.py:28-128): for each of `batch` blocks of M rows of A (row stride
+ * lda; A [batch*M, K]), D[b * out_rows + row_idx[m], :] = A[b*M + m, :] . B^T * col_scale + bias,
+ * written to the row-strided D (ldd); rows of D not named by row_idx are left untouched.
+ * row_idx: int64 device array of M entries; an entry outside [0, out_rows) is skipped and
+ * reported through qf2_workspace_status (QF2_ERR_ARG).  Operands and output dtypes as
+ * qf2_gemm (the reference: bf16 x bf16 -> bf16, no scale, no bias). */
+int qf2_gemm_rows_indexed(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t batch,
+                          int64_t M, int64_t N, int64_t K, int ab_dtype, int d_dtype, const int64_t* row_idx,
+                          int64_t out_rows, const float* col_scale, const void* bias, int bias_dtype, void* workspace,
+                          int64_t workspace_bytes, qf2_stream_t stream);
 /* Fused adaLN input (src/models/flux/mmdit.py:127-128, src/models/common/utilities.py:4-5):
  * y = LayerNorm(x) * (1 + scale[b]) + shift[b] over rows of N (no affine, eps), b = row /
  * rows_per_batch, shift/scale bf16 with row stride mod_stride; out QF2_BF16, or QF2_E4M3

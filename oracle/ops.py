@@ -67,3 +67,30 @@ def softmax_lastdim(x: np.ndarray, dtype: str = "f32") -> np.ndarray:
     m = np.max(x, axis=-1, keepdims=True)
     e = np.exp(x - m)
     return round_to((e / np.sum(e, axis=-1, keepdims=True)).astype(np.float32), dtype)
+
+
+def rope_scatter(x: np.ndarray, f: np.ndarray, idx: np.ndarray, y: np.ndarray) -> np.ndarray:
+    """RAS RoPE with row scatter (src/kernels/cuda/ras.cu:12-52) with the stated rounding:
+    x [B, N, H, D] (bf16 values as float32), f [N, D] float32 (cos, sin per pair), idx [N],
+    y [B, M, H, D] updated copy.  Per pair: re = x0 f0 - x1 f1, im = x0 f1 + x1 f0, every
+    product and sum rounded to fp32, then to bf16."""
+    x = np.asarray(x, np.float32)
+    y = np.array(y, np.float32, copy=True)
+    a0, a1 = x[..., 0::2], x[..., 1::2]
+    c = np.asarray(f, np.float32)[None, :, None, 0::2]
+    s = np.asarray(f, np.float32)[None, :, None, 1::2]
+    re = (a0 * c).astype(np.float32) - (a1 * s).astype(np.float32)
+    im = (a0 * s).astype(np.float32) + (a1 * c).astype(np.float32)
+    out = np.empty_like(x)
+    out[..., 0::2] = re.astype(np.float32)
+    out[..., 1::2] = im.astype(np.float32)
+    y[:, np.asarray(idx)] = round_to(out, "bf16")
+    return y
+
+
+def partially_linear(x: np.ndarray, w: np.ndarray, idx: np.ndarray, out: np.ndarray) -> np.ndarray:
+    """RAS row-indexed linear (src/kernels/triton/ras.py:28-128): out[b, idx[m]] = x[b, m] . w^T
+    (float64 here; the device accumulates in fp32 and rounds once to the output dtype)."""
+    out = np.array(out, np.float64, copy=True)
+    out[:, np.asarray(idx)] = np.einsum("bmk,nk->bmn", np.asarray(x, np.float64), np.asarray(w, np.float64))
+    return out

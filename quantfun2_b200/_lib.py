@@ -96,6 +96,14 @@ SIGNATURES = {
         c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "qf2_codes_convert": (
         c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p]),
+    "qf2_gemm_rows_indexed": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+         c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p]),
+    "qf2_rope_scatter": (
+        c_int,
+        [c_void_p, _P64, c_void_p, c_int64, c_void_p, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64, c_int64,
+         c_int, c_void_p, c_void_p]),
     "qf2_gemm_ex": (
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,

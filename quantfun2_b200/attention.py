@@ -23,7 +23,7 @@ from . import _lib
 from ._lib import QF2Error, check, i64, ptr32, require_device, stream_ptr
 
 __all__ = ["sageattn", "sageattn_varlen", "sage_quantize", "sage_workspace_layout", "block_topk_select",
-           "blocksparse_attn"]
+           "blocksparse_attn", "flash_attn", "do_attn", "unpad_tokens", "pad_tokens", "ATTN"]
 
 
 def _dt(t: torch.Tensor) -> int:
@@ -236,3 +236,75 @@ def blocksparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, idx: tor
                                            stream_ptr(q.device)),
           "qf2_blocksparse_attn")
     return out
+
+
+# ------------------------------------------------ the attention processor seam --
+# Backend of do_attn, as the reference's module global ATTN (src/models/common/attn.py:15):
+# "b200" / "sage" -> Sage INT8/FP8 attention, "flash" / "sdpa" -> bf16 tcgen05 attention.
+ATTN = "b200"
+
+
+def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float | None = None,
+               tensor_layout: str = "NHD") -> torch.Tensor:
+    """Dense bf16 / fp16 attention on the tensor cores (tcgen05 kind::f16, exact online
+    softmax, fp32 accumulation): the block-sparse kernel with every key block kept.  The
+    counterpart of the reference's flash / SDPA branches (src/models/common/attn.py:92-107,
+    123-130) for unmasked batches.  D = 128; equal query and key lengths."""
+    B, Hq, S, D, _ = _hnd(q, tensor_layout)
+    nb = (S + BLOCK - 1) // BLOCK
+    idx = torch.arange(nb, dtype=torch.int32, device=q.device).expand(B, Hq, nb, nb).contiguous()
+    return blocksparse_attn(q, k, v, idx, sm_scale=softmax_scale, tensor_layout=tensor_layout)
+
+
+def unpad_tokens(x: torch.Tensor, mask: torch.Tensor):
+    """x [B, S, H, D], key-padding mask [B, S] (True = token) -> (packed [B*S, H, D] whose
+    first sum(mask) rows are the tokens in order, cu_seqlens int32 [B+1], dest int64 [B, S]:
+    each token's packed row, B*S for padding).  All on the device, no host sync (the
+    reference's _upad_input, src/misc/padding.py:75-182, reads the lengths back with .item())."""
+    B, S = mask.shape
+    m = mask.to(torch.bool)
+    counts = m.sum(1, dtype=torch.int32)
+    cu = torch.zeros(B + 1, dtype=torch.int32, device=x.device)
+    cu[1:] = torch.cumsum(counts, 0, dtype=torch.int32)
+    pos = torch.cumsum(m, 1, dtype=torch.int64) - 1
+    dest = torch.where(m, cu[:-1, None].to(torch.int64) + pos, torch.full_like(pos, B * S))
+    packed = torch.empty(B * S + 1, *x.shape[2:], dtype=x.dtype, device=x.device)
+    packed.index_copy_(0, dest.reshape(-1), x.reshape(B * S, *x.shape[2:]))
+    return packed[:B * S], cu, dest
+
+
+def pad_tokens(packed_out: torch.Tensor, dest: torch.Tensor) -> torch.Tensor:
+    """Inverse of unpad_tokens: [B*S, H, D] packed rows -> [B, S, H, D], zeros at padding
+    (as the reference's pad_input)."""
+    B, S = dest.shape
+    full = torch.cat([packed_out, packed_out.new_zeros(1, *packed_out.shape[1:])], 0)
+    return full.index_select(0, dest.reshape(-1)).view(B, S, *packed_out.shape[1:])
+
+
+def do_attn(attn, xq: torch.Tensor, xk: torch.Tensor, xv: torch.Tensor, attn_mask: torch.Tensor | None,
+            apply_fn=None, batch: int | None = None, seq_len: int | None = None,
+            softmax_scale: float | None = None) -> torch.Tensor:
+    """Mirror of the reference's _do_attn (src/models/common/attn.py:59-130) for the B200
+    kernels: xq [B, S, Hq, D], xk / xv [B, S, Hkv, D] (NHD), attn_mask [B, S] key padding
+    (True = token, None = all tokens) -> [B, S, Hq, D].  ATTN "b200" / "sage": Sage INT8/FP8
+    attention, through the varlen kernel on the unpadded tokens when the mask pads (no
+    host sync, padded rows of the output are zero); "flash" / "sdpa": bf16 attention on the
+    tensor cores (unpadded batches).  `attn`, `apply_fn`, `batch` and `seq_len` are
+    accepted for signature parity (the reference builds the SDPA mask with apply_fn)."""
+    D = xq.shape[-1]
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(D)
+    if ATTN in ("flash", "sdpa"):
+        if attn_mask is not None:
+            raise QF2Error("the bf16 attention path takes unpadded batches; use ATTN='b200' for padded ones")
+        return flash_attn(xq, xk, xv, softmax_scale, tensor_layout="NHD")
+    if ATTN not in ("b200", "sage"):
+        raise QF2Error(f"unknown ATTN backend {ATTN!r}")
+    if attn_mask is None:
+        return sageattn(xq, xk, xv, tensor_layout="NHD", sm_scale=softmax_scale)
+    B, S = attn_mask.shape
+    pq, cu, dest = unpad_tokens(xq, attn_mask)
+    pk, _, _ = unpad_tokens(xk, attn_mask)
+    pv, _, _ = unpad_tokens(xv, attn_mask)
+    o = sageattn_varlen(pq, pk, pv, cu, cu, S, S, sm_scale=softmax_scale)
+    return pad_tokens(o, dest)

@@ -104,7 +104,7 @@ extern "C" int qf2_workspace_status(void* workspace, qf2_stream_t stream) {
   if (word != 0) {
     const int zero = 0;
     cudaMemcpy(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice);
-    return QF2_ERR_TIMEOUT;
+    return word == qf2::kDevBadIndex ? QF2_ERR_ARG : QF2_ERR_TIMEOUT;
   }
   return QF2_OK;
 }

@@ -65,7 +65,41 @@ struct Args {
   int bn;         // tile width: 256, or 192 / 128 for CTA-pair tiles (fewer idle SMs in the last wave)
   int vec_ok;     // scale / bias / residual / gate rows 16-byte aligned: vector loads
   int* status;
+  // row scatter (the row-indexed product of the reference's RAS ops): row m of the product
+  // goes to output row (m / idx_rows) * out_rows + row_idx[m % idx_rows]; null = none
+  const int64_t* row_idx;
+  int64_t idx_rows, out_rows;
 };
+
+// 32 output values of one row to a scattered row: 16-bit (bf16 / fp16) or fp32, vector
+// stores when the whole chunk is in range and aligned
+QF2_DEV void store_row32(const Args& A, int64_t row, int64_t nc, int ncols, const float* o) {
+  if (A.d_f32) {
+    float* dst = reinterpret_cast<float*>(A.d) + row * A.ldd + nc;
+    for (int i = 0; i < 32; ++i)
+      if (i < ncols) dst[i] = o[i];
+    return;
+  }
+  uint16_t h[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (A.d_f16) {
+      __half t = __float2half_rn(o[i]);
+      h[i] = *reinterpret_cast<uint16_t*>(&t);
+    } else {
+      __nv_bfloat16 t = __float2bfloat16_rn(o[i]);
+      h[i] = *reinterpret_cast<uint16_t*>(&t);
+    }
+  }
+  uint16_t* dst = reinterpret_cast<uint16_t*>(A.d) + row * A.ldd + nc;
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) *reinterpret_cast<uint4*>(dst + 8 * v) = *reinterpret_cast<const uint4*>(h + 8 * v);
+  } else {
+    for (int i = 0; i < 32; ++i)
+      if (i < ncols) dst[i] = h[i];
+  }
+}
 
 QF2_DEV void load_f32x32(const float* p, float* o) {
 #pragma unroll
@@ -252,6 +286,16 @@ QF2_DEV void epilogue_tile(const Args& A, Stager& st, uint32_t tacc, int64_t m0w
           o[i] = fmaf(g, o[i], __bfloat162float(A.residual[m * A.ldr + nc + i]));
         }
       }
+    }
+    if (A.row_idx != nullptr) {  // warp-uniform: scattered rows, direct stores
+      if (row_ok) {
+        const int64_t ri = A.row_idx[m % A.idx_rows];
+        if (ri >= 0 && ri < A.out_rows)
+          store_row32(A, (m / A.idx_rows) * A.out_rows + ri, nc, ncols, o);
+        else
+          atomicExch(A.status, kDevBadIndex);  // skipped; the status word reports it
+      }
+      continue;
     }
     if (!A.d_f32) {
       stage_store(st, o, lane, nc, m0w);  // TMA clips rows >= M and columns >= N
@@ -659,11 +703,12 @@ static cudaError_t pair_clusters(K* kern, int* out) {
 
 using namespace qf2::gemm;
 
-extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M,
-                           int64_t N, int64_t K, int ab_dtype, int d_dtype, const float* row_scale,
-                           const float* col_scale, const void* bias, int bias_dtype, int64_t gelu_col0, int glu,
-                           const void* residual, int64_t ldr, const void* gate, int64_t gate_stride,
-                           int64_t rows_per_gate, void* workspace, int64_t workspace_bytes, qf2_stream_t stream) {
+static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M, int64_t N,
+                    int64_t K, int ab_dtype, int d_dtype, const float* row_scale, const float* col_scale,
+                    const void* bias, int bias_dtype, int64_t gelu_col0, int glu, const void* residual, int64_t ldr,
+                    const void* gate, int64_t gate_stride, int64_t rows_per_gate, const int64_t* row_idx,
+                    int64_t idx_rows, int64_t out_rows, void* workspace, int64_t workspace_bytes,
+                    qf2_stream_t stream) {
   if (!a || !b || !d) return QF2_ERR_ARG;
   if (ab_dtype != QF2_BF16 && ab_dtype != QF2_F16 && ab_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
   if (d_dtype != QF2_BF16 && d_dtype != QF2_F16 && d_dtype != QF2_F32) return QF2_ERR_DTYPE;
@@ -700,11 +745,11 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
   CUtensorMap md;
   const uint64_t dd[2] = {(uint64_t)(glu ? N / 2 : N), (uint64_t)M};
   const uint32_t bd[2] = {32, 32};
-  if (d_dtype != QF2_F32 &&
+  if (d_dtype != QF2_F32 && !row_idx &&
       !qf2_make_tmap_2d_sw64(&md, d_dtype == QF2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                              d, dd, (uint64_t)ldd * 2, bd))
     return QF2_ERR_ALIGN;
-  if (d_dtype == QF2_F32) md = ma;
+  if (d_dtype == QF2_F32 || row_idx) md = ma;
   Args args;
   args.d = d;
   args.ldd = ldd;
@@ -729,6 +774,9 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
                 (gate_stride % 8) == 0;
   if (glu && !args.vec_ok) return QF2_ERR_ALIGN;
   args.status = reinterpret_cast<int*>(workspace);
+  args.row_idx = row_idx;
+  args.idx_rows = idx_rows > 0 ? idx_rows : 1;
+  args.out_rows = out_rows;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   QF2_CUDA_CHECK(cudaMemsetAsync(workspace, 0, sizeof(int), s));
   if (use_pair) {
@@ -748,6 +796,29 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
   }
   QF2_LAUNCH_CHECK();
   return QF2_OK;
+}
+
+extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M,
+                           int64_t N, int64_t K, int ab_dtype, int d_dtype, const float* row_scale,
+                           const float* col_scale, const void* bias, int bias_dtype, int64_t gelu_col0, int glu,
+                           const void* residual, int64_t ldr, const void* gate, int64_t gate_stride,
+                           int64_t rows_per_gate, void* workspace, int64_t workspace_bytes, qf2_stream_t stream) {
+  return gemm_run(a, lda, b, ldb, d, ldd, M, N, K, ab_dtype, d_dtype, row_scale, col_scale, bias, bias_dtype, gelu_col0,
+                  glu, residual, ldr, gate, gate_stride, rows_per_gate, nullptr, 0, 0, workspace, workspace_bytes,
+                  stream);
+}
+
+extern "C" int qf2_gemm_rows_indexed(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd,
+                                     int64_t batch, int64_t M, int64_t N, int64_t K, int ab_dtype, int d_dtype,
+                                     const int64_t* row_idx, int64_t out_rows, const float* col_scale,
+                                     const void* bias, int bias_dtype, void* workspace, int64_t workspace_bytes,
+                                     qf2_stream_t stream) {
+  if (!row_idx) return QF2_ERR_ARG;
+  if (batch <= 0 || M <= 0 || out_rows < 1) return QF2_ERR_SHAPE;
+  // a's rows are the batch's M rows one after another (row stride lda); a row whose index
+  // is outside [0, out_rows) is not written and sets the workspace status word
+  return gemm_run(a, lda, b, ldb, d, ldd, batch * M, N, K, ab_dtype, d_dtype, nullptr, col_scale, bias, bias_dtype, -1,
+                  0, nullptr, 0, nullptr, 0, 1, row_idx, M, out_rows, workspace, workspace_bytes, stream);
 }
 
 extern "C" int qf2_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M,

@@ -37,6 +37,7 @@ enum : int {
   kDevTimeoutSoftmax = 3,
   kDevTimeoutEpilogue = 4,
   kDevBadLaunch = 5,
+  kDevBadIndex = 6,   // an index argument outside its range (the access was skipped)
 };
 
 // ~2 s at 1.9 GHz; each wait gives up after this many SM clocks.

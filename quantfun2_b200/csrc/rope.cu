@@ -280,3 +280,94 @@ extern "C" int qf2_qkv_norm_rope(const void* qkv, int64_t qkv_row_stride, int64_
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }
+
+// ------------------------------------------------------- RoPE with row scatter --
+// The RoPE of the reference's RAS partial ops (PYCUDA_ROPE_KERNEL, src/kernels/cuda/ras.cu:
+// 12-52): y[b, idx[n], h, :] = x[b, n, h, :] rotated by f[n] (interleaved pairs times the
+// complex f[n, p], fp32 products, each pair rounded to bf16).  One warp per (b, n) row of
+// H * D elements, 8 elements (4 pairs) per 16-byte vector; rows of y not named by idx are
+// left untouched; an index outside [0, M) skips its row and sets the status word.
+// The complex product is rounded step by step (no fused multiply-add): re = x0 f0 - x1 f1,
+// im = x0 f1 + x1 f0, each product and the sum rounded to fp32.
+namespace qf2 {
+namespace rope {
+
+struct ScatterArgs {
+  const __nv_bfloat16* x;
+  const float* f;
+  const int64_t* idx;
+  __nv_bfloat16* y;
+  int64_t xb, xn, xh;   // x strides (elements)
+  int64_t yb, ym, yh;   // y strides (elements)
+  int64_t fn;           // f stride per n (floats)
+  int64_t B, N, M;
+  int H, D;
+  int* status;
+};
+
+__global__ void __launch_bounds__(256) rope_scatter_kernel(ScatterArgs A) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= A.B * A.N) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t b = row / A.N, n = row - b * A.N;
+  const int64_t m = A.idx[n];
+  if (m < 0 || m >= A.M) {
+    if (lane == 0 && A.status) atomicExch(A.status, kDevBadIndex);
+    return;
+  }
+  const int vpr = A.D / 8;               // vectors per head row
+  const int nvec = A.H * vpr;
+  for (int v = lane; v < nvec; v += 32) {
+    const int h = v / vpr, d = (v - h * vpr) * 8;
+    const uint4 raw = *reinterpret_cast<const uint4*>(A.x + b * A.xb + n * A.xn + h * A.xh + d);
+    const float4 f01 = *reinterpret_cast<const float4*>(A.f + n * A.fn + d);
+    const float4 f23 = *reinterpret_cast<const float4*>(A.f + n * A.fn + d + 4);
+    const float fr[8] = {f01.x, f01.y, f01.z, f01.w, f23.x, f23.y, f23.z, f23.w};
+    const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    uint4 out;
+    __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float2 a = __bfloat1622float2(xp[p]);
+      const float c = fr[2 * p], sn = fr[2 * p + 1];
+      const float re = __fsub_rn(__fmul_rn(a.x, c), __fmul_rn(a.y, sn));
+      const float im = __fadd_rn(__fmul_rn(a.x, sn), __fmul_rn(a.y, c));
+      op[p] = __floats2bfloat162_rn(re, im);
+    }
+    *reinterpret_cast<uint4*>(A.y + b * A.yb + m * A.ym + h * A.yh + d) = out;
+  }
+}
+
+}  // namespace rope
+}  // namespace qf2
+
+extern "C" int qf2_rope_scatter(const void* x, const int64_t* x_strides, const float* f, int64_t f_stride,
+                                const int64_t* idx, void* y, const int64_t* y_strides, int64_t B, int64_t N,
+                                int64_t M, int64_t H, int64_t D, int dtype, void* workspace, qf2_stream_t stream) {
+  using namespace qf2::rope;
+  if (!x || !x_strides || !f || !idx || !y || !y_strides) return QF2_ERR_ARG;
+  if (dtype != QF2_BF16) return QF2_ERR_DTYPE;
+  if (B < 0 || N < 0 || M < 0 || H <= 0 || D <= 0 || D % 8 || H * D > (1 << 24)) return QF2_ERR_SHAPE;
+  if (B == 0 || N == 0) return QF2_OK;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                       reinterpret_cast<uintptr_t>(f);
+  if ((al & 15) || (f_stride % 4)) return QF2_ERR_ALIGN;
+  for (int i = 0; i < 3; ++i)
+    if ((x_strides[i] % 8) || (y_strides[i] % 8)) return QF2_ERR_ALIGN;
+  ScatterArgs A;
+  A.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  A.f = f;
+  A.idx = idx;
+  A.y = reinterpret_cast<__nv_bfloat16*>(y);
+  A.xb = x_strides[0]; A.xn = x_strides[1]; A.xh = x_strides[2];
+  A.yb = y_strides[0]; A.ym = y_strides[1]; A.yh = y_strides[2];
+  A.fn = f_stride;
+  A.B = B; A.N = N; A.M = M;
+  A.H = (int)H; A.D = (int)D;
+  A.status = reinterpret_cast<int*>(workspace);
+  const int64_t blocks = (B * N + 7) / 8;
+  if (blocks > 2147483647ll) return QF2_ERR_SHAPE;
+  rope_scatter_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(A);
+  QF2_LAUNCH_CHECK();
+  return QF2_OK;
+}

@@ -168,6 +168,33 @@ QF2_DEV uint32_t sage_code(float x, float s, float r) {
   return (n ^ neg) - neg;
 }
 
+// sage_code on two lanes with the sm_100 f32x2 instructions (each lane rounds like the
+// scalar .rn / .rz instruction; the mul feeds only fma multiplicands, so nothing contracts).
+// ns = -s.  Returns the two codes in the low bytes of c.x / c.y.
+QF2_DEV uint2 sage_code2(float2 x, float2 ns, float2 r) {
+  float2 f;
+  uint32_t tx, ty;
+  asm("{\n\t.reg .b64 rx, rr, rs, rq, rm, rt, rv, rh, rz;\n\t"
+      ".reg .b32 ax, ay;\n\t"
+      "mov.b64 rx, {%4, %5};\n\tmov.b64 rr, {%6, %7};\n\tmov.b64 rs, {%8, %9};\n\t"
+      "mul.rn.f32x2 rq, rx, rr;\n\t"          // q0 = x r
+      "fma.rn.f32x2 rm, rq, rs, rx;\n\t"      // rem = x - s q0 (exact)
+      "fma.rn.f32x2 rt, rm, rr, rq;\n\t"      // t = RN(x / s)
+      "mov.b64 {%2, %3}, rt;\n\t"
+      "and.b32 ax, %2, 0x7fffffff;\n\tand.b32 ay, %3, 0x7fffffff;\n\t"
+      "mov.b64 rv, {ax, ay};\n\t"
+      "mov.b64 rh, {0f3F000000, 0f3F000000};\n\t"
+      "add.rn.f32x2 rv, rv, rh;\n\t"         // |t| + 0.5
+      "mov.b64 rz, {0f4B000000, 0f4B000000};\n\t"
+      "add.rz.f32x2 rv, rv, rz;\n\t"         // 2^23 + floor(|t| + 0.5)
+      "mov.b64 {%0, %1}, rv;\n\t}"
+      : "=f"(f.x), "=f"(f.y), "=r"(tx), "=r"(ty)
+      : "f"(x.x), "f"(x.y), "f"(r.x), "f"(r.y), "f"(ns.x), "f"(ns.y));
+  const uint32_t nx = __float_as_uint(f.x) & 0xffu, ny = __float_as_uint(f.y) & 0xffu;
+  const uint32_t sx = (uint32_t)((int32_t)tx >> 31), sy = (uint32_t)((int32_t)ty >> 31);
+  return make_uint2((nx ^ sx) - sx, (ny ^ sy) - sy);
+}
+
 // ------------------------------------------------------------ preparation --
 // One persistent, TMA-fed, warp-specialised kernel launched in clusters of C CTAs
 // (C <= 8).  Warp 8 produces: it picks the tiles, writes each tile's descriptor next to
@@ -623,20 +650,23 @@ __global__ void __launch_bounds__(kPrepThreads, kPrepCtasPerSm)
     // dequant scales of the two 64-token blocks and their correctly rounded reciprocals
     const float bs[2] = {bm[0] > 0.f ? __fdiv_rn(bm[0], 127.0f) : 1.0f, bm[1] > 0.f ? __fdiv_rn(bm[1], 127.0f) : 1.0f};
     const float br[2] = {__frcp_rn(bs[0]), __frcp_rn(bs[1])};
+    const float2 nbs2[2] = {make_float2(-bs[0], -bs[0]), make_float2(-bs[1], -bs[1])};
+    const float2 br2[2] = {make_float2(br[0], br[0]), make_float2(br[1], br[1])};
     const int64_t tslot = (int64_t)h * (is_q ? ws.tq : ws.tk) + si.tile0 + tile;
     int8_t* dst = (is_q ? ws.qc : ws.kc) + tslot * kTileBytes;
 #pragma unroll
     for (int r8 = 0; r8 < 8; ++r8) {
       const int r = rg + 16 * r8;
-      const float sb = bs[r8 >> 2], rb = br[r8 >> 2];
+      const float2 nsb = nbs2[r8 >> 2], rb = br2[r8 >> 2];
       const uint32_t* wd = reinterpret_cast<const uint32_t*>(&raw[r8]);
       uint32_t y[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = unpack2<T>(wd[j]);
         const float2 x = is_q ? fmul2(f, mul) : fadd2(f, neg[j]);
-        y[2 * j] = sage_code(x.x, sb, rb);
-        y[2 * j + 1] = sage_code(x.y, sb, rb);
+        const uint2 c = sage_code2(x, nsb, rb);
+        y[2 * j] = c.x;
+        y[2 * j + 1] = c.y;
       }
       const uint32_t lo = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
       const uint32_t hi = __byte_perm(__byte_perm(y[4], y[5], 0x0040), __byte_perm(y[6], y[7], 0x0040), 0x5410);

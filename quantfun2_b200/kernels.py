@@ -248,3 +248,62 @@ def copy_chunks(dst: torch.Tensor, src: torch.Tensor, chunk_bytes: int, dims, sr
         ds.insert(0, 0)
     check(_lib.load().qf2_copy_chunks(dst.data_ptr(), src.data_ptr(), int(chunk_bytes), i64(*d), i64(*ss), i64(*ds),
                                       stream_ptr(dst.device)), "qf2_copy_chunks")
+
+
+def rope_scatter(x: torch.Tensor, f: torch.Tensor, idx: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """RoPE of the reference's RAS partial ops (PYCUDA_ROPE_KERNEL, src/kernels/cuda/ras.cu:
+    12-52): y[b, idx[n], h] = x[b, n, h] rotated by f[n] for x [B, N, H, D] bf16, f [N, D]
+    fp32 (interleaved cos, sin per pair; a leading 1 dim is accepted), idx int64 [N] and the
+    destination y [B, M, H, D] bf16, updated in place (rows not in idx untouched).
+    Raises QF2Error when an index lies outside [0, M) (that row is skipped)."""
+    require_device(x)
+    B, N, H, D = x.shape
+    M = y.shape[1]
+    f2 = f.reshape(-1, f.shape[-1]).to(device=x.device, dtype=torch.float32)
+    if f2.stride(-1) != 1:
+        f2 = f2.contiguous()
+    if f2.shape != (N, D):
+        raise QF2Error(f"f must be [N, D] = [{N}, {D}] floats")
+    ix = idx.to(device=x.device, dtype=torch.int64).contiguous()
+    ws = torch.zeros(64, dtype=torch.int32, device=x.device)
+    st = lambda t: i64(t.stride(0), t.stride(1), t.stride(2))  # noqa: E731
+    lib = _lib.load()
+    check(lib.qf2_rope_scatter(x.data_ptr(), st(x), f2.data_ptr(), f2.stride(0), ix.data_ptr(), y.data_ptr(), st(y),
+                               B, N, M, H, D, _lib.dtype_code(x.dtype), ws.data_ptr(), stream_ptr(x.device)),
+          "qf2_rope_scatter")
+    check(lib.qf2_workspace_status(ws.data_ptr(), stream_ptr(x.device)), "qf2_rope_scatter (index range)")
+    return y
+
+
+def partially_linear(x: torch.Tensor, w: torch.Tensor, index: torch.Tensor, out: torch.Tensor | None = None,
+                     check_index: bool = True) -> torch.Tensor:
+    """Row-indexed linear of the reference's RAS partial ops (_partially_linear,
+    src/kernels/triton/ras.py:100-128): out[b, index[m]] = x[b, m] . w^T for x [B, M, K],
+    w [N, K] (bf16 or fp16, same dtype), index int64 [M].  `out` [B, M_out, N] is updated in
+    place (rows not in index untouched); without it a new [B, M, N] tensor is returned
+    whose unindexed rows are uninitialized (the reference returns torch.empty_like(x)).
+    check_index=True synchronizes to report an index outside [0, M_out)."""
+    require_device(x)
+    B, M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K or w.dtype != x.dtype:
+        raise QF2Error("w must be [N, K] in x's dtype")
+    if out is None:
+        out = torch.empty(B, M, N, dtype=x.dtype, device=x.device)
+    if out.dim() != 3 or out.shape[0] != B or out.shape[2] != N or out.stride(2) != 1 or \
+            out.stride(0) != out.shape[1] * out.stride(1):
+        raise QF2Error("out must be [B, M_out, N] with contiguous rows and batches")
+    x2 = x.reshape(B * M, K)
+    if x2.stride(-1) != 1 or x2.stride(0) != K:
+        x2 = x2.contiguous()
+    wc = w.contiguous()
+    ix = index.to(device=x.device, dtype=torch.int64).contiguous()
+    ws = torch.zeros(64, dtype=torch.int32, device=x.device)
+    lib = _lib.load()
+    check(lib.qf2_gemm_rows_indexed(x2.data_ptr(), K, wc.data_ptr(), K, out.data_ptr(), out.stride(1), B, M, N, K,
+                                    _lib.dtype_code(x.dtype), _lib.dtype_code(out.dtype), ix.data_ptr(), out.shape[1],
+                                    None, None, _lib.QF2_F32, ws.data_ptr(), 256, stream_ptr(x.device)),
+          "qf2_gemm_rows_indexed")
+    if check_index:
+        check(lib.qf2_workspace_status(ws.data_ptr(), stream_ptr(x.device)), "qf2_gemm_rows_indexed (index range)")
+    return out

@@ -59,3 +59,21 @@ def test_device_check_reports_missing_device():
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
     assert _lib.load().qf2_device_check() == -7
+
+
+def test_loader_reports_a_missing_tensor(tmp_path):
+    """create_quantized_model_from_safetensors names the tensor it cannot find, before
+    anything is allocated or quantized (src/pipeline.py:325-327 raises ValueError too)."""
+    import torch
+    from safetensors.torch import save_file
+
+    from quantfun2_b200.loader import create_quantized_model_from_safetensors
+    from quantfun2_b200.quant import qint8
+
+    lin = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.Linear(16, 8))
+    sd = {k: v for k, v in lin.state_dict().items() if k != "1.bias"}
+    save_file(sd, str(tmp_path / "m.safetensors"))
+    with torch.device("meta"):
+        meta = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.Linear(16, 8))
+    with pytest.raises(ValueError, match="1.bias"):
+        create_quantized_model_from_safetensors(meta, tmp_path / "m.safetensors", device="cpu", dtype=qint8)
