@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--no-cpu-baselines", action="store_true", help="skip the CPU baselines of configs 1, 3, 4, 5")
     p.add_argument("--flux-sides", default="64,128",
                    help="image-token grid sides of the Flux step (64 -> 4608 tokens, 128 -> 16,896)")
+    p.add_argument("--profile-kernel", default=None,
+                   help="run one kernel's case three times and exit (single-kernel ncu captures)")
     p.add_argument("--profile", action="store_true",
                    help="for ncu runs: no clock soak, no cuBLAS peak, no CPU baseline, no 8-sample Lumina batch")
     return p.parse_args()
@@ -541,6 +543,139 @@ def run_lumina_step(rank: int, world: int, dev, batch: int = 1, warmup: int = 2,
             "attention": "Sage INT8 QK / FP8 PV, GQA 24/8, head_dim 96"}
 
 
+def profile_cases(dev) -> dict:
+    """One case per kernel for single-kernel ncu captures (`--profile-kernel NAME`): inputs
+    of 0.1-1.2 GB (above the 126 MB L2) in the DiT steps' shapes; each case runs its
+    kernel(s) three times."""
+    from quantfun2_b200 import kernels as K
+    from quantfun2_b200 import quant as Q
+    from quantfun2_b200.attention import block_topk_select, blocksparse_attn, sageattn
+    from quantfun2_b200.dit import flux_position_ids, rope_freqs
+
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1)
+    rn = lambda *sh: torch.randn(*sh, device=dev, generator=g)  # noqa: E731
+
+    def rope():
+        q, k = rn(4, 4608, 24, 128).to(bf), rn(4, 4608, 24, 128).to(bf)
+        f = rope_freqs(flux_position_ids(4, 512, 64, 64, dev), (16, 56, 56))
+        return lambda: K.rope_apply_(q, k, f, fp16_trig=False)
+
+    def qkv_norm_rope():
+        qkv = rn(4, 4608, 9216).to(bf)
+        o = [torch.empty(4, 4608, 24, 128, device=dev, dtype=bf) for _ in range(3)]
+        w = torch.ones(128, device=dev, dtype=bf)
+        f = rope_freqs(flux_position_ids(4, 512, 64, 64, dev), (16, 56, 56))
+        return lambda: K.qkv_norm_rope(qkv, 24, w, w, f, *o)
+
+    def rmsnorm():
+        x, w = rn(65536, 2304).to(bf), torch.ones(2304, device=dev, dtype=bf)
+        return lambda: K.rmsnorm_apply(x, w, 1e-5)
+
+    def softmax():
+        x = rn(8192, 16384).to(bf)
+        return lambda: K.inplace_softmax(x)
+
+    def gate_residual():
+        x, y, h = (rn(65536, 2304).to(bf) for _ in range(3))
+        w, gt = torch.ones(2304, device=dev, dtype=bf), rn(1, 2304).to(bf)
+        return lambda: K.rms_gate_residual(x, y, h, 65536, w, 1e-5, gt, True, w, 1e-5, gt)
+
+    def ln_modulate():
+        x, mod = rn(36864, 3072).to(bf), rn(1, 6144).to(bf)
+        return lambda: (Q.ln_modulate(x, mod[:, :3072], mod[:, 3072:], 36864, "bf16"),
+                        Q.ln_modulate(x, mod[:, :3072], mod[:, 3072:], 36864, "e4m3"))
+
+    def quantize_rows():
+        x = rn(36864, 3072).to(bf)
+        return lambda: Q.quantize_rows(x, "e4m3")
+
+    def codes_to_bf16():
+        c, _ = Q.quantize_rows(rn(36864, 3072).to(bf), "int8")
+        return lambda: Q.codes_to_bf16(c, "int8")
+
+    def quantize_weight():
+        w = rn(12288, 3072).half()
+        return lambda: Q.quantize_weight(w, "int8")
+
+    def copy_chunks():
+        src = rn(8 * 3 * 4 * 4608 * 3 * 128).to(bf)
+        dst = torch.empty_like(src)
+        hb = 768
+        return lambda: K.copy_chunks(dst, src, hb, (8, 3, 4 * 4608), (hb, 8 * hb, 24 * hb),
+                                     (3 * 4 * 4608 * hb, 4 * 4608 * hb, hb))
+
+    def sage():
+        q, v = rn(2, 24, 4608, 128).to(bf), rn(2, 24, 4608, 128).to(bf)
+        k = (rn(2, 24, 4608, 128) + 3 * rn(1, 24, 1, 128)).to(bf)
+        return lambda: sageattn(q, k, v)
+
+    def sage_split():   # 3 heads per GPU: split-KV attention + sage_combine_kernel
+        q, k, v = (rn(1, 3, 4608, 128).to(bf) for _ in range(3))
+        return lambda: sageattn(q, k, v)
+
+    def gemm_fp8():
+        a, _ = Q.quantize_rows(rn(4608, 3072).to(bf), "e4m3")
+        b, _ = Q.quantize_rows(rn(12288, 3072).to(bf), "e4m3")
+        return lambda: Q.gemm(a, b, fp8=True)
+
+    def gemm_bf16_glu():
+        a, b = rn(4352, 2304).to(bf), rn(12288, 2304).to(bf)
+        return lambda: Q.gemm(a, b, glu=True)
+
+    def gemm_single():   # M <= 128: single-CTA tiles (adaLN linear)
+        a, b = rn(1, 3072).to(bf), rn(18432, 3072).to(bf)
+        return lambda: Q.gemm(a, b)
+
+    def blocksparse():
+        q, k, v = (rn(1, 24, 16384, 128).to(bf) for _ in range(3))
+        idx = block_topk_select(q, k, 16)
+        return lambda: (block_topk_select(q, k, 16), blocksparse_attn(q, k, v, idx))
+
+    def ras():
+        x = rn(2, 2048, 24, 128).to(bf)
+        f = rn(2048, 128)
+        idx = torch.randperm(4608, device=dev)[:2048]
+        y = torch.empty(2, 4608, 24, 128, device=dev, dtype=bf)
+        xa, w = rn(2, 2048, 3072).to(bf), rn(3072, 3072).to(bf)
+        out = torch.empty(2, 4608, 3072, device=dev, dtype=bf)
+        return lambda: (K.rope_scatter(x, f, idx, y), K.partially_linear(xa, w, idx, out=out, check_index=False))
+
+    def lumina_step():   # one Lumina-2B-shaped forward, B=1, eager (launch lists)
+        from quantfun2_b200.lumina import LuminaDiT
+
+        m = LuminaDiT(device=dev, seed=0)
+        img, cap = rn(1, 4096, 64).to(bf), rn(1, 256, 2304).to(bf)
+        t, fr = torch.rand(1, device=dev, generator=g), m.make_freqs(1, 256, 64, 64, dev)
+        return lambda: m(img, t, cap, fr)
+
+    def flux_step():     # one Flux-dev-shaped forward at 4608 tokens, eager (launch lists)
+        from quantfun2_b200.dit import FluxDiT
+
+        m = FluxDiT(device=dev, seed=0)
+        img, txt = rn(1, 4096, 64).to(bf), rn(1, 512, 4096).to(bf)
+        t, y = torch.rand(1, device=dev, generator=g), rn(1, 768).to(bf)
+        fr = rope_freqs(flux_position_ids(1, 512, 64, 64, dev), (16, 56, 56))
+        return lambda: m(img, txt, t, y, fr)
+
+    return {"lumina_step": lumina_step, "flux_step": flux_step, "rope": rope, "qkv_norm_rope": qkv_norm_rope, "rmsnorm": rmsnorm, "softmax": softmax,
+            "gate_residual": gate_residual, "ln_modulate": ln_modulate, "quantize_rows": quantize_rows,
+            "codes_to_bf16": codes_to_bf16, "quantize_weight": quantize_weight, "copy_chunks": copy_chunks,
+            "sage": sage, "sage_split": sage_split, "gemm_fp8": gemm_fp8, "gemm_bf16_glu": gemm_bf16_glu,
+            "gemm_single": gemm_single, "blocksparse": blocksparse, "ras": ras}
+
+
+def run_profile_kernel(name: str, dev) -> None:
+    cases = profile_cases(dev)
+    if name not in cases:
+        raise SystemExit(f"unknown kernel case {name!r}; one of {sorted(cases)}")
+    fn = cases[name]()
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    print(f"profile case {name}: ok", flush=True)
+
+
 def run_ours(args, rank: int, world: int, dev):
     from quantfun2_b200 import _lib
     from quantfun2_b200._lib import check, i64, stream_ptr
@@ -768,6 +903,9 @@ def main():
         return
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.profile_kernel:
+        run_profile_kernel(args.profile_kernel, dev)
+        return
     if world > 1:
         from datetime import timedelta
 

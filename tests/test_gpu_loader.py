@@ -47,7 +47,8 @@ def test_safetensors_quantize_on_load_matches_quantize_model(cuda, tmp_path, qna
     m = _Model()
     path = tmp_path / "model.safetensors"
     save_file({k: v.contiguous() for k, v in m.state_dict().items()}, str(path))
-    ref = quant.quantize_model(copy.deepcopy(m), q, device="cuda", quantization_device="cuda")
+    # like the reference's, quantize_model moves only the converted linears to the device
+    ref = quant.quantize_model(copy.deepcopy(m), q, device="cuda", quantization_device="cuda").to(cuda)
     with torch.device("meta"):
         meta = _Model()
     got = create_quantized_model_from_safetensors(meta, path, device="cuda", quantization_device="cuda", dtype=q)
