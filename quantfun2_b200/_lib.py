@@ -11,7 +11,9 @@ import os
 from ctypes import c_float, c_int, c_int64, c_void_p, POINTER
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libqf2b200.so"
+# QF2_LIBRARY may name another build of the same library (same C ABI), e.g. one compiled
+# with different tuning macros; the default is the in-tree build.
+LIB_PATH = Path(os.environ.get("QF2_LIBRARY") or Path(__file__).resolve().parent / "libqf2b200.so")
 
 QF2_OK = 0
 QF2_F32, QF2_F16, QF2_BF16, QF2_I8, QF2_E4M3, QF2_I32 = range(6)

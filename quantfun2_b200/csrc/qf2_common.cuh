@@ -404,6 +404,13 @@ QF2_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
       : "memory");
 }
 
+// Registers -> TMEM: every one of 32 lanes x 8 consecutive columns set to v (the store's
+// eight source registers are one aligned block, so wider forms would tie up more of them).
+QF2_DEV void tmem_fill8(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+               : "memory");
+}
+
 QF2_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 QF2_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

@@ -764,6 +764,47 @@ QF2_DEV void store_row_out(void* out, const Strides3& os, int b, int h, int64_t 
   }
 }
 
+// 2^x on the FMA pipe (no SFU) for two lanes, x >= -126 after clamping: x = n + f with
+// n = floor(x) (round-toward-minus-infinity add of 1.5 * 2^23) and f in [0, 1); 2^f by a
+// degree-3 polynomial (relative error < 7.5e-5 on [0, 1); coefficients from a Lawson
+// minimax fit of 2^f done for this kernel), then n added to the exponent field: the low
+// bits of 1.5 * 2^23 + n shifted left by 23 are n << 23.  Used for part of the softmax
+// exponentials so that the SFU and the FMA pipe share them.
+#ifndef QF2_SAGE_EMU_MASK
+#define QF2_SAGE_EMU_MASK 0
+#endif
+constexpr uint32_t kEmuMask = QF2_SAGE_EMU_MASK;   // bit c: chunk c of a row's 8 uses exp2_fma2
+// the chunk (of 8 per row) after which a softmax warpgroup lets the other one start its exp
+// pass (measured: 5, i.e. three quarters into the pass)
+#ifndef QF2_SAGE_PP_CHUNK
+#define QF2_SAGE_PP_CHUNK 5
+#endif
+constexpr int kPingPongChunk = QF2_SAGE_PP_CHUNK;
+QF2_DEV float2 exp2_fma2(float2 x) {
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  float2 r;
+  asm("{\n\t.reg .b64 rx, rm, rt, rn, rf, rp, rc;\n\t.reg .b32 px, py, tx, ty;\n\t"
+      "mov.b64 rx, {%2, %3};\n\t"
+      "mov.b64 rm, {0f4B400000, 0f4B400000};\n\t"
+      "add.rm.f32x2 rt, rx, rm;\n\t"                       // 1.5 * 2^23 + floor(x)
+      "sub.rn.f32x2 rn, rm, rt;\n\t"                       // -floor(x), exact
+      "add.rn.f32x2 rf, rx, rn;\n\t"                       // f = x - floor(x), exact
+      "mov.b64 rc, {0f3D9FCB2E, 0f3D9FCB2E};\n\t"
+      "mov.b64 rp, {0f3E677E2C, 0f3E677E2C};\n\t"
+      "fma.rn.f32x2 rp, rc, rf, rp;\n\t"
+      "mov.b64 rc, {0f3F322228, 0f3F322228};\n\t"
+      "fma.rn.f32x2 rp, rp, rf, rc;\n\t"
+      "mov.b64 rc, {0f3F7FFB19, 0f3F7FFB19};\n\t"
+      "fma.rn.f32x2 rp, rp, rf, rc;\n\t"                   // 2^f
+      "mov.b64 {px, py}, rp;\n\tmov.b64 {tx, ty}, rt;\n\t"
+      "shl.b32 tx, tx, 23;\n\tshl.b32 ty, ty, 23;\n\t"
+      "add.s32 %0, px, tx;\n\tadd.s32 %1, py, ty;\n\t}"
+      : "=r"(*reinterpret_cast<uint32_t*>(&r.x)), "=r"(*reinterpret_cast<uint32_t*>(&r.y))
+      : "f"(x.x), "f"(x.y));
+  return r;
+}
+
 // fma on two packed fp32 lanes (sm_100 f32x2 instruction)
 QF2_DEV float2 ffma2(float2 a, float2 b, float2 c) {
   float2 r;
@@ -925,13 +966,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         if (!wwait(bar_kv_full + s, (j / kStages) & 1)) { ok = false; break; }
         const uint64_t dK = dK0 + (uint64_t)s * kStageStep;
         for (int t = 0; t < ntile && ok; ++t) {
-          if (j > 0 && !wwait(bar_s_empty + t, (j - 1) & 1)) { ok = false; break; }
+          // S_t holds the softmax warps' fill of the magic bits (their arrive of phase j)
+          if (!wwait(bar_s_empty + t, j & 1)) { ok = false; break; }
           tc_fence_after();
           const uint64_t dQ = dQ0 + (uint64_t)t * kTileStep;
           if (lane == 0) {
+            // accumulate onto the fill: S = 0x4B400000 + q.k (int32) is the fp32 bit pattern
+            // of 1.5 * 2^23 + q.k, the magic encoding the softmax reads as a float directly
 #pragma unroll
-            for (int kk = 0; kk < KSTEPS; ++kk)
-              mma_i8(tmem + t * 128, dQ + 2 * kk, dK + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < KSTEPS; ++kk) mma_i8(tmem + t * 128, dQ + 2 * kk, dK + 2 * kk, idesc_qk, 1u);
             tc_commit(bar_s_full + t);
           }
           __syncwarp();
@@ -965,6 +1008,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       sqs = ws.qs[qslot * 4 + (row >> 6)];
       ok = wwait(bar_q, 0);  // k scales are in smem once the Q tiles have landed
     }
+    // S_t starts each KV tile filled with the magic bits 0x4B400000 (the QK MMA accumulates
+    // onto it), so the int32 scores read back are already the fp32 encoding 1.5 * 2^23 + s
+    // (|s| <= 128 * 127^2 < 2^22): no conversion per element.  The fill of tile j + 1 is
+    // stored right after tile j is read, before S_t is handed back to the MMA warp.
+    auto fill_s = [&]() {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) tmem_fill8(tS + c * 8, (uint32_t)kMagicBits);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_s_empty + t);
+    };
+    if (ok) fill_s();
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; ok && j < nkt; ++j) {
       if (!wwait(bar_s_full + t, j & 1)) { ok = false; break; }
@@ -973,14 +1029,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_s_empty + t);
-
-      // int32 -> fp32 exactly via the 1.5*2^23 magic constant (|s| < 2^22)
+      if (j + 1 < nkt) fill_s();
       float mf[128];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) mf[i] = __int_as_float((int)s[i] + kMagicBits);
+      for (int i = 0; i < 128; ++i) mf[i] = __uint_as_float(s[i]);
       const int64_t rem = sk.len - (int64_t)(jb + j) * kTile;
       if (rem < kTile) {
         // ragged last tile: keys past the sequence end get -inf (below every magic-encoded
@@ -1037,8 +1089,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
           const int i0 = chunk * 16 + q4 * 4;
           const float2 x01 = ffma2(make_float2(mf[i0], mf[i0 + 1]), scv, cv);
           const float2 x23 = ffma2(make_float2(mf[i0 + 2], mf[i0 + 3]), scv, cv);
-          const float2 p01 = make_float2(fast_exp2(x01.x), fast_exp2(x01.y));
-          const float2 p23 = make_float2(fast_exp2(x23.x), fast_exp2(x23.y));
+          float2 p01, p23;
+          if ((kEmuMask >> chunk) & 1u) {   // compile-time: this chunk's exps on the FMA pipe
+            p01 = exp2_fma2(x01);
+            p23 = exp2_fma2(x23);
+          } else {
+            p01 = make_float2(fast_exp2(x01.x), fast_exp2(x01.y));
+            p23 = make_float2(fast_exp2(x23.x), fast_exp2(x23.y));
+          }
           acc = fadd2(acc, fadd2(p01, p23));
           w[q4] = (uint32_t)f32x2_to_e4m3x2(p01.x, p01.y) | ((uint32_t)f32x2_to_e4m3x2(p23.x, p23.y) << 16);
         }
@@ -1047,7 +1105,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         // iteration j starts when tile 0's is three quarters done, tile 0's of j + 1 when
         // tile 1's is (measured: the exp pass of one warpgroup alone does not fill the
         // SFU, two fully overlapped ones leave it idle during the max passes)
-        if (ntile == 2 && chunk == 5) {
+        if (ntile == 2 && chunk == kPingPongChunk) {
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_pp + t);
         }
