@@ -37,7 +37,15 @@ QF2_DEV_HOST_INLINE bool head_dim_ok(int64_t D) { return D == 64 || D == 96 || D
 constexpr int kTileBytes = 16384;   // 128 rows x 128 bytes of 8-bit codes
 constexpr int kQuantBlock = 64;     // tokens per INT8 scale block
 static_assert(kTile == 2 * kQuantBlock, "a Q/K tile holds two INT8 scale blocks");
-constexpr int kStages = 4;          // K/V smem ring depth
+// P tiles per Q tile in shared memory: 2 lets the softmax write P(j) while PV(j-1) still
+// reads P(j-1) (the K/V ring then has 3 stages to stay within shared memory; measured
+// 0.4370 -> 0.4332 ms at B=2, H=24, S=4608)
+#ifndef QF2_SAGE_PBUF
+#define QF2_SAGE_PBUF 2
+#endif
+constexpr int kPBuf = QF2_SAGE_PBUF;
+static_assert(kPBuf == 1 || kPBuf == 2, "one or two P tiles per Q tile");
+constexpr int kStages = kPBuf == 2 ? 3 : 4;  // K/V smem ring depth
 constexpr int kMaxKvTiles = 512;    // k-scale smem capacity (65536 tokens)
 constexpr int kMaxSplits = 8;       // KV splits of the attention
 constexpr float kLog2_448 = 8.807354922057604f;
@@ -711,14 +719,15 @@ constexpr int kMagicBits = 0x4B400000;
 struct AttnSmem {
   static constexpr int q = 0;                                   // 2 Q tiles
   static constexpr int kv = q + 2 * kTileBytes;                 // stages x (K, V)
-  static constexpr int p = kv + kStages * 2 * kTileBytes;       // one P tile per Q tile
-  static constexpr int kscale = p + 2 * kTileBytes;             // up to kMaxKvTiles x 16 B
+  static constexpr int p = kv + kStages * 2 * kTileBytes;       // kPBuf P tiles per Q tile ([t][buf])
+  static constexpr int kscale = p + 2 * kPBuf * kTileBytes;     // up to kMaxKvTiles x 16 B
   static constexpr int bars = kscale + kMaxKvTiles * 16;
-  static constexpr int nbars = 1 + 2 * kStages + 2 * 5 + 1;
+  static constexpr int nbars = 1 + 2 * kStages + 2 * 4 + 2 * kPBuf + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int total = misc + 64;
   static constexpr int alloc = total + 1024;  // slack for manual 1024-B alignment
 };
+static_assert(AttnSmem::alloc <= 227 * 1024, "attention shared memory exceeds the per-CTA limit");
 
 struct AttnParams {
   Workspace ws;
@@ -853,8 +862,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
   uint64_t* bar_s_full = bar_kv_empty + kStages;  // [2] per Q tile
   uint64_t* bar_s_empty = bar_s_full + 2;          // [2]
   uint64_t* bar_p_full = bar_s_empty + 2;          // [2 tiles]
-  uint64_t* bar_o_done = bar_p_full + 2;           // [2 tiles]: PV_t(i) completed
-  uint64_t* bar_pp = bar_o_done + 2;              // [2 tiles]: softmax t is far enough into its exp pass
+  uint64_t* bar_o_done = bar_p_full + 2;           // [tile][P buffer]: PV_t(i) of P buffer i % kPBuf completed
+  uint64_t* bar_pp = bar_o_done + 2 * kPBuf;       // [2 tiles]: softmax t is far enough into its exp pass
   uint64_t* bar_drain = bar_pp + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + AttnSmem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + AttnSmem::misc + 8);
@@ -868,7 +877,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       mbar_init(bar_s_full + t, 1);
       mbar_init(bar_s_empty + t, 4);
       mbar_init(bar_p_full + t, 4);
-      mbar_init(bar_o_done + t, 1);
+      for (int bb = 0; bb < kPBuf; ++bb) mbar_init(bar_o_done + t * kPBuf + bb, 1);
       mbar_init(bar_pp + t, 4);
     }
     mbar_init(bar_drain, 1);
@@ -947,13 +956,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
         for (int t = 0; t < ntile; ++t) {
           if (!wwait(bar_p_full + t, i & 1)) return false;
           tc_fence_after();
-          const uint64_t dP = dP0 + (uint64_t)t * kTileStep;
+          const uint64_t dP = dP0 + (uint64_t)(t * kPBuf + i % kPBuf) * kTileStep;
           if (lane == 0) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               mma_f8f6f4(tmem + 256 + t * 128, dP + 2 * kk, sdesc_sw128_mnmajor(aV + kk * 4096, kTileBytes, 1024),
                          idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(bar_o_done + t);
+            tc_commit(bar_o_done + t * kPBuf + i % kPBuf);
           }
           __syncwarp();
         }
@@ -1072,13 +1081,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       const float c0 = -fmaf(kMagic, sc0, bias), c1 = -fmaf(kMagic, sc1, bias);
       const float2 cv0 = make_float2(c0, c0), cv1 = make_float2(c1, c1);
       const float2 sc0v = make_float2(sc0, sc0), sc1v = make_float2(sc1, sc1);
-      // P_t was last read by PV_t(j-1); its completion also orders the O rescale below
-      if (j >= 1 && !wwait(bar_o_done + t, (j - 1) & 1)) { ok = false; break; }
+      // P buffer j % kPBuf was last read by PV_t(j - kPBuf): wait for it (phase
+      // (j - kPBuf) / kPBuf of that buffer's barrier; its next phase needs this thread's P)
+      const int pb = j % kPBuf;
+      if (j >= kPBuf && !wwait(bar_o_done + t * kPBuf + pb, ((j - kPBuf) / kPBuf) & 1)) { ok = false; break; }
       if (ntile == 2) {  // ping-pong (see the arrive in the exp pass below)
         if (t == 1 && !wwait(bar_pp, j & 1)) { ok = false; break; }
         if (t == 0 && j >= 1 && !wwait(bar_pp + 1, (j - 1) & 1)) { ok = false; break; }
       }
-      uint8_t* pdst = sP + t * kTileBytes;
+      uint8_t* pdst = sP + (t * kPBuf + pb) * kTileBytes;
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int chunk = 0; chunk < 8; ++chunk) {
@@ -1112,8 +1123,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
       }
       l_run += acc.x + acc.y;
       if (rescale && j > 0) {
-        // O holds sum_{i<j} P_i V_i against the old max (PV(j-1) completed above);
+        // O holds sum_{i<j} P_i V_i against the old max once PV(j-1) has completed;
         // PV(j) is only issued after p_full(j) below
+        if (kPBuf > 1 && !wwait(bar_o_done + t * kPBuf + (j - 1) % kPBuf, ((j - 1) / kPBuf) & 1)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -1136,7 +1151,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sage_attn_kernel(AttnParams P
     if (active) {
       const int64_t r_tok = (int64_t)qt * kTile + row;
       if (ok && nkt > 0) {
-        if (!wwait(bar_o_done + t, (nkt - 1) & 1)) {
+        if (!wwait(bar_o_done + t * kPBuf + (nkt - 1) % kPBuf, ((nkt - 1) / kPBuf) & 1)) {
           fail(kDevTimeoutEpilogue);
           ok = false;
         }
