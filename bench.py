@@ -45,8 +45,8 @@ B, H, S, D = 2, 24, 4608, 128
 WORKLOAD = f"sage attention, B={B} H={H} S={S} (4096 img + 512 txt) D={D}, bf16 io, INT8 QK^T / FP8 PV"
 METRIC = "attention TFLOPS (Flux-shaped 4608 tok, Sage INT8 QK / FP8 PV)"
 # dram bytes (read + write) of one sage_attn_kernel launch at this workload, from an ncu
-# capture of this kernel at this shape (85.075 MB read + 25.301 MB written)
-NCU_ATTN_TRAFFIC_BYTES = 110_376_448
+# capture of this kernel at this shape (85.074 MB read + 24.418 MB written)
+NCU_ATTN_TRAFFIC_BYTES = 109_491_712
 
 
 def parse():
