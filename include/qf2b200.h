@@ -246,7 +246,8 @@ int qf2_blocksparse_attn(const void* q, const int64_t* q_strides, const void* k,
  * contiguous (row strides lda/ldb in elements), fp32 accumulation, D QF2_BF16, QF2_F16
  * or QF2_F32 (row stride ldd; the residual and SwiGLU epilogues need QF2_BF16).  row_scale, col_scale and bias may be NULL; bias is QF2_BF16 or QF2_F32.
  * N % 8 == 0.  Workspace: >= 256 bytes (status word).
- * Weight-only INT8/FP8 linear: D = qf2_gemm(x_bf16, bf16(codes), col_scale = w_scale).
+ * Weight-only INT8/FP8 linear: D = qf2_gemm_codes(x, codes, col_scale = w_scale) for M <= 128,
+ * else D = qf2_gemm_ex(x, qf2_codes_convert(codes), col_scale = w_scale).
  * W8A8 FP8 linear: D = qf2_gemm(e4m3(x), e4m3 codes, row_scale = x_scale, col_scale = w_scale). */
 int qf2_quantize_rows(const void* x, int64_t ldx, int x_dtype, int64_t M, int64_t K, void* q, int64_t ldq,
                       int q_dtype, float* scales, qf2_stream_t stream);
@@ -282,6 +283,21 @@ int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* d,
                 const void* bias, int bias_dtype, int64_t gelu_col0, int glu, const void* residual, int64_t ldr,
                 const void* gate, int64_t gate_stride, int64_t rows_per_gate, void* workspace,
                 int64_t workspace_bytes, qf2_stream_t stream);
+/* Weight-only linear on 8-bit weight codes, the compute of the reference's torchao
+ * int8 / float8 weight-only linears (src/quant.py:209-241: y = F.linear(x, T(codes)) *
+ * scale, T the activation dtype).  A [M, K] is a_dtype (QF2_BF16 or QF2_F16); B [N, K]
+ * holds codes of b_dtype (QF2_I8, or QF2_E4M3 as bytes), row stride ldb bytes (a multiple
+ * of 16); the kernel converts them in shared memory to exact a_dtype values (every int8
+ * and e4m3 code is one), so D equals qf2_gemm_ex(A, a_dtype(codes), ...) bit for bit
+ * while reading 1 byte per weight.  Epilogue arguments as qf2_gemm_ex.  The conversion is
+ * repeated for every 128-row tile of A: it is the faster route up to M = 128 (the
+ * adaLN / embedding linears); for M of thousands qf2_codes_convert once and qf2_gemm_ex
+ * take about half the time. */
+int qf2_gemm_codes(const void* a, int64_t lda, const void* b_codes, int64_t ldb, int b_dtype, void* d, int64_t ldd,
+                   int64_t M, int64_t N, int64_t K, int a_dtype, int d_dtype, const float* row_scale,
+                   const float* col_scale, const void* bias, int bias_dtype, int64_t gelu_col0, int glu,
+                   const void* residual, int64_t ldr, const void* gate, int64_t gate_stride, int64_t rows_per_gate,
+                   void* workspace, int64_t workspace_bytes, qf2_stream_t stream);
 /* Row-indexed product of the reference's RAS partial ops (_partially_linear,
  * src/kernels/triton/ras.py:28-128): for each of `batch` blocks of M rows of A (row stride
  * lda; A [batch*M, K]), D[b * out_rows + row_idx[m], :] = A[b*M + m, :] . B^T * col_scale + bias,

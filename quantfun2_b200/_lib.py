@@ -106,6 +106,12 @@ SIGNATURES = {
         c_int,
         [c_void_p, _P64, c_void_p, c_int64, c_void_p, c_void_p, _P64, c_int64, c_int64, c_int64, c_int64, c_int64,
          c_int, c_void_p, c_void_p]),
+    "qf2_gemm_codes": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+         c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64,
+         c_void_p, c_int64, c_void_p],
+    ),
     "qf2_gemm_ex": (
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,

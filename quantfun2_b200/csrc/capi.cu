@@ -61,6 +61,14 @@ bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* b
   return make_tmap(map, dtype, 2, base, gdim, gstr, bdim);
 }
 
+bool qf2_make_tmap_2d_noswizzle(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
+                                uint64_t stride_bytes, const uint32_t box[2]) {
+  const cuuint64_t gdim[2] = {dims[0], dims[1]};
+  const cuuint64_t gstr[1] = {stride_bytes};
+  const cuuint32_t bdim[2] = {box[0], box[1]};
+  return make_tmap(map, dtype, 2, base, gdim, gstr, bdim, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 bool qf2_make_tmap_2d_sw64(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
                            uint64_t stride_bytes, const uint32_t box[2]) {
   const cuuint64_t gdim[2] = {dims[0], dims[1]};

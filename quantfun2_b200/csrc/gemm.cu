@@ -14,19 +14,19 @@
 //   warp 1     MMA issuer: 4 x (M128 N256) per stage into one of two TMEM accumulators
 //   warps 2-9  epilogue: TMEM -> registers -> scales/bias/GELU/gated residual -> global,
 //              overlapped with the next tile's main loop through the second accumulator
+//   warps 10-13 (weight-code kernels only) converters: B arrives as 8-bit weight codes
+//              (int8 or e4m3, half the bytes of a 16-bit copy) and is rewritten in shared
+//              memory as the exact 16-bit values of the activations' type before the MMA
 #include "qf2_common.cuh"
 
 #include <algorithm>
 #include <climits>
+#include <type_traits>
 
 namespace qf2 {
 namespace gemm {
 
 constexpr int BM = 128, BN = 256;
-constexpr int kStages = 4;
-constexpr int kABytes = BM * 128;   // 128 rows x 128 bytes of K
-constexpr int kBBytes = BN * 128;   // 256 rows x 128 bytes of K
-constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 320;           // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kEpilogueWarps = 8;
 constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
@@ -34,15 +34,127 @@ constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
 // per epilogue warp: two 32 x 32 bf16 output staging tiles (64-byte swizzle) for TMA stores
 constexpr int kStagingBytes = kEpilogueWarps * 2 * 2048;
 
-struct Smem {
-  static constexpr int stages = 0;
-  static constexpr int staging = kStages * kStageBytes;
+// Operand kinds of the kernels: 16-bit A and B (kind::f16), e4m3 A and B (kind::f8f6f4),
+// or 16-bit A with 8-bit weight codes for B, converted in shared memory (kind::f16).
+enum Kind { kK16 = 0, kKE4M3 = 1, kKCodes = 2 };
+constexpr int kConvWarps = 4;
+constexpr int kConvThreads = 32 * kConvWarps;
+
+// Shared-memory layout per kernel kind and tile form.  A stage holds the A tile (128 rows
+// x 128 bytes of K) and the B tile this CTA feeds the MMA (256 rows, or 128 in a CTA pair);
+// the single-CTA weight-code kernel adds a staging slot per stage for the codes as they
+// arrive (256 rows x 64 bytes), and has one stage fewer to make room.
+template <int KIND, bool PAIR>
+struct Lay {
+  static_assert(!(PAIR && KIND == kKCodes), "weight codes run on the single-CTA gemm_kernel");
+  static constexpr bool codes = KIND == kKCodes;
+  static constexpr int stages = PAIR ? 6 : (codes ? 3 : 4);
+  static constexpr int a_bytes = BM * 128;
+  static constexpr int b_rows = PAIR ? 128 : BN;
+  static constexpr int b_bytes = b_rows * 128;
+  static constexpr int stage_bytes = a_bytes + b_bytes;
+  static constexpr int raw_bytes = codes ? b_rows * 64 : 0;
+  static constexpr int raw = stages * stage_bytes;
+  static constexpr int staging = raw + stages * raw_bytes;
   static constexpr int bars = staging + kStagingBytes;
-  static constexpr int nbars = 2 * kStages + 4 + 1;
+  // full, empty, raw_full per stage; acc_full, acc_empty per accumulator; drain
+  static constexpr int nbars = 3 * stages + 4 + 1;
   static constexpr int misc = bars + nbars * 8;
-  static constexpr int total = misc + 64;
-  static constexpr int alloc = total + 1024;
+  static constexpr int alloc = misc + 64 + 1024;
+  static constexpr int threads = codes ? kThreads + kConvThreads : kThreads;
+  static_assert(alloc <= 227 * 1024, "shared memory");
 };
+
+// Two 8-bit codes (bytes 0 and 2 of r; bytes 1 and 3 zero) -> their exact 16-bit values.
+//   int8 -> bf16: bf16(128 + (c & 127)) - bf16(c < 0 ? 256 : 128); operands and result are
+//                 integers of at most 8 significant bits, so the subtraction is exact
+//   int8 -> fp16: fp16(1024 + (c + 128)) - 1152, exact (integers below 2048)
+QF2_DEV uint32_t i8x2_to_bf16x2(uint32_t r) {
+  const uint32_t hi = (r & 0x007F007Fu) | 0x43004300u;
+  const uint32_t lo = (r & 0x00800080u) | 0x43004300u;
+  uint32_t o;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(o) : "r"(hi), "r"(lo));
+  return o;
+}
+QF2_DEV uint32_t i8x2_to_f16x2(uint32_t r) {
+  const uint32_t v = (r ^ 0x00800080u) | 0x64006400u;
+  uint32_t o;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(o) : "r"(v), "r"(0x64806480u));
+  return o;
+}
+// Two e4m3 codes (bytes 0 and 1 of b) -> fp16x2 (exact: every e4m3 value is an fp16 normal)
+// or bf16x2 (through fp32, exact likewise).
+QF2_DEV uint32_t e4m3x2_to_16(uint32_t b, bool f16) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(b & 0xffffu), __NV_E4M3);
+  if (f16) return (uint32_t)h.x | ((uint32_t)h.y << 16);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  __nv_bfloat162 t = __floats2bfloat162_rn(f.x, f.y);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
+// Converter side of the weight-code kernels: the codes of a B tile (row-major, 64 bytes of
+// K per row, as TMA wrote them without swizzle) -> the K-major 128-byte-swizzled 16-bit
+// tile the MMA reads (16-byte chunk j of row r at r * 128 + ((j ^ (r % 8)) * 16)).  Thread
+// ct converts 16-byte code chunks ct, ct + kConvThreads, ... (chunk k = row k / 4, codes
+// 16 (k % 4) .. + 15 -> output chunks 2 (k % 4) and 2 (k % 4) + 1; the second sits at the
+// first's offset ^ 16).  The offsets are fixed for the kernel's life and computed once.
+template <int CHUNKS>
+struct ConvPlan {
+  uint32_t src[CHUNKS];  // byte offset of the code chunk in its staging slot
+  uint32_t dst[CHUNKS];  // byte offset of its first output chunk in the 16-bit tile
+  int n;                 // chunks this thread converts (the tile may have fewer rows)
+  QF2_DEV ConvPlan(int ct, int nchunks) : n(0) {
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const uint32_t k = (uint32_t)(ct + i * kConvThreads), r = k >> 2, c = k & 3;
+      src[i] = k * 16;
+      dst[i] = r * 128 + (((2 * c) ^ (r & 7)) << 4);
+      if ((int)k < nchunks) n = i + 1;
+    }
+  }
+};
+
+// One staging slot -> one 16-bit tile.  FMT QF2_I8 / QF2_E4M3, F16: fp16 (else bf16)
+// output.  All loads first: the stores cannot alias them, but the compiler cannot tell.
+template <int CHUNKS, int FMT, bool F16>
+QF2_DEV void convert_codes_tile(const uint8_t* raw, uint8_t* dst, const ConvPlan<CHUNKS>& p) {
+  uint4 v[CHUNKS];
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i)
+    if (i < p.n) v[i] = *reinterpret_cast<const uint4*>(raw + p.src[i]);
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    if (i >= p.n) break;
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    uint32_t o[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if constexpr (FMT == QF2_E4M3) {
+        o[2 * q] = e4m3x2_to_16(w[q], F16);
+        o[2 * q + 1] = e4m3x2_to_16(w[q] >> 16, F16);
+      } else {
+        const uint32_t r01 = __byte_perm(w[q], 0u, 0x4140), r23 = __byte_perm(w[q], 0u, 0x4342);
+        o[2 * q] = F16 ? i8x2_to_f16x2(r01) : i8x2_to_bf16x2(r01);
+        o[2 * q + 1] = F16 ? i8x2_to_f16x2(r23) : i8x2_to_bf16x2(r23);
+      }
+    }
+    *reinterpret_cast<uint4*>(dst + p.dst[i]) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + (p.dst[i] ^ 16u)) = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// Calls body(std::integral_constant<int, FMT>, std::integral_constant<bool, F16>) for the
+// run-time code format and activation type: the converter loop is compiled once per pair.
+template <typename F>
+QF2_DEV void with_code_format(int fmt, bool f16, F&& body) {
+  if (fmt == QF2_E4M3) {
+    if (f16) body(std::integral_constant<int, QF2_E4M3>{}, std::true_type{});
+    else body(std::integral_constant<int, QF2_E4M3>{}, std::false_type{});
+  } else {
+    if (f16) body(std::integral_constant<int, QF2_I8>{}, std::true_type{});
+    else body(std::integral_constant<int, QF2_I8>{}, std::false_type{});
+  }
+}
 
 struct Args {
   void* d;
@@ -56,6 +168,7 @@ struct Args {
   int d_f16;      // 16-bit output: 1 fp16, 0 bf16
   int fp8;        // operand type: 1 e4m3, 0 16-bit
   int f16;        // 16-bit operands: 1 fp16, 0 bf16
+  int b_fmt;      // weight-code kernels: B codes QF2_I8 or QF2_E4M3
   int64_t gelu_col0;                 // GELU (tanh form) on columns >= gelu_col0
   const __nv_bfloat16* residual;     // D = residual + gate * y when non-null
   int64_t ldr;
@@ -210,16 +323,22 @@ QF2_DEV void epilogue_tile(const Args& A, Stager& st, uint32_t tacc, int64_t m0w
   const bool row_ok = m < A.M;
   const float rs = (A.row_scale != nullptr && row_ok) ? A.row_scale[m] : 1.0f;
   if (A.glu) {
-    // output columns n_tile / 2 + half * 64 + c * 32 ...: gate at accumulator column
-    // half * 64 + c * 32, up 128 columns further (N % 256 == 0, vec_ok)
+    // B's rows come in groups of 256: [128 gate rows | their 128 up rows].  A tile of
+    // width bn holds bn / 2 gate columns then their bn / 2 up columns (bn = 256: one whole
+    // group; bn = 128: the gate and up quarters of one, rows 64 (n_tile % 256) / 128 on):
+    // gate at accumulator column col, up at gh + col, weight row src0 + col (+ 128 for
+    // up), output column n_tile / 2 + col.  This half takes gh / 2 columns (N % 256 == 0,
+    // vec_ok).
+    const int gh = A.bn / 2;
+    const int64_t src0 = (n_tile / 256) * 256 + (n_tile % 256) / 2;
 #pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
+    for (int c = 0; c < gh / 64; ++c) {
       uint32_t vg[32], vu[32];
-      const int col = half * 64 + c * 32;
+      const int col = half * (gh / 2) + c * 32;
       tmem_ld32(tacc + col, vg);
-      tmem_ld32(tacc + 128 + col, vu);
+      tmem_ld32(tacc + gh + col, vu);
       tmem_wait_ld();
-      const int64_t ns = n_tile + col;
+      const int64_t ns = src0 + col;
       float g[32], u[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
@@ -315,21 +434,34 @@ QF2_DEV void epilogue_tile(const Args& A, Stager& st, uint32_t tacc, int64_t m0w
 }
 
 // ------------------------------------------------------- single-CTA tiles --
-// 128 x 256 tiles, one CTA per SM (small M: the adaLN / embedding linears).
-template <bool FP8>
-__global__ void __launch_bounds__(kThreads, 1)
+// 128 x 256 tiles, one CTA per SM (small M: the adaLN / embedding linears).  Also the
+// weight-code kernel (KIND kKCodes), for every M: B arrives as 8-bit codes and warps 10-13
+// rewrite each stage's 256 x 64 codes as 16-bit values in shared memory.  That conversion
+// is repeated for every 128-row tile of A and its shared-memory traffic (1 byte read and 2
+// written per code) comes on top of the operand traffic of the tile, so it pays where one
+// tile of A covers M (the weight is read at 1 byte instead of 2 and no expansion kernel
+// runs); for M of a few thousand rows one expansion per call followed by the 16-bit
+// product is faster (measured: 4352 x 12288 x 2304 in 0.44 ms here against 0.21 ms), and
+// neither 256 x 128 single-CTA tiles (two M = 128 accumulators sharing the converted B)
+// nor CTA pairs (each CTA converting its half of B, handed to the even CTA's MMA issuer
+// through a cluster barrier) came near it: 0.31-0.51 ms.
+template <int KIND>
+__global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                 const __grid_constant__ CUtensorMap tmd, Args A) {
+  using L = Lay<KIND, false>;
+  constexpr bool FP8 = KIND == kKE4M3, CODES = KIND == kKCodes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Smem::bars);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::bars);
   uint64_t* full = bars;
-  uint64_t* empty = bars + kStages;
-  uint64_t* acc_full = bars + 2 * kStages;
+  uint64_t* empty = bars + L::stages;
+  uint64_t* acc_full = bars + 2 * L::stages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + Smem::misc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + Smem::misc + 8);
+  uint64_t* raw_full = drain + 1;  // weight-code kernels: A tile + B codes landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + L::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::misc + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   const int64_t mt = (A.M + BM - 1) / BM, nt = (A.N + BN - 1) / BN;
@@ -338,7 +470,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t nk = (A.K + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int s = 0; s < L::stages; ++s) {
+      mbar_init(full + s, CODES ? kConvWarps : 1);
+      mbar_init(empty + s, 1);
+      mbar_init(raw_full + s, 1);
+    }
     for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, kEpilogueWarps); }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -367,18 +503,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tma);
       prefetch_tmap(&tmb);
     }
+    // the barrier each stage's copies complete on: full, or raw_full when converters
+    // stand between the copies and the MMA
+    uint64_t* landed = CODES ? raw_full : full;
     int64_t g = 0;
     bool ok = true;
     for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       const int m0 = (int)((tile % mt) * BM), n0 = (int)((tile / mt) * BN);
       for (int64_t kb = 0; kb < nk; ++kb, ++g) {
-        const int s = (int)(g % kStages);
-        if (!wwait(empty + s, (uint32_t)(((g / kStages) & 1) ^ 1))) { ok = false; break; }
+        const int s = (int)(g % L::stages);
+        if (!wwait(empty + s, (uint32_t)(((g / L::stages) & 1) ^ 1))) { ok = false; break; }
         if (lane == 0) {
-          uint8_t* st = base + s * kStageBytes;
-          mbar_arrive_expect_tx(full + s, kStageBytes);
-          tma_load_2d(st, &tma, (int)(kb * bk), m0, full + s);
-          tma_load_2d(st + kABytes, &tmb, (int)(kb * bk), n0, full + s);
+          uint8_t* st = base + s * L::stage_bytes;
+          mbar_arrive_expect_tx(landed + s, CODES ? L::a_bytes + L::raw_bytes : L::stage_bytes);
+          tma_load_2d(st, &tma, (int)(kb * bk), m0, landed + s);
+          tma_load_2d(CODES ? base + L::raw + s * L::raw_bytes : st + L::a_bytes, &tmb, (int)(kb * bk), n0,
+                      landed + s);
         }
         __syncwarp();
       }
@@ -386,7 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok && lane == 0) {
       fail(kDevTimeoutProducer);
       // let issued copies land before the CTA's shared memory goes away
-      for (int64_t j = g > kStages ? g - kStages : 0; j < g; ++j) mbar_wait(full + (j % kStages), (j / kStages) & 1);
+      for (int64_t j = g > L::stages ? g - L::stages : 0; j < g; ++j)
+        mbar_wait(landed + (j % L::stages), (j / L::stages) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA --
@@ -395,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t fmt16 = A.f16 ? 0u : 1u;
     const uint32_t idesc = FP8 ? make_idesc(1, 0, 0, 0, 0, BM, BN) : make_idesc(1, fmt16, fmt16, 0, 0, BM, BN);
     const uint64_t d0 = sdesc_sw128_kmajor(smem_u32(base));
-    constexpr uint64_t kStageStep = kStageBytes >> 4, kBOff = kABytes >> 4;
+    constexpr uint64_t kStageStep = L::stage_bytes >> 4, kBOff = L::a_bytes >> 4;
     int64_t g = 0;
     int it = 0;
     bool ok = true;
@@ -405,8 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t dt = tmem + buf * BN;
       for (int64_t kb = 0; kb < nk; ++kb, ++g) {
-        const int s = (int)(g % kStages);
-        if (!wwait(full + s, (uint32_t)((g / kStages) & 1))) { ok = false; break; }
+        const int s = (int)(g % L::stages);
+        if (!wwait(full + s, (uint32_t)((g / L::stages) & 1))) { ok = false; break; }
         tc_fence_after();
         const uint64_t da = d0 + (uint64_t)s * kStageStep, db = da + kBOff;
         if (lane == 0) {
@@ -430,13 +571,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 2 + kEpilogueWarps) {
     // ------------------------------------------------------- epilogue --
     // 8 warps: lane quarter = warp & 3 (TMEM lanes / tile rows), column half = (warp - 2) / 4
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    Stager stg{base + Smem::staging + (warp - 2) * 4096, &tmd, 0, A.M, A.d_f16};
+    Stager stg{base + L::staging + (warp - 2) * 4096, &tmd, 0, A.M, A.d_f16};
     int it = 0;
     bool ok = true;
     for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
@@ -450,6 +591,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!ok && lane == 0) fail(kDevTimeoutEpilogue);
     if (lane == 0) bulk_wait_all();
+  } else if constexpr (CODES) {
+    // ----------------------------------------------------- converters --
+    constexpr int kChunks = L::raw_bytes / 16 / kConvThreads;
+    const ConvPlan<kChunks> plan(threadIdx.x - 32 * (2 + kEpilogueWarps), L::raw_bytes / 16);
+    bool ok = true;
+    with_code_format(A.b_fmt, A.f16 != 0, [&](auto fmt_c, auto f16_c) {
+      int64_t g = 0;
+      for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        for (int64_t kb = 0; kb < nk; ++kb, ++g) {
+          const int s = (int)(g % L::stages);
+          if (!wwait(raw_full + s, (uint32_t)((g / L::stages) & 1))) { ok = false; break; }
+          convert_codes_tile<kChunks, decltype(fmt_c)::value, decltype(f16_c)::value>(
+              base + L::raw + s * L::raw_bytes, base + s * L::stage_bytes + L::a_bytes, plan);
+          fence_async_smem();  // the generic-proxy writes, before the MMA reads them
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full + s);
+        }
+      }
+    });
+    if (!ok && lane == 0) fail(kDevTimeoutConvert);
   }
 
   tc_fence_before();
@@ -471,32 +632,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   empty[s]     on each CTA: arrived by the even CTA's MMA commit
 //   acc_full[b]  on each CTA: arrived by the even CTA's MMA commit
 //   acc_empty[b] on the even CTA: 8 epilogue warps of each CTA (16 arrivals)
-namespace pair {
-constexpr int kStages = 6;
-constexpr int kABytes = 128 * 128;   // this CTA's 128 rows x 128 bytes of K
-constexpr int kBBytes = 128 * 128;   // this CTA's half of the 256 B rows
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int staging = kStages * kStageBytes;
-constexpr int bars = staging + kStagingBytes;
-constexpr int nbars = 2 * kStages + 4 + 1;
-constexpr int misc = bars + nbars * 8;
-constexpr int alloc = misc + 64 + 1024;
-}  // namespace pair
-
-template <bool FP8>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int KIND>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Lay<KIND, true>::threads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                      const __grid_constant__ CUtensorMap tmd, Args A) {
+  static_assert(KIND != kKCodes, "weight codes run on the single-CTA gemm_kernel");
+  using L = Lay<KIND, true>;
+  constexpr bool FP8 = KIND == kKE4M3;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars_p = reinterpret_cast<uint64_t*>(base + pair::bars);
+  uint64_t* bars_p = reinterpret_cast<uint64_t*>(base + L::bars);
   uint64_t* full = bars_p;
-  uint64_t* empty = bars_p + pair::kStages;
-  uint64_t* acc_full = bars_p + 2 * pair::kStages;
+  uint64_t* empty = bars_p + L::stages;
+  uint64_t* acc_full = bars_p + 2 * L::stages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + pair::misc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + pair::misc + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + L::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::misc + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
@@ -510,7 +662,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int64_t nk = (A.K + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < pair::kStages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    // full[s] of the even CTA completes on its expect_tx and the TMA bytes of both CTAs
+    for (int s = 0; s < L::stages; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, 2 * kEpilogueWarps); }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -532,26 +685,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const bool w = mbar_wait(bar, parity) && (*abort_flag == 0);
     return __all_sync(0xffffffffu, w);
   };
-
   if (warp == 0) {
     // --------------------------------------------- producer (both CTAs) --
+    const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // the even CTA's full[0]
     if (lane == 0) {
       prefetch_tmap(&tma);
       prefetch_tmap(&tmb);
     }
-    const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // the even CTA's full[0]
     int64_t g = 0;
     bool ok = true;
     for (int64_t tile = cid; ok && tile < ntiles; tile += ncl) {
       const int m0 = (int)((tile % mt) * (2 * BM) + rank * BM), n0 = (int)((tile / mt) * bn + rank * (bn / 2));
       for (int64_t kb = 0; kb < nk; ++kb, ++g) {
-        const int s = (int)(g % pair::kStages);
-        if (!wwait(empty + s, (uint32_t)(((g / pair::kStages) & 1) ^ 1))) { ok = false; break; }
+        const int s = (int)(g % L::stages);
+        if (!wwait(empty + s, (uint32_t)(((g / L::stages) & 1) ^ 1))) { ok = false; break; }
         if (lane == 0) {
-          uint8_t* st = base + s * pair::kStageBytes;
-          if (leader) mbar_arrive_expect_tx(full + s, 2 * (pair::kABytes + (bn / 2) * 128));
+          uint8_t* st = base + s * L::stage_bytes;
+          if (leader) mbar_arrive_expect_tx(full + s, 2 * (L::a_bytes + (bn / 2) * 128));
           tma_load_2d_pair(st, &tma, (int)(kb * bk), m0, full0 + s * 8);
-          tma_load_2d_pair(st + pair::kABytes, &tmb, (int)(kb * bk), n0, full0 + s * 8);
+          tma_load_2d_pair(st + L::a_bytes, &tmb, (int)(kb * bk), n0, full0 + s * 8);
         }
         __syncwarp();
       }
@@ -559,7 +711,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (!ok && lane == 0) {
       fail(kDevTimeoutProducer);
       if (leader)
-        for (int64_t j = g > pair::kStages ? g - pair::kStages : 0; j < g; ++j) mbar_wait(full + (j % pair::kStages), (j / pair::kStages) & 1);
+        for (int64_t j = g > L::stages ? g - L::stages : 0; j < g; ++j)
+          mbar_wait(full + (j % L::stages), (j / L::stages) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA (even CTA) --
@@ -568,7 +721,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t idesc = FP8 ? make_idesc(1, 0, 0, 0, 0, 2 * BM, bn)
                                  : make_idesc(1, fmt16, fmt16, 0, 0, 2 * BM, bn);
       const uint64_t d0 = sdesc_sw128_kmajor(smem_u32(base));
-      constexpr uint64_t kStageStep = pair::kStageBytes >> 4, kBOff = pair::kABytes >> 4;
+      constexpr uint64_t kStageStep = L::stage_bytes >> 4, kBOff = L::a_bytes >> 4;
       const uint32_t empty_own = smem_u32(empty), empty_peer = mapa_shared(smem_u32(empty), peer);
       const uint32_t accf_own = smem_u32(acc_full), accf_peer = mapa_shared(smem_u32(acc_full), peer);
       int64_t g = 0;
@@ -580,8 +733,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t dt = tmem + buf * BN;
         for (int64_t kb = 0; kb < nk; ++kb, ++g) {
-          const int s = (int)(g % pair::kStages);
-          if (!wwait(full + s, (uint32_t)((g / pair::kStages) & 1))) { ok = false; break; }
+          const int s = (int)(g % L::stages);
+          if (!wwait(full + s, (uint32_t)((g / L::stages) & 1))) { ok = false; break; }
           tc_fence_after();
           const uint64_t da = d0 + (uint64_t)s * kStageStep, db = da + kBOff;
           if (lane == 0) {
@@ -616,7 +769,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t acce0 = mapa_shared(smem_u32(acc_empty), 0);
-    Stager stg{base + pair::staging + (warp - 2) * 4096, &tmd, 0, A.M, A.d_f16};
+    Stager stg{base + L::staging + (warp - 2) * 4096, &tmd, 0, A.M, A.d_f16};
     int it = 0;
     bool ok = true;
     for (int64_t tile = cid; ok && tile < ntiles; tile += ncl, ++it) {
@@ -644,16 +797,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
-template <typename K>
-static cudaError_t pair_clusters(K* kern, int* out);
+template <typename Kern>
+static cudaError_t pair_clusters(Kern* kern, int threads, int smem, std::atomic<int>* cache, int* out);
 
-// Shared-memory attribute of the pair kernel (per device) and the resident pair count.
-static cudaError_t pair_setup(bool fp8, int* clusters) {
-  static std::atomic<uint64_t> attr{0}, attr8{0};
-  auto kern = fp8 ? gemm_pair_kernel<true> : gemm_pair_kernel<false>;
-  cudaError_t e = qf2_set_smem_once(kern, pair::alloc, fp8 ? &attr8 : &attr);
+template <int KIND>
+static cudaError_t pair_setup_kind(int* clusters) {
+  static std::atomic<uint64_t> attr{0};
+  static std::atomic<int> cache[64];
+  cudaError_t e = qf2_set_smem_once(gemm_pair_kernel<KIND>, Lay<KIND, true>::alloc, &attr);
   if (e != cudaSuccess) return e;
-  return pair_clusters(kern, clusters);
+  return pair_clusters(gemm_pair_kernel<KIND>, Lay<KIND, true>::threads, Lay<KIND, true>::alloc, cache, clusters);
+}
+
+// Shared-memory attribute of a CTA-pair kernel (per device) and its resident pair count.
+static cudaError_t pair_setup(int kind, int* clusters) {
+  return kind == kKE4M3 ? pair_setup_kind<kKE4M3>(clusters) : pair_setup_kind<kK16>(clusters);
 }
 
 // Tile width of the CTA-pair kernel: among 256 / 192 / 128 the one with the least
@@ -677,9 +835,8 @@ static int pick_bn(int64_t M, int64_t N, int clusters) {
 
 // How many CTA pairs of gemm_pair_kernel are resident at once on the current device
 // (the persistent grid's size), cached per device.  Needs the smem attribute set.
-template <typename K>
-static cudaError_t pair_clusters(K* kern, int* out) {
-  static std::atomic<int> cache[64];
+template <typename Kern>
+static cudaError_t pair_clusters(Kern* kern, int threads, int smem, std::atomic<int>* cache, int* out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -687,8 +844,8 @@ static cudaError_t pair_clusters(K* kern, int* out) {
   if (v == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = pair::alloc;
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
     e = cudaOccupancyMaxActiveClusters(&v, kern, &cfg);
     if (e != cudaSuccess) return e;
     if (v <= 0) return cudaErrorInvalidConfiguration;
@@ -703,14 +860,17 @@ static cudaError_t pair_clusters(K* kern, int* out) {
 
 using namespace qf2::gemm;
 
+// ab_dtype: the operands' type (A's, and B's unless b_codes); b_codes: 0, or QF2_I8 /
+// QF2_E4M3 when B holds 8-bit weight codes that the kernel converts to ab_dtype (16-bit).
 static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd, int64_t M, int64_t N,
                     int64_t K, int ab_dtype, int d_dtype, const float* row_scale, const float* col_scale,
                     const void* bias, int bias_dtype, int64_t gelu_col0, int glu, const void* residual, int64_t ldr,
                     const void* gate, int64_t gate_stride, int64_t rows_per_gate, const int64_t* row_idx,
                     int64_t idx_rows, int64_t out_rows, void* workspace, int64_t workspace_bytes,
-                    qf2_stream_t stream) {
+                    qf2_stream_t stream, int b_codes = 0) {
   if (!a || !b || !d) return QF2_ERR_ARG;
   if (ab_dtype != QF2_BF16 && ab_dtype != QF2_F16 && ab_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
+  if (b_codes && ((b_codes != QF2_I8 && b_codes != QF2_E4M3) || ab_dtype == QF2_E4M3)) return QF2_ERR_DTYPE;
   if (d_dtype != QF2_BF16 && d_dtype != QF2_F16 && d_dtype != QF2_F32) return QF2_ERR_DTYPE;
   // the fused residual / SwiGLU epilogues read and write bf16 only
   if (d_dtype == QF2_F16 && (residual || glu)) return QF2_ERR_DTYPE;
@@ -718,10 +878,11 @@ static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void
   if (M <= 0 || N <= 0 || K <= 0 || (N % 8)) return QF2_ERR_SHAPE;
   if (residual && (ldr < N || (gate && rows_per_gate <= 0))) return QF2_ERR_SHAPE;
   if (glu && (N % BN || residual || gelu_col0 >= 0 || d_dtype != QF2_BF16)) return QF2_ERR_SHAPE;
-  const int esz = ab_dtype == QF2_E4M3 ? 1 : 2;
-  if (!al16(a) || !al16(b) || !al16(d) || (lda * esz) % 16 || (ldb * esz) % 16 || (ldd % 8) || lda < K || ldb < K ||
+  const int esz = ab_dtype == QF2_E4M3 ? 1 : 2, bsz = b_codes ? 1 : esz;
+  if (!al16(a) || !al16(b) || !al16(d) || (lda * esz) % 16 || (ldb * bsz) % 16 || (ldd % 8) || lda < K || ldb < K ||
       ldd < (glu ? N / 2 : N))
     return QF2_ERR_ALIGN;
+  const int kind = ab_dtype == QF2_E4M3 ? kKE4M3 : b_codes ? kKCodes : kK16;
   if (!workspace || workspace_bytes < 256 || !al16(workspace)) return QF2_ERR_WORKSPACE;
   const CUtensorMapDataType tdt = ab_dtype == QF2_E4M3  ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                   : ab_dtype == QF2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -729,18 +890,21 @@ static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void
   const uint32_t bk = ab_dtype == QF2_E4M3 ? 128 : 64;
   // CTA pairs (256-row tiles) once there are two 128-row tiles of A; single CTAs for the
   // thin products (adaLN / embedding linears on a few rows)
-  const bool use_pair = M > BM;
+  // weight codes always run on single-CTA tiles (see gemm_kernel)
+  const bool use_pair = M > BM && kind != kKCodes;
   CUtensorMap ma, mb;
   const uint64_t da[2] = {(uint64_t)K, (uint64_t)M}, db[2] = {(uint64_t)K, (uint64_t)N};
   int clusters = 0, bn = BN;
   if (use_pair) {
-    QF2_CUDA_CHECK(pair_setup(ab_dtype == QF2_E4M3, &clusters));
+    QF2_CUDA_CHECK(pair_setup(kind, &clusters));
     if (!glu) bn = pick_bn(M, N, clusters);
   }
-  const uint32_t ba[2] = {bk, (uint32_t)BM}, bb[2] = {bk, (uint32_t)(use_pair ? bn / 2 : BN)};
-  if (!qf2_make_tmap_2d(&ma, tdt, a, da, (uint64_t)lda * esz, ba) ||
-      !qf2_make_tmap_2d(&mb, tdt, b, db, (uint64_t)ldb * esz, bb))
-    return QF2_ERR_ALIGN;
+  const uint32_t ba[2] = {bk, (uint32_t)BM},
+                 bb[2] = {bk, (uint32_t)(use_pair ? bn / 2 : BN)};
+  // weight codes: bk bytes of K per row, unswizzled (the converters rewrite them)
+  const bool bmap_ok = b_codes ? qf2_make_tmap_2d_noswizzle(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, db, (uint64_t)ldb, bb)
+                               : qf2_make_tmap_2d(&mb, tdt, b, db, (uint64_t)ldb * esz, bb);
+  if (!qf2_make_tmap_2d(&ma, tdt, a, da, (uint64_t)lda * esz, ba) || !bmap_ok) return QF2_ERR_ALIGN;
   // 16-bit output goes out through 32 x 32 TMA stores; the fp32 output map is never used
   CUtensorMap md;
   const uint64_t dd[2] = {(uint64_t)(glu ? N / 2 : N), (uint64_t)M};
@@ -762,6 +926,7 @@ static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void
   args.d_f16 = d_dtype == QF2_F16;
   args.fp8 = ab_dtype == QF2_E4M3;
   args.f16 = ab_dtype == QF2_F16;
+  args.b_fmt = b_codes;
   args.gelu_col0 = gelu_col0 < 0 ? INT64_MAX : gelu_col0;
   args.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
   args.ldr = ldr;
@@ -780,19 +945,28 @@ static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   QF2_CUDA_CHECK(cudaMemsetAsync(workspace, 0, sizeof(int), s));
   if (use_pair) {
-    auto kern = args.fp8 ? gemm_pair_kernel<true> : gemm_pair_kernel<false>;
     const int64_t ntiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + bn - 1) / bn);
     const unsigned grid = 2 * (unsigned)std::min<int64_t>(ntiles, clusters);
-    kern<<<grid, kThreads, pair::alloc, s>>>(ma, mb, md, args);
+    if (kind == kKE4M3)
+      gemm_pair_kernel<kKE4M3><<<grid, Lay<kKE4M3, true>::threads, Lay<kKE4M3, true>::alloc, s>>>(ma, mb, md, args);
+    else
+      gemm_pair_kernel<kK16><<<grid, Lay<kK16, true>::threads, Lay<kK16, true>::alloc, s>>>(ma, mb, md, args);
   } else {
-    static std::atomic<uint64_t> attr_done{0}, attr_done8{0};
-    auto kern = args.fp8 ? gemm_kernel<true> : gemm_kernel<false>;
-    QF2_CUDA_CHECK(qf2_set_smem_once(kern, Smem::alloc, args.fp8 ? &attr_done8 : &attr_done));
+    static std::atomic<uint64_t> attr_done[3];
     int sms = 148;
     QF2_CUDA_CHECK(qf2_sm_count(&sms));
     const int64_t ntiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms);
-    kern<<<grid, kThreads, Smem::alloc, s>>>(ma, mb, md, args);
+    if (kind == kKE4M3) {
+      QF2_CUDA_CHECK(qf2_set_smem_once(gemm_kernel<kKE4M3>, Lay<kKE4M3, false>::alloc, &attr_done[kind]));
+      gemm_kernel<kKE4M3><<<grid, Lay<kKE4M3, false>::threads, Lay<kKE4M3, false>::alloc, s>>>(ma, mb, md, args);
+    } else if (kind == kKCodes) {
+      QF2_CUDA_CHECK(qf2_set_smem_once(gemm_kernel<kKCodes>, Lay<kKCodes, false>::alloc, &attr_done[kind]));
+      gemm_kernel<kKCodes><<<grid, Lay<kKCodes, false>::threads, Lay<kKCodes, false>::alloc, s>>>(ma, mb, md, args);
+    } else {
+      QF2_CUDA_CHECK(qf2_set_smem_once(gemm_kernel<kK16>, Lay<kK16, false>::alloc, &attr_done[kind]));
+      gemm_kernel<kK16><<<grid, Lay<kK16, false>::threads, Lay<kK16, false>::alloc, s>>>(ma, mb, md, args);
+    }
   }
   QF2_LAUNCH_CHECK();
   return QF2_OK;
@@ -806,6 +980,19 @@ extern "C" int qf2_gemm_ex(const void* a, int64_t lda, const void* b, int64_t ld
   return gemm_run(a, lda, b, ldb, d, ldd, M, N, K, ab_dtype, d_dtype, row_scale, col_scale, bias, bias_dtype, gelu_col0,
                   glu, residual, ldr, gate, gate_stride, rows_per_gate, nullptr, 0, 0, workspace, workspace_bytes,
                   stream);
+}
+
+extern "C" int qf2_gemm_codes(const void* a, int64_t lda, const void* b_codes, int64_t ldb, int b_dtype, void* d,
+                              int64_t ldd, int64_t M, int64_t N, int64_t K, int a_dtype, int d_dtype,
+                              const float* row_scale, const float* col_scale, const void* bias, int bias_dtype,
+                              int64_t gelu_col0, int glu, const void* residual, int64_t ldr, const void* gate,
+                              int64_t gate_stride, int64_t rows_per_gate, void* workspace, int64_t workspace_bytes,
+                              qf2_stream_t stream) {
+  if (a_dtype != QF2_BF16 && a_dtype != QF2_F16) return QF2_ERR_DTYPE;
+  if (b_dtype != QF2_I8 && b_dtype != QF2_E4M3) return QF2_ERR_DTYPE;
+  return gemm_run(a, lda, b_codes, ldb, d, ldd, M, N, K, a_dtype, d_dtype, row_scale, col_scale, bias, bias_dtype,
+                  gelu_col0, glu, residual, ldr, gate, gate_stride, rows_per_gate, nullptr, 0, 0, workspace,
+                  workspace_bytes, stream, b_dtype);
 }
 
 extern "C" int qf2_gemm_rows_indexed(const void* a, int64_t lda, const void* b, int64_t ldb, void* d, int64_t ldd,

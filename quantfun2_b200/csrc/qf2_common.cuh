@@ -38,6 +38,7 @@ enum : int {
   kDevTimeoutEpilogue = 4,
   kDevBadLaunch = 5,
   kDevBadIndex = 6,   // an index argument outside its range (the access was skipped)
+  kDevTimeoutConvert = 7,
 };
 
 // ~2 s at 1.9 GHz; each wait gives up after this many SM clocks.
@@ -290,6 +291,7 @@ QF2_DEV void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+
 // ----------------------------------------------------------------- tcgen05 --
 QF2_DEV void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
@@ -411,6 +413,7 @@ QF2_DEV void tmem_fill8(uint32_t taddr, uint32_t v) {
                : "memory");
 }
 
+
 QF2_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 QF2_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -511,6 +514,8 @@ bool qf2_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* b
                       uint64_t stride_bytes, const uint32_t box[2]);
 
 // Same, 2-D with 64-byte swizzle (output staging tiles of 64-byte rows).
+bool qf2_make_tmap_2d_noswizzle(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
+                                uint64_t stride_bytes, const uint32_t box[2]);
 bool qf2_make_tmap_2d_sw64(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[2],
                            uint64_t stride_bytes, const uint32_t box[2]);
 

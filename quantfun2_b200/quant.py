@@ -100,9 +100,11 @@ def codes_to_bf16(q: torch.Tensor, fmt: str) -> torch.Tensor:
 def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=None, fp8: bool = False,
          out_dtype=torch.bfloat16, out: torch.Tensor | None = None, gelu_col0: int = -1,
          residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, rows_per_gate: int = 1,
-         glu: bool = False) -> torch.Tensor:
+         glu: bool = False, codes: str | None = None) -> torch.Tensor:
     """D = (a . b^T) * row_scale[:, None] * col_scale[None, :] + bias on tcgen05.
-    a [M, K], b [N, K]: both bf16, both fp16, or uint8 e4m3 codes with fp8=True.
+    a [M, K], b [N, K]: both bf16, both fp16, or uint8 e4m3 codes with fp8=True; with
+    codes="int8" / "e4m3", b holds 8-bit weight codes (int8 / uint8 e4m3, K % 16 == 0) that
+    the kernel turns into a's 16-bit type in shared memory (exact), for weight-only linears.
     out_dtype bf16, fp16 or fp32 (fused residual / SwiGLU: bf16).
     Fused epilogue: GELU (tanh) on columns >= gelu_col0; D = residual + gate * D when
     residual is given (gate [rows/rows_per_gate, N] bf16, may be a strided view); with
@@ -114,7 +116,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
     N = b.shape[0]
     if b.shape[1] != K:
         raise QF2Error("inner dimensions differ")
-    if not fp8 and (a.dtype not in (torch.bfloat16, torch.float16) or b.dtype != a.dtype):
+    if codes is not None:
+        if codes not in ("int8", "e4m3") or fp8 or a.dtype not in (torch.bfloat16, torch.float16):
+            raise QF2Error("weight codes need a bf16 or fp16 activation operand")
+        if b.dtype != (torch.int8 if codes == "int8" else torch.uint8):
+            raise QF2Error("int8 codes are torch.int8, e4m3 codes torch.uint8")
+    elif not fp8 and (a.dtype not in (torch.bfloat16, torch.float16) or b.dtype != a.dtype):
         raise QF2Error("16-bit GEMM operands must both be bf16 or both fp16")
     if a.stride(-1) != 1:
         a = a.contiguous()
@@ -136,17 +143,34 @@ def gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=
         if bias.dtype not in (torch.bfloat16, torch.float32):
             bias = bias.float()
     ws = _ws(a.device)
+    tail = (row_scale.data_ptr() if row_scale is not None else None,
+            col_scale.data_ptr() if col_scale is not None else None,
+            bias.data_ptr() if bias is not None else None, bias_dt, int(gelu_col0), int(bool(glu)),
+            residual.data_ptr() if residual is not None else None, residual.stride(0) if residual is not None else 0,
+            gate.data_ptr() if gate is not None else None, gate.stride(0) if gate is not None else 0,
+            int(rows_per_gate), ws.data_ptr(), 256, stream_ptr(a.device))
+    if codes is not None:
+        check(_lib.load().qf2_gemm_codes(
+            a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), _lib.QF2_I8 if codes == "int8" else _lib.QF2_E4M3,
+            out.data_ptr(), out.stride(0), M, N, K, _lib.dtype_code(a.dtype), _lib.dtype_code(out_dtype), *tail),
+            "qf2_gemm_codes")
+        return out
     check(_lib.load().qf2_gemm_ex(
         a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), out.data_ptr(), out.stride(0), M, N, K,
-        _lib.QF2_E4M3 if fp8 else _lib.dtype_code(a.dtype), _lib.dtype_code(out_dtype),
-        row_scale.data_ptr() if row_scale is not None else None,
-        col_scale.data_ptr() if col_scale is not None else None,
-        bias.data_ptr() if bias is not None else None, bias_dt, int(gelu_col0), int(bool(glu)),
-        residual.data_ptr() if residual is not None else None, residual.stride(0) if residual is not None else 0,
-        gate.data_ptr() if gate is not None else None, gate.stride(0) if gate is not None else 0,
-        int(rows_per_gate), ws.data_ptr(), 256, stream_ptr(a.device)),
+        _lib.QF2_E4M3 if fp8 else _lib.dtype_code(a.dtype), _lib.dtype_code(out_dtype), *tail),
         "qf2_gemm_ex")
     return out
+
+
+def _weight_only(a: torch.Tensor, codes: torch.Tensor, fmt: str, scale, bias, **epilogue) -> torch.Tensor:
+    """Weight-only linear on 8-bit codes: y = (a . fmt(codes)^T) * scale + bias in a's dtype.
+    Up to 128 rows the codes go straight into the GEMM (converted in shared memory, one
+    128-row tile of a); above that one expansion to a's dtype and the 16-bit GEMM are
+    faster, since the in-GEMM conversion would repeat for every 128-row tile."""
+    if a.shape[0] <= 128:
+        return gemm(a, codes, col_scale=scale, bias=bias, out_dtype=a.dtype, codes=fmt, **epilogue)
+    w = codes_to_bf16(codes, fmt) if a.dtype == torch.bfloat16 else codes_to(codes, fmt, a.dtype)
+    return gemm(a, w, col_scale=scale, bias=bias, out_dtype=a.dtype, **epilogue)
 
 
 def glu_interleave(w1: torch.Tensor, w3: torch.Tensor) -> torch.Tensor:
@@ -232,9 +256,8 @@ class QLinear(nn.Module):
         if self.fp8_activations:
             return gemm(a, self.codes, row_scale=row_scale, col_scale=self.scale, bias=self.bias, fp8=True,
                         out_dtype=out_dtype, **epilogue)
-        fmt = "int8" if self.mode == "int8" else "e4m3"
-        wb = codes_to_bf16(self.codes, fmt) if a.dtype == torch.bfloat16 else codes_to(self.codes, fmt, a.dtype)
-        return gemm(a, wb, col_scale=self.scale, bias=self.bias, out_dtype=a.dtype, **epilogue)
+        return _weight_only(a, self.codes, "int8" if self.mode == "int8" else "e4m3", self.scale, self.bias,
+                            **epilogue)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
@@ -289,9 +312,8 @@ class QuantizedWeight(torch.Tensor):
             xc, xs = quantize_rows(x2, "e4m3")
             y = gemm(xc, self.codes, row_scale=xs, col_scale=self.scale, bias=b, fp8=True, out_dtype=x.dtype)
         else:
-            wv = codes_to(self.codes, "int8" if self.mode == "int8" else "e4m3", x.dtype)
-            y = gemm(x2.contiguous() if x2.stride(-1) != 1 else x2, wv, col_scale=self.scale, bias=b,
-                     out_dtype=x.dtype)
+            y = _weight_only(x2.contiguous() if x2.stride(-1) != 1 else x2, self.codes,
+                             "int8" if self.mode == "int8" else "e4m3", self.scale, b)
         return y.reshape(*x.shape[:-1], N)
 
     @classmethod

@@ -112,6 +112,65 @@ def test_gemm_pair_tile_widths(cuda, n, fp8):
     assert rel_err(d.float().cpu(), ref.cpu()) < 8e-3
 
 
+def _random_codes(fmt, n, k, device, seed):
+    g = torch.Generator().manual_seed(seed)
+    if fmt == "int8":
+        q = torch.randint(-128, 128, (n, k), generator=g, dtype=torch.int8)
+        q[0, :4] = torch.tensor([-128, 127, 0, -1], dtype=torch.int8)
+    else:
+        q = torch.randint(0, 256, (n, k), generator=g, dtype=torch.int32).to(torch.uint8)
+        q[(q & 0x7F) == 0x7F] = 0   # no NaN codes
+        q[0, :6] = torch.tensor([0x7E, 0xFE, 0x01, 0x81, 0x08, 0x80], dtype=torch.uint8)  # +-448, subnormals, -0
+    return q.to(device)
+
+
+@pytest.mark.parametrize("fmt", ["int8", "e4m3"])
+@pytest.mark.parametrize("act", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("mnk", [(1, 9216, 1024), (100, 776, 272), (300, 2304, 2304), (4392, 1000, 384),
+                                 (4352, 2304, 2304)])
+def test_gemm_codes_bit_exact_vs_converted(cuda, fmt, act, mnk):
+    """Weight-code GEMM (codes converted to 16-bit in shared memory) against the 16-bit
+    GEMM on the same codes converted beforehand: bit for bit, on the single-CTA (M <= 128)
+    and CTA-pair kernels, ragged N and K tails, every code class (int8 extremes, e4m3
+    +-448, subnormals, -0)."""
+    from quantfun2_b200.quant import codes_to, gemm
+
+    M, N, K = mnk
+    g = torch.Generator(device=cuda).manual_seed(M + N)
+    x = torch.randn(M, K, device=cuda, generator=g).to(act)
+    q = _random_codes(fmt, N, K, cuda, N)
+    sc = torch.rand(N, device=cuda, generator=g) * 0.01
+    bias = torch.randn(N, device=cuda, generator=g).bfloat16()
+    d = gemm(x, q, col_scale=sc, bias=bias, out_dtype=act, codes=fmt)
+    ref = gemm(x, codes_to(q, fmt, act), col_scale=sc, bias=bias, out_dtype=act)
+    assert torch.equal(d.view(torch.int16), ref.view(torch.int16))
+    wf = codes_to(q, fmt, act).float()
+    exact = (x.double() @ wf.double().T) * sc.double() + bias.double()
+    assert rel_err(d.float().cpu(), exact.cpu()) < 1e-2
+
+
+@pytest.mark.parametrize("fmt", ["int8", "e4m3"])
+def test_gemm_codes_fused_epilogues(cuda, fmt):
+    """The DiT epilogues on the weight-code kernel: SwiGLU (interleaved w1 / w3 codes) and
+    GELU + gated residual in place, bit for bit against the converted-weight GEMM."""
+    from quantfun2_b200.quant import codes_to, gemm
+
+    g = torch.Generator(device=cuda).manual_seed(5)
+    M, N, K, L = 600, 1024, 512, 300
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    q = _random_codes(fmt, N, K, cuda, 11)
+    sc = torch.rand(N, device=cuda, generator=g) * 0.01
+    wb = codes_to(q, fmt, torch.bfloat16)
+    d = gemm(x, q, col_scale=sc, glu=True, codes=fmt)
+    assert torch.equal(d.view(torch.int16), gemm(x, wb, col_scale=sc, glu=True).view(torch.int16))
+    res = torch.randn(M, N, device=cuda, generator=g).bfloat16()
+    gate = torch.randn(2, N, device=cuda, generator=g).bfloat16()
+    o1, o2 = res.clone(), res.clone()
+    gemm(x, q, col_scale=sc, gelu_col0=100, residual=o1, gate=gate, rows_per_gate=L, out=o1, codes=fmt)
+    gemm(x, wb, col_scale=sc, gelu_col0=100, residual=o2, gate=gate, rows_per_gate=L, out=o2)
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+
+
 @pytest.mark.parametrize("mnk", [(128, 256, 128), (300, 776, 272), (4608, 3072, 3072)])
 def test_gemm_e4m3(cuda, mnk):
     from quantfun2_b200.quant import gemm, quantize_rows
