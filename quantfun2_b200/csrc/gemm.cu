@@ -49,6 +49,9 @@ struct Lay {
   static_assert(!(PAIR && KIND == kKCodes), "weight codes run on the single-CTA gemm_kernel");
   static constexpr bool codes = KIND == kKCodes;
   static constexpr int stages = PAIR ? 6 : (codes ? 3 : 4);
+  // the single-CTA 16-bit / e4m3 kernel also runs 128- and 64-column tiles (thin
+  // products), whose smaller stages fit up to 6 and 8 times into the same region
+  static constexpr int max_stages = (PAIR || codes) ? stages : 8;
   static constexpr int a_bytes = BM * 128;
   static constexpr int b_rows = PAIR ? 128 : BN;
   static constexpr int b_bytes = b_rows * 128;
@@ -58,7 +61,7 @@ struct Lay {
   static constexpr int staging = raw + stages * raw_bytes;
   static constexpr int bars = staging + kStagingBytes;
   // full, empty, raw_full per stage; acc_full, acc_empty per accumulator; drain
-  static constexpr int nbars = 3 * stages + 4 + 1;
+  static constexpr int nbars = 3 * max_stages + 4 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int alloc = misc + 64 + 1024;
   static constexpr int threads = codes ? kThreads + kConvThreads : kThreads;
@@ -455,8 +458,8 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::bars);
   uint64_t* full = bars;
-  uint64_t* empty = bars + L::stages;
-  uint64_t* acc_full = bars + 2 * L::stages;
+  uint64_t* empty = bars + L::max_stages;
+  uint64_t* acc_full = bars + 2 * L::max_stages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint64_t* raw_full = drain + 1;  // weight-code kernels: A tile + B codes landed
@@ -464,13 +467,17 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::misc + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int64_t mt = (A.M + BM - 1) / BM, nt = (A.N + BN - 1) / BN;
+  // tile width (256, or 128 / 64 for thin products) and the stages that fit at that width
+  const int bn = CODES ? BN : A.bn;
+  const int sbytes = L::a_bytes + bn * 128;
+  const int ns = CODES ? L::stages : min(L::max_stages, L::raw / sbytes);
+  const int64_t mt = (A.M + BM - 1) / BM, nt = (A.N + bn - 1) / bn;
   const int64_t ntiles = mt * nt;
   constexpr int bk = FP8 ? 128 : 64;  // K elements per stage (128 bytes)
   const int64_t nk = (A.K + bk - 1) / bk;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < L::stages; ++s) {
+    for (int s = 0; s < ns; ++s) {
       mbar_init(full + s, CODES ? kConvWarps : 1);
       mbar_init(empty + s, 1);
       mbar_init(raw_full + s, 1);
@@ -509,13 +516,13 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
     int64_t g = 0;
     bool ok = true;
     for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-      const int m0 = (int)((tile % mt) * BM), n0 = (int)((tile / mt) * BN);
+      const int m0 = (int)((tile % mt) * BM), n0 = (int)((tile / mt) * bn);
       for (int64_t kb = 0; kb < nk; ++kb, ++g) {
-        const int s = (int)(g % L::stages);
-        if (!wwait(empty + s, (uint32_t)(((g / L::stages) & 1) ^ 1))) { ok = false; break; }
+        const int s = (int)(g % ns);
+        if (!wwait(empty + s, (uint32_t)(((g / ns) & 1) ^ 1))) { ok = false; break; }
         if (lane == 0) {
-          uint8_t* st = base + s * L::stage_bytes;
-          mbar_arrive_expect_tx(landed + s, CODES ? L::a_bytes + L::raw_bytes : L::stage_bytes);
+          uint8_t* st = base + s * sbytes;
+          mbar_arrive_expect_tx(landed + s, CODES ? L::a_bytes + L::raw_bytes : sbytes);
           tma_load_2d(st, &tma, (int)(kb * bk), m0, landed + s);
           tma_load_2d(CODES ? base + L::raw + s * L::raw_bytes : st + L::a_bytes, &tmb, (int)(kb * bk), n0,
                       landed + s);
@@ -526,17 +533,17 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
     if (!ok && lane == 0) {
       fail(kDevTimeoutProducer);
       // let issued copies land before the CTA's shared memory goes away
-      for (int64_t j = g > L::stages ? g - L::stages : 0; j < g; ++j)
-        mbar_wait(landed + (j % L::stages), (j / L::stages) & 1);
+      for (int64_t j = g > ns ? g - ns : 0; j < g; ++j) mbar_wait(landed + (j % ns), (j / ns) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA --
     // e4m3 x e4m3, bf16 x bf16 or fp16 x fp16 -> f32 (the 16-bit format is a descriptor
     // field, not a branch between the MMAs)
     const uint32_t fmt16 = A.f16 ? 0u : 1u;
-    const uint32_t idesc = FP8 ? make_idesc(1, 0, 0, 0, 0, BM, BN) : make_idesc(1, fmt16, fmt16, 0, 0, BM, BN);
+    const uint32_t idesc = FP8 ? make_idesc(1, 0, 0, 0, 0, BM, bn) : make_idesc(1, fmt16, fmt16, 0, 0, BM, bn);
     const uint64_t d0 = sdesc_sw128_kmajor(smem_u32(base));
-    constexpr uint64_t kStageStep = L::stage_bytes >> 4, kBOff = L::a_bytes >> 4;
+    const uint64_t kStageStep = (uint64_t)(sbytes >> 4);
+    constexpr uint64_t kBOff = L::a_bytes >> 4;
     int64_t g = 0;
     int it = 0;
     bool ok = true;
@@ -546,8 +553,8 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
       tc_fence_after();
       const uint32_t dt = tmem + buf * BN;
       for (int64_t kb = 0; kb < nk; ++kb, ++g) {
-        const int s = (int)(g % L::stages);
-        if (!wwait(full + s, (uint32_t)((g / L::stages) & 1))) { ok = false; break; }
+        const int s = (int)(g % ns);
+        if (!wwait(full + s, (uint32_t)((g / ns) & 1))) { ok = false; break; }
         tc_fence_after();
         const uint64_t da = d0 + (uint64_t)s * kStageStep, db = da + kBOff;
         if (lane == 0) {
@@ -584,7 +591,7 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
       const int buf = it & 1;
       if (!wwait(acc_full + buf, (uint32_t)((it >> 1) & 1))) { ok = false; break; }
       tc_fence_after();
-      epilogue_tile(A, stg, tmem + lane_off + buf * BN, (tile % mt) * BM + quarter * 32, (tile / mt) * BN, half);
+      epilogue_tile(A, stg, tmem + lane_off + buf * BN, (tile % mt) * BM + quarter * 32, (tile / mt) * bn, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + buf);
@@ -833,6 +840,25 @@ static int pick_bn(int64_t M, int64_t N, int clusters) {
   return best;
 }
 
+// Tile width of the single-CTA kernel for products of at most 128 rows: 256, 128 or 64
+// columns, the one with the least estimated time = rounds of the one-CTA-per-SM grid x
+// the bytes a stage moves (A's 16 KB + B's width x 128 bytes, relative to a 256 tile):
+// a thin product's tiles are few and each walks all of K, so narrower tiles (with deeper
+// rings: 6 or 8 stages) put more SMs on it.
+static int pick_bn_thin(int64_t M, int64_t N, int sms) {
+  const int cand[3] = {256, 128, 64};
+  const int64_t mt = (M + BM - 1) / BM;
+  int best = 256;
+  double best_t = 1e300;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t tiles = mt * ((N + cand[i] - 1) / cand[i]);
+    const int64_t rounds = (tiles + sms - 1) / sms;
+    const double t = (double)rounds * (128.0 + cand[i]) / 384.0;
+    if (t < best_t - 1e-9) { best_t = t; best = cand[i]; }
+  }
+  return best;
+}
+
 // How many CTA pairs of gemm_pair_kernel are resident at once on the current device
 // (the persistent grid's size), cached per device.  Needs the smem attribute set.
 template <typename Kern>
@@ -894,13 +920,16 @@ static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void
   const bool use_pair = M > BM && kind != kKCodes;
   CUtensorMap ma, mb;
   const uint64_t da[2] = {(uint64_t)K, (uint64_t)M}, db[2] = {(uint64_t)K, (uint64_t)N};
-  int clusters = 0, bn = BN;
+  int clusters = 0, bn = BN, sms = 148;
+  QF2_CUDA_CHECK(qf2_sm_count(&sms));
   if (use_pair) {
     QF2_CUDA_CHECK(pair_setup(kind, &clusters));
     if (!glu) bn = pick_bn(M, N, clusters);
+  } else if (kind != kKCodes && !glu) {
+    bn = pick_bn_thin(M, N, sms);
   }
   const uint32_t ba[2] = {bk, (uint32_t)BM},
-                 bb[2] = {bk, (uint32_t)(use_pair ? bn / 2 : BN)};
+                 bb[2] = {bk, (uint32_t)(use_pair ? bn / 2 : bn)};
   // weight codes: bk bytes of K per row, unswizzled (the converters rewrite them)
   const bool bmap_ok = b_codes ? qf2_make_tmap_2d_noswizzle(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, db, (uint64_t)ldb, bb)
                                : qf2_make_tmap_2d(&mb, tdt, b, db, (uint64_t)ldb * esz, bb);
@@ -953,9 +982,7 @@ static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void
       gemm_pair_kernel<kK16><<<grid, Lay<kK16, true>::threads, Lay<kK16, true>::alloc, s>>>(ma, mb, md, args);
   } else {
     static std::atomic<uint64_t> attr_done[3];
-    int sms = 148;
-    QF2_CUDA_CHECK(qf2_sm_count(&sms));
-    const int64_t ntiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int64_t ntiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
     const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms);
     if (kind == kKE4M3) {
       QF2_CUDA_CHECK(qf2_set_smem_once(gemm_kernel<kKE4M3>, Lay<kKE4M3, false>::alloc, &attr_done[kind]));

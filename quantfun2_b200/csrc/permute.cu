@@ -13,6 +13,8 @@
 // GPU; the chunk's digits are decoded once per CTA.
 #include "qf2_common.cuh"
 
+#include <algorithm>
+
 namespace qf2 {
 namespace perm {
 
@@ -58,12 +60,13 @@ __global__ void __launch_bounds__(kThreads) copy_chunks_kernel(ChunkArgs A) {
   }
 }
 
-// Small chunks (at most kSmallMax bytes: a few heads of one token): a warp walks
-// kChunksPerWarp consecutive chunks, kUnroll at a time -- their addresses are decoded once
-// per chunk (32-bit digit division), the lanes stride over the 16-byte vectors, and the
-// loads of the kUnroll chunks are issued before their stores.
+// Small chunks (at most kSmallMax bytes: a few heads of one token): a warp walks `per`
+// consecutive chunks (4 to 16: enough warps for a few waves over the SMs, so copies of a
+// few MB are not left to a fraction of the GPU), kUnroll at a time -- their addresses are
+// decoded once per chunk (32-bit digit division), the lanes stride over the 16-byte
+// vectors, and the loads of the kUnroll chunks are issued before their stores.
 constexpr int64_t kSmallMax = 4096;
-constexpr int kChunksPerWarp = 16;
+constexpr int kChunksPerWarpMax = 16;
 constexpr int kUnroll = 4;
 
 struct SmallArgs {
@@ -71,6 +74,7 @@ struct SmallArgs {
   uint8_t* dst;
   uint32_t nv;     // 16-byte vectors per chunk
   uint32_t n;      // chunks
+  uint32_t per;    // chunks per warp (a multiple of kUnroll)
   uint32_t d[4];
   int64_t ss[4], ds[4];
 };
@@ -90,14 +94,14 @@ QF2_DEV void chunk_offsets(const SmallArgs& A, uint32_t c, int64_t& so, int64_t&
 
 __global__ void __launch_bounds__(kThreads) copy_small_chunks_kernel(SmallArgs A) {
   const int lane = threadIdx.x & 31;
-  const uint32_t c0 = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kChunksPerWarp;
-  for (uint32_t cb = c0; cb < c0 + kChunksPerWarp && cb < A.n; cb += kUnroll) {
+  const uint32_t c0 = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * A.per;
+  for (uint32_t cb = c0; cb < c0 + A.per && cb < A.n; cb += kUnroll) {
     const uint4* s[kUnroll];
     uint4* d[kUnroll];
     bool live[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      live[u] = cb + u < A.n && cb + u < c0 + kChunksPerWarp;
+      live[u] = cb + u < A.n && cb + u < c0 + A.per;
       int64_t so = 0, dof = 0;
       if (live[u]) chunk_offsets(A, cb + u, so, dof);
       s[u] = reinterpret_cast<const uint4*>(A.src + so);
@@ -150,7 +154,15 @@ extern "C" int qf2_copy_chunks(void* dst, const void* src, int64_t chunk_bytes, 
       S.ss[k] = A.ss[k];
       S.ds[k] = A.ds[k];
     }
-    const int64_t per_cta = (int64_t)(kThreads / 32) * kChunksPerWarp;
+    // chunks per warp: 16, or fewer (down to kUnroll) until there are ~4 warps' worth of
+    // work per resident warp slot (148 SMs x 64 warps)
+    int sms = 148;
+    QF2_CUDA_CHECK(qf2_sm_count(&sms));
+    const int64_t want_warps = (int64_t)sms * 64 * 4;
+    int64_t per = (n + want_warps - 1) / want_warps;
+    per = std::min<int64_t>(kChunksPerWarpMax, std::max<int64_t>(kUnroll, (per + kUnroll - 1) / kUnroll * kUnroll));
+    S.per = (uint32_t)per;
+    const int64_t per_cta = (int64_t)(kThreads / 32) * per;
     copy_small_chunks_kernel<<<(unsigned)((n + per_cta - 1) / per_cta), kThreads, 0,
                                reinterpret_cast<cudaStream_t>(stream)>>>(S);
     QF2_LAUNCH_CHECK();

@@ -171,6 +171,39 @@ def test_gemm_codes_fused_epilogues(cuda, fmt):
     assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
 
 
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("mn", [(64, 3072), (1, 18432), (128, 1000), (100, 64512), (64, 9216)])
+def test_gemm_thin_tile_widths(cuda, mn, fp8):
+    """Single-CTA products (M <= 128) over widths that select 64-, 128- and 256-column tiles
+    (6 / 8-stage rings), ragged N, with bias, GELU on part of the columns and a gated
+    residual, against fp64."""
+    from quantfun2_b200.quant import gemm, quantize_rows
+
+    M, N = mn
+    K = 3072 if fp8 else 1024
+    g = torch.Generator(device=cuda).manual_seed(N + M)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=cuda, generator=g) / K ** 0.5).bfloat16()
+    bias = torch.randn(N, device=cuda, generator=g).bfloat16()
+    res = torch.randn(M, N, device=cuda, generator=g).bfloat16()
+    gate = torch.randn(1, N, device=cuda, generator=g).bfloat16()
+    out = res.clone()
+    if fp8:
+        xq, xs = quantize_rows(x, "e4m3")
+        wq, ws = quantize_rows(w, "e4m3")
+        gemm(xq, wq, row_scale=xs, col_scale=ws, bias=bias, fp8=True, gelu_col0=N // 3, residual=out, gate=gate,
+             rows_per_gate=M, out=out)
+        xf = torch.from_numpy(e4m3_bits_to_f32(xq.cpu().numpy())).double().to(cuda) * xs.double()[:, None]
+        wf = torch.from_numpy(e4m3_bits_to_f32(wq.cpu().numpy())).double().to(cuda) * ws.double()[:, None]
+    else:
+        gemm(x, w, bias=bias, gelu_col0=N // 3, residual=out, gate=gate, rows_per_gate=M, out=out)
+        xf, wf = x.double(), w.double()
+    y = xf @ wf.T + bias.double()
+    y = torch.where(torch.arange(N, device=cuda) >= N // 3, torch.nn.functional.gelu(y, approximate="tanh"), y)
+    ref = res.double() + gate.double() * y
+    assert rel_err(out.float().cpu(), ref.cpu()) < 8e-3
+
+
 @pytest.mark.parametrize("mnk", [(128, 256, 128), (300, 776, 272), (4608, 3072, 3072)])
 def test_gemm_e4m3(cuda, mnk):
     from quantfun2_b200.quant import gemm, quantize_rows
