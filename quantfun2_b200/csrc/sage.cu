@@ -1395,6 +1395,40 @@ static bool make_prep_map(CUtensorMap* m, const void* base, const Strides3& st, 
                                     base, dims, strides, box);
 }
 
+
+// Whether clusters of 16 prep CTAs (non-portable size) can run on the current device,
+// cached per device; enables the size on first use.
+template <typename T>
+static bool prep_cluster16_ok() {
+  static std::atomic<int> cache[64];  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  int v = cache[dev & 63].load(std::memory_order_relaxed);
+  if (v == 0) {
+    v = 2;
+    if (cudaFuncSetAttribute(sage_prep_kernel<T>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+        cudaFuncSetAttribute(sage_prep_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrepSmem::total) ==
+            cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(16);
+      cfg.blockDim = dim3(kPrepThreads);
+      cfg.dynamicSmemBytes = PrepSmem::total;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 16;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, sage_prep_kernel<T>, &cfg) == cudaSuccess && n >= 4) v = 1;
+    }
+    cudaGetLastError();  // a refused size leaves no sticky error behind
+    cache[dev & 63].store(v, std::memory_order_relaxed);
+  }
+  return v == 1;
+}
+
 template <typename T>
 static int launch_quant(const Args& a) {
   const bool varlen = a.cu_q != nullptr;
@@ -1430,7 +1464,11 @@ static int launch_quant(const Args& a) {
   // CTAs join when they are done.
   const int64_t slots = (int64_t)sms * kPrepCtasPerSm;
   const int64_t heads = a.batch * a.Hkv;
-  const int C = (int)std::min<int64_t>(kMaxCluster, std::max<int64_t>(1, mtk));
+  int C = (int)std::min<int64_t>(kMaxCluster, std::max<int64_t>(1, mtk));
+  // few kv heads (a head-parallel shard: 3 heads of 4608 tokens on 8 GPUs): clusters of 16
+  // (a non-portable size, used where the device can place them) halve each K/V CTA's share
+  // of its head, which is the critical path when the K/V role cannot fill its CTA budget
+  if (mtk >= 16 && heads * kMaxCluster * 3 < slots * 2 && prep_cluster16_ok<T>()) C = 16;
   const int64_t n_cl = std::min(heads, std::max<int64_t>(1, std::llround((double)slots * 2.0 / 3.0 / C)));
   const int64_t n_kv = n_cl * C;
   const int64_t nq_tiles = a.batch * a.Hq * A.mtq;
