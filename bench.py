@@ -627,6 +627,11 @@ def profile_cases(dev) -> dict:
         a, b = rn(1, 3072).to(bf), rn(18432, 3072).to(bf)
         return lambda: Q.gemm(a, b)
 
+    def gemm_codes():    # weight-only int8 codes read directly by the GEMM (M <= 128)
+        a = rn(1, 3072).to(bf)
+        c, sc = Q.quantize_weight(rn(18432, 3072).to(bf), "int8")
+        return lambda: Q.gemm(a, c, col_scale=sc, codes="int8")
+
     def blocksparse():
         q, k, v = (rn(1, 24, 16384, 128).to(bf) for _ in range(3))
         idx = block_topk_select(q, k, 16)
@@ -662,7 +667,7 @@ def profile_cases(dev) -> dict:
             "gate_residual": gate_residual, "ln_modulate": ln_modulate, "quantize_rows": quantize_rows,
             "codes_to_bf16": codes_to_bf16, "quantize_weight": quantize_weight, "copy_chunks": copy_chunks,
             "sage": sage, "sage_split": sage_split, "gemm_fp8": gemm_fp8, "gemm_bf16_glu": gemm_bf16_glu,
-            "gemm_single": gemm_single, "blocksparse": blocksparse, "ras": ras}
+            "gemm_single": gemm_single, "gemm_codes": gemm_codes, "blocksparse": blocksparse, "ras": ras}
 
 
 def run_profile_kernel(name: str, dev) -> None:

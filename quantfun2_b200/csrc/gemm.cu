@@ -49,9 +49,9 @@ struct Lay {
   static_assert(!(PAIR && KIND == kKCodes), "weight codes run on the single-CTA gemm_kernel");
   static constexpr bool codes = KIND == kKCodes;
   static constexpr int stages = PAIR ? 6 : (codes ? 3 : 4);
-  // the single-CTA 16-bit / e4m3 kernel also runs 128- and 64-column tiles (thin
-  // products), whose smaller stages fit up to 6 and 8 times into the same region
-  static constexpr int max_stages = (PAIR || codes) ? stages : 8;
+  // the single-CTA kernel also runs 128- and 64-column tiles (thin products), whose
+  // smaller stages (and code slots) fit more times into the same region
+  static constexpr int max_stages = PAIR ? stages : 8;
   static constexpr int a_bytes = BM * 128;
   static constexpr int b_rows = PAIR ? 128 : BN;
   static constexpr int b_bytes = b_rows * 128;
@@ -439,7 +439,7 @@ QF2_DEV void epilogue_tile(const Args& A, Stager& st, uint32_t tacc, int64_t m0w
 // ------------------------------------------------------- single-CTA tiles --
 // 128 x 256 tiles, one CTA per SM (small M: the adaLN / embedding linears).  Also the
 // weight-code kernel (KIND kKCodes), for every M: B arrives as 8-bit codes and warps 10-13
-// rewrite each stage's 256 x 64 codes as 16-bit values in shared memory.  That conversion
+// rewrite each stage's bn x 64 codes as 16-bit values in shared memory.  That conversion
 // is repeated for every 128-row tile of A and its shared-memory traffic (1 byte read and 2
 // written per code) comes on top of the operand traffic of the tile, so it pays where one
 // tile of A covers M (the weight is read at 1 byte instead of 2 and no expansion kernel
@@ -467,10 +467,13 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::misc + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // tile width (256, or 128 / 64 for thin products) and the stages that fit at that width
-  const int bn = CODES ? BN : A.bn;
+  // tile width (256, or 128 / 64 for thin products) and the stages (A + B tiles, and for
+  // weight codes a code slot each) that fit into the region at that width
+  const int bn = A.bn;
   const int sbytes = L::a_bytes + bn * 128;
-  const int ns = CODES ? L::stages : min(L::max_stages, L::raw / sbytes);
+  const int rbytes = CODES ? bn * 64 : 0;
+  const int ns = min(L::max_stages, L::staging / (sbytes + rbytes));
+  uint8_t* const raw_base = base + ns * sbytes;  // code slots after the stages
   const int64_t mt = (A.M + BM - 1) / BM, nt = (A.N + bn - 1) / bn;
   const int64_t ntiles = mt * nt;
   constexpr int bk = FP8 ? 128 : 64;  // K elements per stage (128 bytes)
@@ -522,9 +525,9 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
         if (!wwait(empty + s, (uint32_t)(((g / ns) & 1) ^ 1))) { ok = false; break; }
         if (lane == 0) {
           uint8_t* st = base + s * sbytes;
-          mbar_arrive_expect_tx(landed + s, CODES ? L::a_bytes + L::raw_bytes : sbytes);
+          mbar_arrive_expect_tx(landed + s, CODES ? L::a_bytes + rbytes : sbytes);
           tma_load_2d(st, &tma, (int)(kb * bk), m0, landed + s);
-          tma_load_2d(CODES ? base + L::raw + s * L::raw_bytes : st + L::a_bytes, &tmb, (int)(kb * bk), n0,
+          tma_load_2d(CODES ? raw_base + s * rbytes : st + L::a_bytes, &tmb, (int)(kb * bk), n0,
                       landed + s);
         }
         __syncwarp();
@@ -601,16 +604,16 @@ __global__ void __launch_bounds__(Lay<KIND, false>::threads, 1)
   } else if constexpr (CODES) {
     // ----------------------------------------------------- converters --
     constexpr int kChunks = L::raw_bytes / 16 / kConvThreads;
-    const ConvPlan<kChunks> plan(threadIdx.x - 32 * (2 + kEpilogueWarps), L::raw_bytes / 16);
+    const ConvPlan<kChunks> plan(threadIdx.x - 32 * (2 + kEpilogueWarps), bn * 4);
     bool ok = true;
     with_code_format(A.b_fmt, A.f16 != 0, [&](auto fmt_c, auto f16_c) {
       int64_t g = 0;
       for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
         for (int64_t kb = 0; kb < nk; ++kb, ++g) {
-          const int s = (int)(g % L::stages);
-          if (!wwait(raw_full + s, (uint32_t)((g / L::stages) & 1))) { ok = false; break; }
+          const int s = (int)(g % ns);
+          if (!wwait(raw_full + s, (uint32_t)((g / ns) & 1))) { ok = false; break; }
           convert_codes_tile<kChunks, decltype(fmt_c)::value, decltype(f16_c)::value>(
-              base + L::raw + s * L::raw_bytes, base + s * L::stage_bytes + L::a_bytes, plan);
+              raw_base + s * rbytes, base + s * sbytes + L::a_bytes, plan);
           fence_async_smem();  // the generic-proxy writes, before the MMA reads them
           __syncwarp();
           if (lane == 0) mbar_arrive(full + s);
@@ -925,7 +928,7 @@ static int gemm_run(const void* a, int64_t lda, const void* b, int64_t ldb, void
   if (use_pair) {
     QF2_CUDA_CHECK(pair_setup(kind, &clusters));
     if (!glu) bn = pick_bn(M, N, clusters);
-  } else if (kind != kKCodes && !glu) {
+  } else if (!glu) {
     bn = pick_bn_thin(M, N, sms);
   }
   const uint32_t ba[2] = {bk, (uint32_t)BM},
