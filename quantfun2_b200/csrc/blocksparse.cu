@@ -10,9 +10,9 @@
 //   3. blocksparse_attn_kernel  exact softmax attention of each 128-row query block over
 //                               its kept key blocks: TMA tiles (bf16/fp16, 128-byte
 //                               swizzle) fetched by block index, tcgen05.mma kind::f16
-//                               QK^T into TMEM (double-buffered S), P through two shared
-//                               memory buffers, PV with V read as an MN-major operand,
-//                               fp32 O in TMEM; 8 softmax warps, lazy rescale.
+//                               QK^T into TMEM (double-buffered S), P written to TMEM
+//                               (two buffers) as PV's A operand, V read as an MN-major
+//                               operand, fp32 O in TMEM; 8 softmax warps, lazy rescale.
 #include "qf2_common.cuh"
 
 #include <algorithm>
@@ -158,30 +158,37 @@ __global__ void __launch_bounds__(256) blocktopk_select_kernel(const float* __re
 
 // ------------------------------------------------------------- attention --
 // One CTA per 128-row query block: warp 0 TMA producer (Q once, K/V of each kept block
-// into a 2-stage ring), warp 1 MMA issuer (QK^T into a double-buffered S in TMEM, PV into
+// into a 3-stage ring), warp 1 MMA issuer (QK^T into a double-buffered S in TMEM, PV into
 // O in TMEM), warps 2-9 softmax.  A row's 128 scores are split over two softmax threads
 // of the same TMEM lane quarter (warps w and w + 4), 64 columns each, so two warps per
 // SM sub-partition feed the SFU; the halves exchange row maxima through shared memory.
 // Lazy rescale: the running max moves (and O is rescaled) only when a block's max
 // exceeds it by more than kTau (log2 units); P (bf16/fp16, at most 2^kTau) goes through
-// two shared-memory buffers so the next block's exps do not wait for the last PV.
+// two TMEM buffers so the next block's exps do not wait for the last PV.
 constexpr int kThreads = 320;   // warp 0 producer, warp 1 MMA, warps 2-9 softmax
 constexpr int kTile = 16384;    // 128 rows x 128 bytes (one 128-byte swizzle atom column)
 constexpr int kOpBytes = 2 * kTile;  // 128 x 128 16-bit elements
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
+// P lives in tensor memory as the PV product's A operand, which leaves shared memory for a
+// 3-stage K/V ring (measured against P in two shared-memory buffers and 2 K/V stages:
+// 0.774 -> 0.729 ms, S=16384, keep 16/128)
+constexpr int kKvStages = 3;
+// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512) (a 128 x 128 16-bit
+// tile is 64 columns: two elements per column)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemP = 384;
 constexpr float kTau = 8.0f;
 
 struct Smem {
   static constexpr int q = 0;
-  static constexpr int kv = q + kOpBytes;          // 2 stages x (K, V)
-  static constexpr int p = kv + 2 * 2 * kOpBytes;  // 2 P buffers
-  static constexpr int xch = p + 2 * kOpBytes;     // row-max [j & 1][half][row] (row sums reuse it)
+  static constexpr int kv = q + kOpBytes;                   // kKvStages x (K, V)
+  static constexpr int xch = kv + kKvStages * 2 * kOpBytes;  // row-max [j & 1][half][row] (row sums reuse it)
   static constexpr int bars = xch + 2 * 2 * 128 * 4;
-  static constexpr int nbars = 1 + 2 + 2 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+  static constexpr int nbars = 1 + 2 * kKvStages + 2 + 2 + 2 + 2 + 1 + 1 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int total = misc + 64;
   static constexpr int alloc = total;  // no alignment slack: the base is declared 1024-aligned
 };
+static_assert(Smem::alloc <= 227 * 1024, "shared memory");
 
 struct AttnArgs {
   const int32_t* idx;
@@ -219,28 +226,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* base = smem_raw;
   uint8_t* sQ = base + Smem::q;
   uint8_t* sKV = base + Smem::kv;
-  uint8_t* sP = base + Smem::p;
   float* xmax = reinterpret_cast<float*>(base + Smem::xch);  // [j & 1][half][row]
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + Smem::bars);
   uint64_t* bar_q = bars;
-  uint64_t* bar_kv_full = bars + 1;   // [2]
-  uint64_t* bar_kv_empty = bars + 3;  // [2]
-  uint64_t* bar_s_full = bars + 5;    // [2]
-  uint64_t* bar_s_empty = bars + 7;   // [2]
-  uint64_t* bar_p_full = bars + 9;    // [P buffer]: P(i) written, i & 1 = buffer
-  uint64_t* bar_o_done = bars + 11;   // [P buffer]: PV(i) completed
-  uint64_t* bar_xm = bars + 13;
-  uint64_t* bar_xl = bars + 14;
-  uint64_t* bar_drain = bars + 15;
+  uint64_t* bar_kv_full = bars + 1;                   // [kKvStages]
+  uint64_t* bar_kv_empty = bar_kv_full + kKvStages;   // [kKvStages]
+  uint64_t* bar_s_full = bar_kv_empty + kKvStages;    // [2]
+  uint64_t* bar_s_empty = bar_s_full + 2;             // [2]
+  uint64_t* bar_p_full = bar_s_empty + 2;             // [P buffer]: P(i) written, i & 1 = buffer
+  uint64_t* bar_o_done = bar_p_full + 2;              // [P buffer]: PV(i) completed
+  uint64_t* bar_xm = bar_o_done + 2;
+  uint64_t* bar_xl = bar_xm + 1;
+  uint64_t* bar_drain = bar_xl + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + Smem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + Smem::misc + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kKvStages; ++s) {
       mbar_init(bar_kv_full + s, 1);
       mbar_init(bar_kv_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar_s_full + s, 1);
       mbar_init(bar_s_empty + s, 8);
       mbar_init(bar_o_done + s, 1);
@@ -284,8 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int issued = 0;
       for (int j = 0; j < keep; ++j) {
-        const int s = j & 1;
-        if (!wwait(bar_kv_empty + s, ((j >> 1) & 1) ^ 1)) { if (lane == 0) fail(kDevTimeoutProducer); break; }
+        const int s = j % kKvStages;
+        if (!wwait(bar_kv_empty + s, ((j / kKvStages) & 1) ^ 1)) { if (lane == 0) fail(kDevTimeoutProducer); break; }
         if (lane == 0) {
           const int kb = idx[j];
           uint8_t* dK = sKV + s * 2 * kOpBytes;
@@ -301,7 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*abort_flag && lane == 0) {
         mbar_wait(bar_q, 0);
-        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) mbar_wait(bar_kv_full + (j & 1), (j >> 1) & 1);
+        for (int j = issued > kKvStages ? issued - kKvStages : 0; j < issued; ++j)
+          mbar_wait(bar_kv_full + (j % kKvStages), (j / kKvStages) & 1);
       }
     }
   } else if (warp == 1) {
@@ -315,29 +324,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](int i) -> bool {
         if (!wwait(bar_p_full + (i & 1), (uint32_t)((i >> 1) & 1))) return false;
         tc_fence_after();
-        const uint32_t aV = smem_u32(sKV + (i & 1) * 2 * kOpBytes + kOpBytes);
-        const uint32_t aP = smem_u32(sP + (i & 1) * kOpBytes);
+        const uint32_t aV = smem_u32(sKV + (i % kKvStages) * 2 * kOpBytes + kOpBytes);
         if (lane == 0) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            // A: P rows, 16 keys per step (two 64-key swizzle atoms); B: V rows kk*16.. as
-            // MN-major (head-dim halves 16 KB apart, 8-row groups 1 KB apart)
-            const uint64_t da = sdesc_sw128_kmajor(aP + (kk >> 2) * kTile + (kk & 3) * 32);
+            // A: P rows, 16 keys per step = 8 TMEM columns; B: V rows kk*16.. as MN-major
+            // (head-dim halves 16 KB apart, 8-row groups 1 KB apart)
             const uint64_t db = sdesc_sw128_mnmajor(aV + kk * 16 * 128, kTile, 1024);
-            mma_f16(tmem + 256, da, db, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+            mma_f16_tmem_a(tmem + 256, tmem + kTmemP + (i & 1) * 64 + kk * 8, db, idesc_pv,
+                           (i > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(bar_o_done + (i & 1));
-          tc_commit(bar_kv_empty + (i & 1));
+          tc_commit(bar_kv_empty + (i % kKvStages));
         }
         __syncwarp();
         return true;
       };
       for (int j = 0; ok && j < keep; ++j) {
-        const int s = j & 1;
-        if (!wwait(bar_kv_full + s, (j >> 1) & 1)) { ok = false; break; }
+        const int s = j & 1, ks = j % kKvStages;
+        if (!wwait(bar_kv_full + ks, (j / kKvStages) & 1)) { ok = false; break; }
         if (!wwait(bar_s_empty + s, ((j >> 1) & 1) ^ 1)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t aK = smem_u32(sKV + s * 2 * kOpBytes);
+        const uint32_t aK = smem_u32(sKV + ks * 2 * kOpBytes);
         if (lane == 0) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -409,19 +417,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_use = m_run == -INFINITY ? 0.f : m_run;  // a fully masked row contributes nothing
       // P(j) goes to buffer j & 1, last read by PV(j - 2)
       if (j >= 2 && !o_wait(j - 2)) { ok = false; break; }
-      uint8_t* pbuf = sP + (j & 1) * kOpBytes + half * kTile;  // this half's 64-key swizzle atom column
+      // this half's 64 keys of the row: 32 TMEM columns of packed pairs in P buffer j & 1
       float rs = 0.f;
+      uint32_t w[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float p0 = fast_exp2(x[8 * c + 2 * q] - m_use), p1 = fast_exp2(x[8 * c + 2 * q + 1] - m_use);
-          rs += p0 + p1;
-          w[q] = pack2(p0, p1, f16);
-        }
-        *reinterpret_cast<uint4*>(pbuf + row * 128 + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int q = 0; q < 32; ++q) {
+        const float p0 = fast_exp2(x[2 * q] - m_use), p1 = fast_exp2(x[2 * q + 1] - m_use);
+        rs += p0 + p1;
+        w[q] = pack2(p0, p1, f16);
       }
+      tmem_st32(tmem + lane_off + kTmemP + (j & 1) * 64 + half * 32, w);
       l_run += rs;
       if (rescale && j > 0) {
         // O holds sum_{i<j} P_i V_i against the old max; PV(j) is issued after p_full(j)
@@ -438,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
       }
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p_full + (j & 1));

@@ -381,6 +381,17 @@ QF2_DEV void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t i
       : "memory");
 }
 
+// The same with the A operand in tensor memory (M rows = TMEM lanes, K along the columns,
+// two 16-bit elements per 32-bit column, the lower half holding the even K index).
+QF2_DEV void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // TMEM -> registers: 32 lanes x 32 bits, 32 consecutive columns per thread.
 QF2_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
