@@ -183,7 +183,7 @@ struct Smem {
   static constexpr int kv = q + kOpBytes;                   // kKvStages x (K, V)
   static constexpr int xch = kv + kKvStages * 2 * kOpBytes;  // row-max [j & 1][half][row] (row sums reuse it)
   static constexpr int bars = xch + 2 * 2 * 128 * 4;
-  static constexpr int nbars = 1 + 2 * kKvStages + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+  static constexpr int nbars = 1 + 2 * kKvStages + 2 + 2 + 2 + 2 + 4 + 4 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int total = misc + 64;
   static constexpr int alloc = total;  // no alignment slack: the base is declared 1024-aligned
@@ -235,9 +235,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_s_empty = bar_s_full + 2;             // [2]
   uint64_t* bar_p_full = bar_s_empty + 2;             // [P buffer]: P(i) written, i & 1 = buffer
   uint64_t* bar_o_done = bar_p_full + 2;              // [P buffer]: PV(i) completed
-  uint64_t* bar_xm = bar_o_done + 2;
-  uint64_t* bar_xl = bar_xm + 1;
-  uint64_t* bar_drain = bar_xl + 1;
+  // row-max / row-sum exchange between the two warps of a lane quarter (w and w + 4):
+  // one barrier per quarter, so the quarters do not wait on one another
+  uint64_t* bar_xm = bar_o_done + 2;  // [4]
+  uint64_t* bar_xl = bar_xm + 4;      // [4]
+  uint64_t* bar_drain = bar_xl + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + Smem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + Smem::misc + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -254,8 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_o_done + s, 1);
       mbar_init(bar_p_full + s, 8);
     }
-    mbar_init(bar_xm, 8);
-    mbar_init(bar_xl, 8);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(bar_xm + q, 2);
+      mbar_init(bar_xl + q, 2);
+    }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -402,8 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* xm = xmax + (j & 1) * 256;
       xm[half * 128 + row] = mx;
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_xm);
-      if (!wwait(bar_xm, j & 1)) { ok = false; break; }
+      if (lane == 0) mbar_arrive(bar_xm + quarter);
+      if (!wwait(bar_xm + quarter, j & 1)) { ok = false; break; }
       const float m_tile = fmaxf(mx, xm[(half ^ 1) * 128 + row]);
       const float m_new = fmaxf(m_run, m_tile);
       // both warps of a row pair see the same 32 rows, so they agree on the decision
@@ -457,8 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* xs = xmax + (keep & 1) * 256;
       xs[half * 128 + row] = l_run;
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_xl);
-      if (!wwait(bar_xl, 0) || !o_wait(keep - 1)) {
+      if (lane == 0) mbar_arrive(bar_xl + quarter);
+      if (!wwait(bar_xl + quarter, 0) || !o_wait(keep - 1)) {
         fail(kDevTimeoutEpilogue);
         ok = false;
       } else {
