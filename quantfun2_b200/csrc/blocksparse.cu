@@ -394,15 +394,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar_s_empty + s);
 
       const int64_t valid = A.S - (int64_t)idx[j] * kBlk - half * 64;  // keys of this half inside the sequence
+      // raw scores; the scale (> 0) is applied to the max and folded into the exponent's fma
       float x[64];
-      float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        float v = __uint_as_float(sr[i]) * A.scale_log2;
-        if (i >= valid) v = -INFINITY;
-        x[i] = v;
-        mx = fmaxf(mx, v);
+      for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(sr[i]);
+      if (valid < 64) {  // warp-uniform: the block runs past the sequence end
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i >= valid) x[i] = -INFINITY;
       }
+      float mq[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float m = fmax3(x[c * 16], x[c * 16 + 1], x[c * 16 + 2]);
+#pragma unroll
+        for (int i = 3; i < 15; i += 2) m = fmax3(m, x[c * 16 + i], x[c * 16 + i + 1]);
+        mq[c] = fmaxf(m, x[c * 16 + 15]);
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * A.scale_log2;
       float* xm = xmax + (j & 1) * 256;
       xm[half * 128 + row] = mx;
       __syncwarp();
@@ -422,16 +431,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P(j) goes to buffer j & 1, last read by PV(j - 2)
       if (j >= 2 && !o_wait(j - 2)) { ok = false; break; }
       // this half's 64 keys of the row: 32 TMEM columns of packed pairs in P buffer j & 1
-      float rs = 0.f;
+      // P = 2^(s * scale - m) as one fma per pair of keys (f32x2)
+      const float2 scv = make_float2(A.scale_log2, A.scale_log2), nm = make_float2(-m_use, -m_use);
+      float2 rs = make_float2(0.f, 0.f);
       uint32_t w[32];
 #pragma unroll
       for (int q = 0; q < 32; ++q) {
-        const float p0 = fast_exp2(x[2 * q] - m_use), p1 = fast_exp2(x[2 * q + 1] - m_use);
-        rs += p0 + p1;
-        w[q] = pack2(p0, p1, f16);
+        const float2 e = ffma2(make_float2(x[2 * q], x[2 * q + 1]), scv, nm);
+        const float2 pp = make_float2(fast_exp2(e.x), fast_exp2(e.y));
+        rs = fadd2(rs, pp);
+        w[q] = pack2(pp.x, pp.y, f16);
       }
       tmem_st32(tmem + lane_off + kTmemP + (j & 1) * 64 + half * 32, w);
-      l_run += rs;
+      l_run += rs.x + rs.y;
       if (rescale && j > 0) {
         // O holds sum_{i<j} P_i V_i against the old max; PV(j) is issued after p_full(j)
         if (!o_wait(j - 1)) { ok = false; break; }
