@@ -210,6 +210,9 @@ QF2_DEV uint32_t pack2(float a, float b, bool f16) {
   return *reinterpret_cast<uint32_t*>(&t);
 }
 
+// F16: fp16 operands and output (else bf16), a compile-time choice so the P packing of
+// the exponent loop carries no per-element select
+template <bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     blocksparse_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                             const __grid_constant__ CUtensorMap tmv, AttnArgs A) {
@@ -320,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA --
     if (keep > 0) {
-      const uint32_t ab = A.f16 ? 0u : 1u;
+      const uint32_t ab = F16 ? 0u : 1u;
       const uint32_t idesc_qk = make_idesc(1, ab, ab, 0, 0, kBlk, kBlk);   // K-major x K-major -> f32
       const uint32_t idesc_pv = make_idesc(1, ab, ab, 0, 1, kBlk, kD);     // P K-major x V MN-major -> f32
       const uint32_t aQ = smem_u32(sQ);
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tO = tmem + lane_off + 256 + half * 64;
-    const bool f16 = A.f16 != 0;
+    constexpr bool f16 = F16;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = keep > 0;
     for (int j = 0; ok && j < keep; ++j) {
@@ -614,9 +617,10 @@ extern "C" int qf2_blocksparse_attn(const void* q, const int64_t* q_strides, con
   a.status = reinterpret_cast<int*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   QF2_CUDA_CHECK(cudaMemsetAsync(workspace, 0, sizeof(int), s));
-  static std::atomic<uint64_t> attr_done{0};
-  QF2_CUDA_CHECK(qf2_set_smem_once(blocksparse_attn_kernel, Smem::alloc, &attr_done));
-  blocksparse_attn_kernel<<<dim3((unsigned)nb, (unsigned)Hq, (unsigned)B), kThreads, Smem::alloc, s>>>(mq, mk, mv, a);
+  static std::atomic<uint64_t> attr_done[2];
+  auto kern = a.f16 ? blocksparse_attn_kernel<true> : blocksparse_attn_kernel<false>;
+  QF2_CUDA_CHECK(qf2_set_smem_once(kern, Smem::alloc, &attr_done[a.f16 ? 1 : 0]));
+  kern<<<dim3((unsigned)nb, (unsigned)Hq, (unsigned)B), kThreads, Smem::alloc, s>>>(mq, mk, mv, a);
   QF2_LAUNCH_CHECK();
   return QF2_OK;
 }
