@@ -43,7 +43,8 @@ def test_select_indices_bit_exact(cuda, shape):
             assert np.array_equal(idx[b, h], ref), (b, h)
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 2, 1000, 3), (2, 4, 2, 777, 7), (1, 2, 1, 384, 3)])
+@pytest.mark.parametrize("shape", [(1, 2, 2, 1000, 3), (2, 4, 2, 777, 7), (1, 2, 1, 384, 3), (1, 2, 2, 1000, 1),
+                                   (2, 2, 1, 300, 2)])
 @pytest.mark.parametrize("layout", ["HND", "NHD"])
 def test_blocksparse_attention_vs_oracle(cuda, shape, layout):
     from quantfun2_b200.attention import block_topk_select, blocksparse_attn
